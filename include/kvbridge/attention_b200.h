@@ -1,0 +1,96 @@
+#pragma once
+// kvbridge-b200 extensions beyond the reference interface. Everything here is
+// additive: the reference entry points in attention_common.h keep their
+// contract, and these functions reuse the same memory formats.
+//
+//   * launch_attention_ex     - the single-sequence call with an explicit
+//                               split-K partition count and a fused fp16
+//                               normalised-output epilogue.
+//   * launch_attention_batched- ragged batch of decode sequences over one
+//                               shared page pool (block table per sequence).
+//   * merge_attention_shards  - log-sum-exp merge of per-GPU (m, l, n)
+//                               triples for sequence-sharded decode.
+#include <cuda_runtime.h>
+#include <cstddef>
+#include <cstdint>
+#include "kvbridge/attention_common.h"
+
+namespace kvbridge {
+
+struct LaunchOptions {
+  // Split-K partitions per KV head. 0 lets the launcher choose from the SM
+  // count; otherwise clamped to [1, split_count(shape)] and to the number of
+  // 64-token stages in [begin,end).
+  unsigned partitions;
+  // Optional __half[rows * q_heads * dim]: out = n / l where l > 0, else 0.
+  void* out_f16;
+};
+
+// True when launch_attention(_ex) will use the TMA/tensor-core kernel for this
+// shape and these buffers (int8 KV, dim in {64,128,256}, page_tokens dividing
+// 64, rows*group <= 16, 16-byte aligned K/V/scale buffers). Host-only.
+bool attention_b200_supported(const Shape&, const DeviceInput&) noexcept;
+
+// Partition count launch_attention_ex will use (host-only; needs the SM count
+// of the current device, which it queries once per device).
+unsigned attention_partitions(const Shape&, unsigned requested);
+
+void launch_attention_ex(const Shape&, const DeviceInput&, const LaunchOptions&,
+                         float* scratch, float* m, float* l, float* n, cudaStream_t);
+
+// The two halves of launch_attention_ex on the tensor-core path, for callers
+// that merge partials themselves (e.g. across GPUs). launch_attention_partials
+// writes one (m, l, n) partial per partition into the leading splits of the
+// scratch layout of attention_common.h and returns the partition count used
+// (0 for an empty range, where nothing is launched); it throws
+// std::invalid_argument unless attention_b200_supported(shape, input).
+// merge_attention_ex merges the leading `partitions` splits of every
+// row-head (partitions <= split_count(shape)), marks the remaining splits as
+// empty partials, and optionally writes the fp16 output n / l.
+unsigned launch_attention_partials(const Shape&, const DeviceInput&, unsigned partitions,
+                                   float* scratch, cudaStream_t);
+void merge_attention_ex(const Shape&, const float* scratch, unsigned partitions, float* m,
+                        float* l, float* n, void* out_f16, cudaStream_t);
+
+// Ragged batch: sequence b attends its tokens [0, seq_lens[b]) (all visible;
+// the query is the next token). Logical page j of sequence b lives at physical
+// page block_table[b * table_stride + j] of the shared pool, whose K/V/scale
+// layout is the one of attention_common.h with `pages` physical pages.
+struct BatchShape {
+  uint32_t batch, q_heads, kv_heads, dim, page_tokens, pages, table_stride;
+  uint32_t max_tokens;  // host-known upper bound of every seq_lens[b]
+  float scale;
+};
+struct BatchInput {
+  const float* q;               // float[batch * q_heads * dim]
+  const uint32_t* seq_lens;     // uint32[batch], each <= max_tokens
+  const uint32_t* block_table;  // uint32[batch * table_stride]
+  const int8_t* k;
+  const int8_t* v;
+  const float* k_scales;
+  const float* v_scales;
+};
+const char* batch_shape_error(const BatchShape&) noexcept;
+// Bytes of caller-owned workspace launch_attention_batched needs on the
+// current device (partials of every CTA/sequence piece).
+size_t batch_workspace_bytes(const BatchShape&);
+// Outputs: m, l float[batch * q_heads]; n float[batch * q_heads * dim];
+// out_f16 optional __half[batch * q_heads * dim].
+void launch_attention_batched(const BatchShape&, const BatchInput&, void* workspace,
+                              size_t workspace_bytes, float* m, float* l, float* n,
+                              void* out_f16, cudaStream_t);
+
+// Merge `shards` partial results, shard-major: m_parts/l_parts
+// float[shards * row_heads], n_parts float[shards * row_heads * dim]. The
+// result uses the same m/l/n convention (m = -inf, l = 0, n = 0 when no shard
+// saw a visible token).
+void merge_attention_shards(unsigned shards, unsigned row_heads, unsigned dim,
+                            const float* m_parts, const float* l_parts, const float* n_parts,
+                            float* m, float* l, float* n, void* out_f16, cudaStream_t);
+
+// Status word written by the kernels' bounded waits (0 = ok). Reading clears
+// it. A nonzero value means a pipeline wait gave up and that call's outputs
+// are invalid.
+cudaError_t read_device_status(int* status);
+
+}  // namespace kvbridge

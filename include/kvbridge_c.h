@@ -1,0 +1,134 @@
+/* kvbridge-b200 C ABI: plain pointers, sizes and status codes, no C++ types
+ * and no exceptions. Each function mirrors one entry point of the reference's
+ * C++ interface (dkeryyyy/kvbridge, include/kvbridge/attention_common.h and
+ * attention_shape.h) or of the B200 extensions in kvbridge/attention_b200.h.
+ *
+ * Status codes: KVB_OK on success; KVB_EINVAL where the C++ API throws
+ * std::invalid_argument (bad metadata, null or misaligned buffers, nothing was
+ * enqueued); KVB_ECUDA where it throws std::runtime_error (CUDA launch or
+ * setup failure). kvb_last_error() returns the message of the calling
+ * thread's last failure.
+ *
+ * Streams are passed as `void*` (a cudaStream_t; NULL = legacy default
+ * stream). All buffers are device pointers owned by the caller. */
+#ifndef KVBRIDGE_C_H
+#define KVBRIDGE_C_H
+
+#include <stdbool.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define KVB_OK 0
+#define KVB_EINVAL 1
+#define KVB_ECUDA 2
+
+/* Same field order and layout as kvbridge::Shape
+ * (reference include/kvbridge/attention_shape.h:9-13). */
+typedef struct kvb_shape {
+  uint32_t rows, q_heads, kv_heads, dim, page_tokens, pages, tokens, begin, end;
+  float scale;
+  bool int8;
+} kvb_shape;
+
+/* Same field order as kvbridge::DeviceInput
+ * (reference include/kvbridge/attention_common.h:54-63). */
+typedef struct kvb_device_input {
+  const float* q;
+  const int64_t* q_positions;
+  const int64_t* k_positions;
+  const uint32_t* page_table;
+  const void* k;
+  const void* v;
+  const float* k_scales;
+  const float* v_scales;
+} kvb_device_input;
+
+/* Message of the calling thread's last failed call ("" if none). */
+const char* kvb_last_error(void);
+
+/* ---- shape layer: reference src/attention_shape.cpp:20-70 ---- */
+/* attention_shape_error: NULL when valid, else a static message. */
+const char* kvb_attention_shape_error(const kvb_shape* s);
+bool kvb_attention_shape_valid(const kvb_shape* s);
+/* validate_shape / split_count / scratch_elements / output_*_elements:
+ * KVB_EINVAL (with the validation message) instead of throwing. */
+int kvb_validate_shape(const kvb_shape* s);
+int kvb_split_count(const kvb_shape* s, unsigned* splits);
+int kvb_scratch_elements(const kvb_shape* s, size_t* elements);
+int kvb_output_scalar_elements(const kvb_shape* s, size_t* elements);
+int kvb_output_numerator_elements(const kvb_shape* s, size_t* elements);
+bool kvb_attention_mma_supported(const kvb_shape* s);
+
+/* ---- kernels: reference include/kvbridge/attention_common.h:69-96 ---- */
+/* preload_*: return the cudaError_t value (0 = cudaSuccess). */
+int kvb_preload_attention_kernels(void);
+int kvb_preload_attention_reference_kernels(void);
+int kvb_preload_attention_mma_kernels(void);
+/* reference launch_attention (src/attention_shared.cu:339) */
+int kvb_launch_attention(const kvb_shape* s, const kvb_device_input* in, float* scratch,
+                         float* m, float* l, float* n, void* stream);
+/* reference launch_attention_mma (src/attention_mma.cu:33) */
+int kvb_launch_attention_mma(const kvb_shape* s, const kvb_device_input* in, float* scratch,
+                             float* m, float* l, float* n, void* stream);
+/* reference merge_attention (src/attention_shared.cu:368) */
+int kvb_merge_attention(const kvb_shape* s, const float* scratch, unsigned splits,
+                        float* m, float* l, float* n, void* stream);
+
+/* ---- B200 extensions (kvbridge/attention_b200.h) ---- */
+bool kvb_attention_b200_supported(const kvb_shape* s, const kvb_device_input* in);
+/* partitions the launcher will use for `requested` (0 = automatic) */
+int kvb_attention_partitions(const kvb_shape* s, unsigned requested, unsigned* partitions);
+/* launch_attention with explicit partitions and optional fp16 output n/l */
+int kvb_launch_attention_ex(const kvb_shape* s, const kvb_device_input* in, unsigned partitions,
+                            void* out_f16, float* scratch, float* m, float* l, float* n,
+                            void* stream);
+
+/* the two halves of kvb_launch_attention_ex (partial kernel; merge of the
+ * leading `partitions` splits). *partitions_used may be NULL. */
+int kvb_launch_attention_partials(const kvb_shape* s, const kvb_device_input* in,
+                                  unsigned partitions, float* scratch, unsigned* partitions_used,
+                                  void* stream);
+int kvb_merge_attention_ex(const kvb_shape* s, const float* scratch, unsigned partitions,
+                           float* m, float* l, float* n, void* out_f16, void* stream);
+
+typedef struct kvb_batch_shape {
+  uint32_t batch, q_heads, kv_heads, dim, page_tokens, pages, table_stride, max_tokens;
+  float scale;
+} kvb_batch_shape;
+
+typedef struct kvb_batch_input {
+  const float* q;
+  const uint32_t* seq_lens;
+  const uint32_t* block_table;
+  const int8_t* k;
+  const int8_t* v;
+  const float* k_scales;
+  const float* v_scales;
+} kvb_batch_input;
+
+const char* kvb_batch_shape_error(const kvb_batch_shape* s);
+int kvb_batch_workspace_bytes(const kvb_batch_shape* s, size_t* bytes);
+int kvb_launch_attention_batched(const kvb_batch_shape* s, const kvb_batch_input* in,
+                                 void* workspace, size_t workspace_bytes, float* m, float* l,
+                                 float* n, void* out_f16, void* stream);
+int kvb_merge_attention_shards(unsigned shards, unsigned row_heads, unsigned dim,
+                               const float* m_parts, const float* l_parts,
+                               const float* n_parts, float* m, float* l, float* n,
+                               void* out_f16, void* stream);
+/* Reads and clears the kernels' device status word (0 = ok). Returns the
+ * cudaError_t of the read. */
+int kvb_read_device_status(int* status);
+
+/* Host-side schedule of the split-K kernel, exported for tests: the CTA that
+ * owns global stage `stage` when `total` stages are split over `ctas` CTAs. */
+uint32_t kvb_schedule_cta_of(uint64_t stage, uint64_t total, uint32_t ctas);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KVBRIDGE_C_H */

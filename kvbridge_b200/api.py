@@ -1,0 +1,339 @@
+"""Python mirror of the kvbridge decode-attention interface, over the C ABI.
+
+Names, argument meaning and error behaviour follow the reference's C++ API
+(include/kvbridge/attention_shape.h and attention_common.h of
+dkeryyyy/kvbridge): invalid metadata or buffers raise ``ValueError`` (the
+reference's ``std::invalid_argument``) before anything is enqueued and CUDA
+failures raise ``RuntimeError`` (``std::runtime_error``). Buffers are device
+pointers given as ``torch.Tensor`` (their ``data_ptr()``) or plain integers;
+the caller owns them, exactly as in the reference.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+from typing import Any, Optional
+
+from . import _lib
+from ._lib import KvbBatchInput, KvbBatchShape, KvbDeviceInput, KvbShape, check
+
+kSplitTokens = 256
+
+
+def _ptr(x: Any) -> Optional[int]:
+    if x is None:
+        return None
+    if isinstance(x, int):
+        return x
+    return int(x.data_ptr())
+
+
+def _stream(stream: Any) -> Optional[int]:
+    if stream is None:
+        try:
+            import torch
+
+            if torch.cuda.is_available() and torch.cuda.is_initialized():
+                return int(torch.cuda.current_stream().cuda_stream) or None
+        except ImportError:  # pragma: no cover - torch is always present here
+            pass
+        return None
+    if isinstance(stream, int):
+        return stream or None
+    return int(stream.cuda_stream) or None
+
+
+@dataclass
+class Shape:
+    """kvbridge::Shape (reference attention_shape.h:9-13)."""
+
+    rows: int
+    q_heads: int
+    kv_heads: int
+    dim: int
+    page_tokens: int
+    pages: int
+    tokens: int
+    begin: int
+    end: int
+    scale: float
+    int8: bool = True
+
+    def c(self) -> KvbShape:
+        return KvbShape(
+            self.rows,
+            self.q_heads,
+            self.kv_heads,
+            self.dim,
+            self.page_tokens,
+            self.pages,
+            self.tokens,
+            self.begin,
+            self.end,
+            self.scale,
+            self.int8,
+        )
+
+
+@dataclass
+class DeviceInput:
+    """kvbridge::DeviceInput (reference attention_common.h:54-63)."""
+
+    q: Any
+    q_positions: Any
+    k_positions: Any
+    page_table: Any
+    k: Any
+    v: Any
+    k_scales: Any = None
+    v_scales: Any = None
+
+    def c(self) -> KvbDeviceInput:
+        return KvbDeviceInput(*(_ptr(getattr(self, f)) for f, _ in KvbDeviceInput._fields_))
+
+
+# ---- shape layer (reference src/attention_shape.cpp) ----
+
+
+def attention_shape_error(s: Shape) -> Optional[str]:
+    msg = _lib.load().kvb_attention_shape_error(ctypes.byref(s.c()))
+    return msg.decode() if msg else None
+
+
+def attention_shape_valid(s: Shape) -> bool:
+    return bool(_lib.load().kvb_attention_shape_valid(ctypes.byref(s.c())))
+
+
+def validate_shape(s: Shape) -> None:
+    check(_lib.load().kvb_validate_shape(ctypes.byref(s.c())))
+
+
+def split_count(s: Shape) -> int:
+    out = ctypes.c_uint()
+    check(_lib.load().kvb_split_count(ctypes.byref(s.c()), ctypes.byref(out)))
+    return out.value
+
+
+def _size_query(fn_name: str, s: Shape) -> int:
+    out = ctypes.c_size_t()
+    check(getattr(_lib.load(), fn_name)(ctypes.byref(s.c()), ctypes.byref(out)))
+    return out.value
+
+
+def scratch_elements(s: Shape) -> int:
+    return _size_query("kvb_scratch_elements", s)
+
+
+def output_scalar_elements(s: Shape) -> int:
+    return _size_query("kvb_output_scalar_elements", s)
+
+
+def output_numerator_elements(s: Shape) -> int:
+    return _size_query("kvb_output_numerator_elements", s)
+
+
+def attention_mma_supported(s: Shape) -> bool:
+    return bool(_lib.load().kvb_attention_mma_supported(ctypes.byref(s.c())))
+
+
+# ---- kernels (reference attention_common.h:69-96) ----
+
+
+def preload_attention_kernels() -> int:
+    return int(_lib.load().kvb_preload_attention_kernels())
+
+
+def preload_attention_reference_kernels() -> int:
+    return int(_lib.load().kvb_preload_attention_reference_kernels())
+
+
+def preload_attention_mma_kernels() -> int:
+    return int(_lib.load().kvb_preload_attention_mma_kernels())
+
+
+def launch_attention(s: Shape, inp: DeviceInput, scratch, m, l, n, stream=None) -> None:
+    check(
+        _lib.load().kvb_launch_attention(
+            ctypes.byref(s.c()),
+            ctypes.byref(inp.c()),
+            _ptr(scratch),
+            _ptr(m),
+            _ptr(l),
+            _ptr(n),
+            _stream(stream),
+        )
+    )
+
+
+def launch_attention_mma(s: Shape, inp: DeviceInput, scratch, m, l, n, stream=None) -> None:
+    check(
+        _lib.load().kvb_launch_attention_mma(
+            ctypes.byref(s.c()),
+            ctypes.byref(inp.c()),
+            _ptr(scratch),
+            _ptr(m),
+            _ptr(l),
+            _ptr(n),
+            _stream(stream),
+        )
+    )
+
+
+def merge_attention(s: Shape, scratch, splits: int, m, l, n, stream=None) -> None:
+    check(
+        _lib.load().kvb_merge_attention(
+            ctypes.byref(s.c()), _ptr(scratch), splits, _ptr(m), _ptr(l), _ptr(n), _stream(stream)
+        )
+    )
+
+
+# ---- B200 extensions (include/kvbridge/attention_b200.h) ----
+
+
+def attention_b200_supported(s: Shape, inp: DeviceInput) -> bool:
+    return bool(_lib.load().kvb_attention_b200_supported(ctypes.byref(s.c()), ctypes.byref(inp.c())))
+
+
+def attention_partitions(s: Shape, requested: int = 0) -> int:
+    out = ctypes.c_uint()
+    check(_lib.load().kvb_attention_partitions(ctypes.byref(s.c()), requested, ctypes.byref(out)))
+    return out.value
+
+
+def launch_attention_ex(
+    s: Shape, inp: DeviceInput, scratch, m, l, n, partitions: int = 0, out_f16=None, stream=None
+) -> None:
+    check(
+        _lib.load().kvb_launch_attention_ex(
+            ctypes.byref(s.c()),
+            ctypes.byref(inp.c()),
+            partitions,
+            _ptr(out_f16),
+            _ptr(scratch),
+            _ptr(m),
+            _ptr(l),
+            _ptr(n),
+            _stream(stream),
+        )
+    )
+
+
+def launch_attention_partials(s: Shape, inp: DeviceInput, scratch, partitions: int = 0, stream=None) -> int:
+    """Partial kernel only; returns the partition count it used."""
+    used = ctypes.c_uint()
+    check(
+        _lib.load().kvb_launch_attention_partials(
+            ctypes.byref(s.c()), ctypes.byref(inp.c()), partitions, _ptr(scratch), ctypes.byref(used), _stream(stream)
+        )
+    )
+    return used.value
+
+
+def merge_attention_ex(s: Shape, scratch, partitions: int, m, l, n, out_f16=None, stream=None) -> None:
+    check(
+        _lib.load().kvb_merge_attention_ex(
+            ctypes.byref(s.c()), _ptr(scratch), partitions, _ptr(m), _ptr(l), _ptr(n), _ptr(out_f16), _stream(stream)
+        )
+    )
+
+
+@dataclass
+class BatchShape:
+    batch: int
+    q_heads: int
+    kv_heads: int
+    dim: int
+    page_tokens: int
+    pages: int
+    table_stride: int
+    max_tokens: int
+    scale: float
+
+    def c(self) -> KvbBatchShape:
+        return KvbBatchShape(
+            self.batch,
+            self.q_heads,
+            self.kv_heads,
+            self.dim,
+            self.page_tokens,
+            self.pages,
+            self.table_stride,
+            self.max_tokens,
+            self.scale,
+        )
+
+
+@dataclass
+class BatchInput:
+    q: Any
+    seq_lens: Any
+    block_table: Any
+    k: Any
+    v: Any
+    k_scales: Any
+    v_scales: Any
+
+    def c(self) -> KvbBatchInput:
+        return KvbBatchInput(*(_ptr(getattr(self, f)) for f, _ in KvbBatchInput._fields_))
+
+
+def batch_shape_error(s: BatchShape) -> Optional[str]:
+    msg = _lib.load().kvb_batch_shape_error(ctypes.byref(s.c()))
+    return msg.decode() if msg else None
+
+
+def batch_workspace_bytes(s: BatchShape) -> int:
+    out = ctypes.c_size_t()
+    check(_lib.load().kvb_batch_workspace_bytes(ctypes.byref(s.c()), ctypes.byref(out)))
+    return out.value
+
+
+def launch_attention_batched(
+    s: BatchShape, inp: BatchInput, workspace, workspace_bytes: int, m, l, n, out_f16=None, stream=None
+) -> None:
+    check(
+        _lib.load().kvb_launch_attention_batched(
+            ctypes.byref(s.c()),
+            ctypes.byref(inp.c()),
+            _ptr(workspace),
+            workspace_bytes,
+            _ptr(m),
+            _ptr(l),
+            _ptr(n),
+            _ptr(out_f16),
+            _stream(stream),
+        )
+    )
+
+
+def merge_attention_shards(
+    shards: int, row_heads: int, dim: int, m_parts, l_parts, n_parts, m, l, n, out_f16=None, stream=None
+) -> None:
+    check(
+        _lib.load().kvb_merge_attention_shards(
+            shards,
+            row_heads,
+            dim,
+            _ptr(m_parts),
+            _ptr(l_parts),
+            _ptr(n_parts),
+            _ptr(m),
+            _ptr(l),
+            _ptr(n),
+            _ptr(out_f16),
+            _stream(stream),
+        )
+    )
+
+
+def read_device_status() -> int:
+    """Read and clear the kernels' status word (0 = every bounded wait succeeded)."""
+    status = ctypes.c_int()
+    code = _lib.load().kvb_read_device_status(ctypes.byref(status))
+    if code != 0:
+        raise RuntimeError(f"reading the device status failed: cudaError {code}")
+    return status.value
+
+
+def schedule_cta_of(stage: int, total: int, ctas: int) -> int:
+    return int(_lib.load().kvb_schedule_cta_of(stage, total, ctas))

@@ -1,0 +1,505 @@
+// Host launchers of the kvbridge-b200 decode-attention path: the reference's
+// C++ entry points (include/kvbridge/attention_common.h) and the B200
+// extensions (include/kvbridge/attention_b200.h). Every kernel of the library
+// is instantiated in this one translation unit.
+#include <algorithm>
+#include <array>
+#include <atomic>
+#include <cmath>
+#include <cstring>
+#include <limits>
+#include <map>
+#include <mutex>
+#include <stdexcept>
+#include <utility>
+
+#include "kvbridge/attention_b200.h"
+#include "kvbridge/attention_common.h"
+#include "launch_checks.h"
+#include "decode_simt.cuh"
+#include "decode_tma.cuh"
+#include "merge.cuh"
+
+namespace kvbridge {
+namespace {
+
+using detail::aligned_to;
+using detail::cuda_ok;
+
+// ---------------------------------------------------------------------------
+// Device facts, cached per device ordinal (they never change for a device).
+
+struct DeviceFacts {
+  int sms = 0;
+  int major = 0;
+};
+
+DeviceFacts current_device_facts() {
+  static std::mutex mu;
+  static std::map<int, DeviceFacts> cache;
+  int dev = 0;
+  cuda_ok(cudaGetDevice(&dev), "cudaGetDevice");
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = cache.find(dev);
+  if (it != cache.end()) return it->second;
+  DeviceFacts f;
+  cuda_ok(cudaDeviceGetAttribute(&f.sms, cudaDevAttrMultiProcessorCount, dev), "SM count");
+  cuda_ok(cudaDeviceGetAttribute(&f.major, cudaDevAttrComputeCapabilityMajor, dev),
+          "compute capability");
+  cache.emplace(dev, f);
+  return f;
+}
+
+// ---------------------------------------------------------------------------
+// Tensor-core kernel variants: (head dim, n-tiles of 8 query rows, stages).
+
+struct FastVariant {
+  const void* fn = nullptr;
+  uint32_t smem = 0;
+  void (*launch)(const kvb::DecodeParams&, cudaStream_t) = nullptr;
+};
+
+void launch_pdl(const void* fn, dim3 grid, dim3 block, uint32_t smem, cudaStream_t stream,
+                void** args, const char* what) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cuda_ok(cudaLaunchKernelExC(&cfg, fn, args), what);
+}
+
+template <int D, int NT, int STAGES>
+void launch_fast_variant(const kvb::DecodeParams& prm, cudaStream_t stream) {
+  const void* fn = reinterpret_cast<const void*>(&kvb::decode_partial_kernel<D, NT, STAGES>);
+  constexpr uint32_t smem = kvb::DecodeSmem<D, NT, STAGES>::kBytes;
+  cuda_ok(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)),
+          "decode kernel shared-memory opt-in");
+  kvb::DecodeParams copy = prm;
+  void* args[] = {&copy};
+  launch_pdl(fn, dim3(prm.ctas), dim3(kvb::kDecodeThreads), smem, stream, args,
+             "decode partial launch");
+}
+
+template <int D, int NT, int STAGES>
+FastVariant make_variant() {
+  FastVariant v;
+  v.fn = reinterpret_cast<const void*>(&kvb::decode_partial_kernel<D, NT, STAGES>);
+  v.smem = kvb::DecodeSmem<D, NT, STAGES>::kBytes;
+  v.launch = &launch_fast_variant<D, NT, STAGES>;
+  return v;
+}
+
+// Stage counts keep two CTAs per SM resident (<= ~110 KB each) except at
+// dim 256, where one CTA per SM holds four 33 KB stages.
+FastVariant fast_variant(uint32_t dim, uint32_t nt) {
+  if (dim == 128 && nt == 1) return make_variant<128, 1, 5>();
+  if (dim == 128 && nt == 2) return make_variant<128, 2, 4>();
+  if (dim == 64 && nt == 1) return make_variant<64, 1, 8>();
+  if (dim == 64 && nt == 2) return make_variant<64, 2, 7>();
+  if (dim == 256 && nt == 1) return make_variant<256, 1, 4>();
+  return FastVariant{};
+}
+
+// Resident CTAs of a variant per SM on the current device (cached).
+int resident_ctas(const FastVariant& v) {
+  static std::mutex mu;
+  static std::map<std::pair<int, const void*>, int> cache;
+  int dev = 0;
+  cuda_ok(cudaGetDevice(&dev), "cudaGetDevice");
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = cache.find({dev, v.fn});
+    if (it != cache.end()) return it->second;
+  }
+  cuda_ok(cudaFuncSetAttribute(v.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(v.smem)),
+          "decode kernel shared-memory opt-in");
+  int blocks = 0;
+  cuda_ok(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, v.fn, kvb::kDecodeThreads,
+                                                        v.smem),
+          "occupancy query");
+  blocks = std::max(blocks, 1);
+  std::lock_guard<std::mutex> lock(mu);
+  cache[{dev, v.fn}] = blocks;
+  return blocks;
+}
+
+uint32_t query_rows(const Shape& s) { return s.rows * (s.q_heads / s.kv_heads); }
+
+bool fast_geometry(uint32_t dim, uint32_t page_tokens, uint32_t qrows) {
+  const bool dim_ok = dim == 64 || dim == 128 || dim == 256;
+  const bool page_ok = page_tokens == 16 || page_tokens == 32 || page_tokens == 64;
+  const uint32_t max_rows = dim == 256 ? 8u : 16u;
+  return dim_ok && page_ok && qrows >= 1 && qrows <= max_rows;
+}
+
+uint32_t log2_exact(uint32_t x) {
+  uint32_t r = 0;
+  while ((1u << r) < x) ++r;
+  return r;
+}
+
+// ---------------------------------------------------------------------------
+// Merge launches.
+
+void launch_merge(int mode, const kvb::MergeParams& prm, cudaStream_t stream) {
+  const uint32_t blocks = (prm.row_heads + kvb::kMergeWarps - 1) / kvb::kMergeWarps;
+  if (blocks == 0) return;
+  kvb::MergeParams copy = prm;
+  void* args[] = {&copy};
+  const void* fn = nullptr;
+  if (mode == kvb::kMergeScratch)
+    fn = reinterpret_cast<const void*>(&kvb::merge_kernel<kvb::kMergeScratch>);
+  else if (mode == kvb::kMergeBatched)
+    fn = reinterpret_cast<const void*>(&kvb::merge_kernel<kvb::kMergeBatched>);
+  else
+    fn = reinterpret_cast<const void*>(&kvb::merge_kernel<kvb::kMergeShards>);
+  launch_pdl(fn, dim3(blocks), dim3(32 * kvb::kMergeWarps), 0, stream, args,
+             "attention merge launch");
+}
+
+kvb::MergeParams scratch_merge_params(const Shape& s, float* scratch, uint32_t np, uint32_t stride,
+                                      bool fill_empty, float* m, float* l, float* n, void* out) {
+  kvb::MergeParams mp{};
+  mp.part = scratch;
+  mp.m = m;
+  mp.l = l;
+  mp.n = n;
+  mp.out = static_cast<__half*>(out);
+  mp.row_heads = s.rows * s.q_heads;
+  mp.dim = s.dim;
+  mp.np = np;
+  mp.split_stride = stride;
+  mp.fill_empty = fill_empty ? 1u : 0u;
+  return mp;
+}
+
+void launch_simt(const Shape& s, const DeviceInput& in, float* scratch, uint32_t splits,
+                 cudaStream_t stream) {
+  kvb::SimtParams sp{};
+  sp.q = in.q;
+  sp.q_positions = in.q_positions;
+  sp.k_positions = in.k_positions;
+  sp.table = in.page_table;
+  sp.k = in.k;
+  sp.v = in.v;
+  sp.k_scales = in.k_scales;
+  sp.v_scales = in.v_scales;
+  sp.scratch = scratch;
+  sp.rows = s.rows;
+  sp.q_heads = s.q_heads;
+  sp.kv_heads = s.kv_heads;
+  sp.dim = s.dim;
+  sp.page_tokens = s.page_tokens;
+  sp.pages = s.pages;
+  sp.begin = s.begin;
+  sp.end = s.end;
+  sp.splits = splits;
+  sp.scale = s.scale;
+  void* args[] = {&sp};
+  const void* fn = s.int8 ? reinterpret_cast<const void*>(&kvb::decode_simt_kernel<true>)
+                          : reinterpret_cast<const void*>(&kvb::decode_simt_kernel<false>);
+  launch_pdl(fn, dim3(s.rows * s.kv_heads, splits), dim3(kvb::kSimtThreads), 0, stream, args,
+             "attention split launch");
+}
+
+uint32_t batched_ctas(const FastVariant& v) {
+  return uint32_t(current_device_facts().sms) * uint32_t(resident_ctas(v));
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// B200 predicates and planning.
+
+bool attention_b200_supported(const Shape& s, const DeviceInput& in) noexcept {
+  if (!attention_shape_valid(s) || !s.int8) return false;
+  if (!fast_geometry(s.dim, s.page_tokens, query_rows(s))) return false;
+  return aligned_to(in.q, 16) && aligned_to(in.k, 16) && aligned_to(in.v, 16) &&
+         aligned_to(in.k_scales, 16) && aligned_to(in.v_scales, 16);
+}
+
+unsigned attention_partitions(const Shape& s, unsigned requested) {
+  validate_shape(s);
+  const uint32_t stages = kvb::stages_of_range(s.begin, s.end);
+  if (stages == 0) return 0;
+  uint32_t parts = requested;
+  if (parts == 0) {
+    const uint32_t nt = (query_rows(s) + 7) / 8;
+    const FastVariant v = fast_variant(s.dim, nt);
+    const uint32_t wave =
+        v.fn ? uint32_t(current_device_facts().sms) * uint32_t(resident_ctas(v)) : 1u;
+    parts = std::max(1u, wave / s.kv_heads);
+  }
+  parts = std::min(parts, stages);
+  parts = std::min(parts, split_count(s));
+  return std::max(parts, 1u);
+}
+
+// ---------------------------------------------------------------------------
+// Reference entry points.
+
+cudaError_t preload_attention_reference_kernels() {
+  cudaFuncAttributes a{};
+  const void* fns[] = {
+      reinterpret_cast<const void*>(&kvb::decode_simt_kernel<true>),
+      reinterpret_cast<const void*>(&kvb::decode_simt_kernel<false>),
+      reinterpret_cast<const void*>(&kvb::merge_kernel<kvb::kMergeScratch>),
+      reinterpret_cast<const void*>(&kvb::merge_kernel<kvb::kMergeBatched>),
+      reinterpret_cast<const void*>(&kvb::merge_kernel<kvb::kMergeShards>),
+  };
+  for (const void* fn : fns) {
+    const cudaError_t code = cudaFuncGetAttributes(&a, fn);
+    if (code != cudaSuccess) return code;
+  }
+  return cudaSuccess;
+}
+
+cudaError_t preload_attention_mma_kernels() {
+  int dev = 0, major = 0;
+  cudaError_t code = cudaGetDevice(&dev);
+  if (code != cudaSuccess) return code;
+  code = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+  if (code != cudaSuccess) return code;
+  if (major != 10) return cudaErrorNotSupported;
+  const std::pair<uint32_t, uint32_t> variants[] = {{128, 1}, {128, 2}, {64, 1}, {64, 2}, {256, 1}};
+  for (const auto& dv : variants) {
+    const FastVariant v = fast_variant(dv.first, dv.second);
+    cudaFuncAttributes a{};
+    code = cudaFuncGetAttributes(&a, v.fn);
+    if (code != cudaSuccess) return code;
+    code = cudaFuncSetAttribute(v.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(v.smem));
+    if (code != cudaSuccess) return code;
+  }
+  return cudaSuccess;
+}
+
+cudaError_t preload_attention_kernels() {
+  const cudaError_t code = preload_attention_reference_kernels();
+  return code == cudaSuccess ? preload_attention_mma_kernels() : code;
+}
+
+unsigned launch_attention_partials(const Shape& s, const DeviceInput& in, unsigned partitions,
+                                   float* scratch, cudaStream_t stream) {
+  if (scratch == nullptr) throw std::invalid_argument("scratch must be a non-null device buffer");
+  detail::check_inputs(s, in, scratch, scratch, scratch, scratch);
+  if (!attention_b200_supported(s, in))
+    throw std::invalid_argument("launch_attention_partials needs the tensor-core geometry "
+                                "(attention_b200_supported)");
+  const uint32_t splits = split_count(s);
+  const uint32_t parts = attention_partitions(s, partitions);
+  if (parts == 0) return 0;
+  const uint32_t nt = (query_rows(s) + 7) / 8;
+  const FastVariant v = fast_variant(s.dim, nt);
+  kvb::DecodeParams prm{};
+  prm.q = in.q;
+  prm.q_positions = in.q_positions;
+  prm.k_positions = in.k_positions;
+  prm.table = in.page_table;
+  prm.k = static_cast<const int8_t*>(in.k);
+  prm.v = static_cast<const int8_t*>(in.v);
+  prm.k_scales = in.k_scales;
+  prm.v_scales = in.v_scales;
+  prm.seq_lens = nullptr;
+  prm.part = scratch;
+  prm.batch = 1;
+  prm.rows = s.rows;
+  prm.q_heads = s.q_heads;
+  prm.kv_heads = s.kv_heads;
+  prm.group = s.q_heads / s.kv_heads;
+  prm.qr = query_rows(s);
+  prm.page_tokens = s.page_tokens;
+  prm.log2_page = log2_exact(s.page_tokens);
+  prm.pages = s.pages;
+  prm.table_stride = 0;
+  prm.begin = s.begin;
+  prm.end = s.end;
+  prm.seg_stages = kvb::stages_of_range(s.begin, s.end);
+  prm.split_stride = splits;
+  prm.max_tokens = s.tokens;
+  prm.ctas = parts * s.kv_heads;
+  prm.total_stages = uint64_t(prm.seg_stages) * s.kv_heads;
+  prm.score_scale = s.scale;
+  v.launch(prm, stream);
+  return parts;
+}
+
+void merge_attention_ex(const Shape& s, const float* scratch, unsigned partitions, float* m,
+                        float* l, float* n, void* out_f16, cudaStream_t stream) {
+  detail::check_outputs(s, scratch, m, l, n);
+  const uint32_t splits = split_count(s);
+  if (partitions > splits)
+    throw std::invalid_argument("merge partitions exceed split_count(shape)");
+  launch_merge(kvb::kMergeScratch,
+               scratch_merge_params(s, const_cast<float*>(scratch), partitions, splits,
+                                    partitions < splits, m, l, n, out_f16),
+               stream);
+}
+
+void launch_attention_ex(const Shape& s, const DeviceInput& in, const LaunchOptions& opt,
+                         float* scratch, float* m, float* l, float* n, cudaStream_t stream) {
+  detail::check_inputs(s, in, scratch, m, l, n);
+  const uint32_t splits = split_count(s);
+  if (!attention_b200_supported(s, in)) {
+    launch_simt(s, in, scratch, splits, stream);
+    launch_merge(kvb::kMergeScratch,
+                 scratch_merge_params(s, scratch, splits, splits, false, m, l, n, opt.out_f16),
+                 stream);
+    return;
+  }
+  const uint32_t parts = launch_attention_partials(s, in, opt.partitions, scratch, stream);
+  merge_attention_ex(s, scratch, parts, m, l, n, opt.out_f16, stream);
+}
+
+void launch_attention(const Shape& s, const DeviceInput& in, float* scratch, float* m, float* l,
+                      float* n, cudaStream_t stream) {
+  launch_attention_ex(s, in, LaunchOptions{0, nullptr}, scratch, m, l, n, stream);
+}
+
+void launch_attention_mma(const Shape& s, const DeviceInput& in, float* scratch, float* m,
+                          float* l, float* n, cudaStream_t stream) {
+  detail::check_inputs(s, in, scratch, m, l, n);
+  if (!attention_mma_supported(s))
+    throw std::invalid_argument(
+        "launch_attention_mma requires int8 KV, rows8/group6/dim256/page32 and a page-aligned "
+        "begin");
+  cuda_ok(preload_attention_mma_kernels(), "MMA current-context preparation");
+  launch_attention_ex(s, in, LaunchOptions{0, nullptr}, scratch, m, l, n, stream);
+}
+
+void merge_attention(const Shape& s, const float* scratch, unsigned splits, float* m, float* l,
+                     float* n, cudaStream_t stream) {
+  detail::check_outputs(s, scratch, m, l, n);
+  if (splits != split_count(s))
+    throw std::invalid_argument("merge split count does not match shape");
+  launch_merge(kvb::kMergeScratch,
+               scratch_merge_params(s, const_cast<float*>(scratch), splits, splits, false, m, l,
+                                    n, nullptr),
+               stream);
+}
+
+// ---------------------------------------------------------------------------
+// Batched ragged decode.
+
+const char* batch_shape_error(const BatchShape& s) noexcept {
+  if (s.batch == 0 || s.q_heads == 0 || s.kv_heads == 0)
+    return "batch and head counts must be positive";
+  if (s.q_heads % s.kv_heads) return "q_heads must be divisible by kv_heads";
+  if (!fast_geometry(s.dim, s.page_tokens, s.q_heads / s.kv_heads))
+    return "batched decode needs dim 64/128/256, page_tokens 16/32/64 and a query group of at "
+           "most 16 (8 at dim 256)";
+  if (s.pages == 0 || s.table_stride == 0) return "pages and table_stride must be positive";
+  if (uint64_t(s.max_tokens) > uint64_t(s.table_stride) * s.page_tokens)
+    return "max_tokens exceeds the block-table row capacity";
+  if (!std::isfinite(s.scale)) return "score scale must be finite";
+  if (uint64_t(s.batch) * s.q_heads > 0x7fffffffull) return "batch/head product too large";
+  const uint64_t extent = uint64_t(s.pages) * s.kv_heads * s.page_tokens * s.dim;
+  if (extent > std::numeric_limits<uint32_t>::max())
+    return "physical KV extent exceeds 32-bit kernel offsets";
+  if (uint64_t(s.batch) * s.table_stride > std::numeric_limits<uint32_t>::max())
+    return "block table exceeds 32-bit indexing";
+  return nullptr;
+}
+
+size_t batch_workspace_bytes(const BatchShape& s) {
+  if (const char* e = batch_shape_error(s)) throw std::invalid_argument(e);
+  const uint32_t group = s.q_heads / s.kv_heads;
+  const FastVariant v = fast_variant(s.dim, (group + 7) / 8);
+  const uint64_t slots = uint64_t(batched_ctas(v)) + uint64_t(s.batch) * s.kv_heads;
+  return size_t(slots * group * (s.dim + 2) * sizeof(float));
+}
+
+void launch_attention_batched(const BatchShape& s, const BatchInput& in, void* workspace,
+                              size_t workspace_bytes, float* m, float* l, float* n, void* out_f16,
+                              cudaStream_t stream) {
+  if (const char* e = batch_shape_error(s)) throw std::invalid_argument(e);
+  if (!in.q || !in.seq_lens || !in.block_table || !in.k || !in.v || !in.k_scales ||
+      !in.v_scales || !workspace || !m || !l || !n)
+    throw std::invalid_argument("batched decode buffers must be non-null");
+  if (!aligned_to(in.q, 16) || !aligned_to(in.k, 16) || !aligned_to(in.v, 16) ||
+      !aligned_to(in.k_scales, 16) || !aligned_to(in.v_scales, 16) || !aligned_to(workspace, 16))
+    throw std::invalid_argument("batched decode buffers must be 16-byte aligned");
+  if (workspace_bytes < batch_workspace_bytes(s))
+    throw std::invalid_argument("workspace smaller than batch_workspace_bytes(shape)");
+  const uint32_t group = s.q_heads / s.kv_heads;
+  const FastVariant v = fast_variant(s.dim, (group + 7) / 8);
+  kvb::DecodeParams prm{};
+  prm.q = in.q;
+  prm.table = in.block_table;
+  prm.k = in.k;
+  prm.v = in.v;
+  prm.k_scales = in.k_scales;
+  prm.v_scales = in.v_scales;
+  prm.seq_lens = in.seq_lens;
+  prm.part = static_cast<float*>(workspace);
+  prm.batch = s.batch;
+  prm.rows = 1;
+  prm.q_heads = s.q_heads;
+  prm.kv_heads = s.kv_heads;
+  prm.group = group;
+  prm.qr = group;
+  prm.page_tokens = s.page_tokens;
+  prm.log2_page = log2_exact(s.page_tokens);
+  prm.pages = s.pages;
+  prm.table_stride = s.table_stride;
+  prm.max_tokens = s.max_tokens;
+  prm.ctas = batched_ctas(v);
+  prm.score_scale = s.scale;
+  v.launch(prm, stream);
+
+  kvb::MergeParams mp{};
+  mp.part = static_cast<float*>(workspace);
+  mp.m = m;
+  mp.l = l;
+  mp.n = n;
+  mp.out = static_cast<__half*>(out_f16);
+  mp.row_heads = s.batch * s.q_heads;
+  mp.dim = s.dim;
+  mp.seq_lens = in.seq_lens;
+  mp.batch = s.batch;
+  mp.q_heads = s.q_heads;
+  mp.kv_heads = s.kv_heads;
+  mp.group = group;
+  mp.max_tokens = s.max_tokens;
+  mp.ctas = prm.ctas;
+  launch_merge(kvb::kMergeBatched, mp, stream);
+}
+
+void merge_attention_shards(unsigned shards, unsigned row_heads, unsigned dim,
+                            const float* m_parts, const float* l_parts, const float* n_parts,
+                            float* m, float* l, float* n, void* out_f16, cudaStream_t stream) {
+  if (shards == 0 || row_heads == 0 || dim == 0 || dim > 256)
+    throw std::invalid_argument("shards, row_heads must be positive and dim in [1,256]");
+  if (!m_parts || !l_parts || !n_parts || !m || !l || !n)
+    throw std::invalid_argument("shard merge buffers must be non-null");
+  kvb::MergeParams mp{};
+  mp.m_parts = m_parts;
+  mp.l_parts = l_parts;
+  mp.n_parts = n_parts;
+  mp.m = m;
+  mp.l = l;
+  mp.n = n;
+  mp.out = static_cast<__half*>(out_f16);
+  mp.row_heads = row_heads;
+  mp.dim = dim;
+  mp.np = shards;
+  launch_merge(kvb::kMergeShards, mp, stream);
+}
+
+cudaError_t read_device_status(int* status) {
+  if (status == nullptr) return cudaErrorInvalidValue;
+  int value = 0;
+  cudaError_t code = cudaMemcpyFromSymbol(&value, kvb::g_kvb_status, sizeof(int));
+  if (code != cudaSuccess) return code;
+  const int zero = 0;
+  code = cudaMemcpyToSymbol(kvb::g_kvb_status, &zero, sizeof(int));
+  *status = value;
+  return code;
+}
+
+}  // namespace kvbridge

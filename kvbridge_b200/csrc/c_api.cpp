@@ -1,0 +1,245 @@
+// extern "C" boundary of kvbridge-b200 (include/kvbridge_c.h). Each function
+// converts the C structs to the kvbridge:: types, calls the C++ entry point
+// and turns its exceptions into status codes plus a thread-local message; no
+// exception crosses this boundary.
+#include <cstddef>
+#include <cstring>
+#include <exception>
+#include <stdexcept>
+#include <string>
+
+#include "kvbridge/attention_b200.h"
+#include "kvbridge/attention_common.h"
+#include "kvbridge_c.h"
+#include "kvb_schedule.h"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+static_assert(sizeof(kvb_shape) == sizeof(kvbridge::Shape), "kvb_shape must mirror Shape");
+static_assert(offsetof(kvb_shape, scale) == offsetof(kvbridge::Shape, scale), "Shape layout");
+static_assert(offsetof(kvb_shape, int8) == offsetof(kvbridge::Shape, int8), "Shape layout");
+static_assert(sizeof(kvb_device_input) == sizeof(kvbridge::DeviceInput), "DeviceInput layout");
+
+kvbridge::Shape to_shape(const kvb_shape* s) {
+  if (s == nullptr) throw std::invalid_argument("shape pointer is null");
+  kvbridge::Shape out;
+  out.rows = s->rows;
+  out.q_heads = s->q_heads;
+  out.kv_heads = s->kv_heads;
+  out.dim = s->dim;
+  out.page_tokens = s->page_tokens;
+  out.pages = s->pages;
+  out.tokens = s->tokens;
+  out.begin = s->begin;
+  out.end = s->end;
+  out.scale = s->scale;
+  out.int8 = s->int8;
+  return out;
+}
+
+kvbridge::DeviceInput to_input(const kvb_device_input* in) {
+  if (in == nullptr) throw std::invalid_argument("input pointer is null");
+  return kvbridge::DeviceInput{in->q,       in->q_positions, in->k_positions, in->page_table,
+                               in->k,       in->v,           in->k_scales,    in->v_scales};
+}
+
+kvbridge::BatchShape to_batch_shape(const kvb_batch_shape* s) {
+  if (s == nullptr) throw std::invalid_argument("shape pointer is null");
+  return kvbridge::BatchShape{s->batch,       s->q_heads,      s->kv_heads,
+                              s->dim,         s->page_tokens,  s->pages,
+                              s->table_stride, s->max_tokens,  s->scale};
+}
+
+kvbridge::BatchInput to_batch_input(const kvb_batch_input* in) {
+  if (in == nullptr) throw std::invalid_argument("input pointer is null");
+  return kvbridge::BatchInput{in->q, in->seq_lens, in->block_table, in->k,
+                              in->v, in->k_scales, in->v_scales};
+}
+
+template <class F>
+int guarded(F&& body) {
+  try {
+    body();
+    g_last_error.clear();
+    return KVB_OK;
+  } catch (const std::invalid_argument& e) {
+    g_last_error = e.what();
+    return KVB_EINVAL;
+  } catch (const std::exception& e) {
+    g_last_error = e.what();
+    return KVB_ECUDA;
+  } catch (...) {
+    g_last_error = "unknown error";
+    return KVB_ECUDA;
+  }
+}
+
+cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
+
+}  // namespace
+
+extern "C" {
+
+const char* kvb_last_error(void) { return g_last_error.c_str(); }
+
+const char* kvb_attention_shape_error(const kvb_shape* s) {
+  if (s == nullptr) return "shape pointer is null";
+  return kvbridge::attention_shape_error(to_shape(s));
+}
+
+bool kvb_attention_shape_valid(const kvb_shape* s) {
+  return s != nullptr && kvbridge::attention_shape_valid(to_shape(s));
+}
+
+int kvb_validate_shape(const kvb_shape* s) {
+  return guarded([&] { kvbridge::validate_shape(to_shape(s)); });
+}
+
+int kvb_split_count(const kvb_shape* s, unsigned* splits) {
+  return guarded([&] {
+    const unsigned v = kvbridge::split_count(to_shape(s));
+    if (splits == nullptr) throw std::invalid_argument("output pointer is null");
+    *splits = v;
+  });
+}
+
+int kvb_scratch_elements(const kvb_shape* s, size_t* elements) {
+  return guarded([&] {
+    const size_t v = kvbridge::scratch_elements(to_shape(s));
+    if (elements == nullptr) throw std::invalid_argument("output pointer is null");
+    *elements = v;
+  });
+}
+
+int kvb_output_scalar_elements(const kvb_shape* s, size_t* elements) {
+  return guarded([&] {
+    const size_t v = kvbridge::output_scalar_elements(to_shape(s));
+    if (elements == nullptr) throw std::invalid_argument("output pointer is null");
+    *elements = v;
+  });
+}
+
+int kvb_output_numerator_elements(const kvb_shape* s, size_t* elements) {
+  return guarded([&] {
+    const size_t v = kvbridge::output_numerator_elements(to_shape(s));
+    if (elements == nullptr) throw std::invalid_argument("output pointer is null");
+    *elements = v;
+  });
+}
+
+bool kvb_attention_mma_supported(const kvb_shape* s) {
+  return s != nullptr && kvbridge::attention_mma_supported(to_shape(s));
+}
+
+int kvb_preload_attention_kernels(void) { return int(kvbridge::preload_attention_kernels()); }
+int kvb_preload_attention_reference_kernels(void) {
+  return int(kvbridge::preload_attention_reference_kernels());
+}
+int kvb_preload_attention_mma_kernels(void) {
+  return int(kvbridge::preload_attention_mma_kernels());
+}
+
+int kvb_launch_attention(const kvb_shape* s, const kvb_device_input* in, float* scratch, float* m,
+                         float* l, float* n, void* stream) {
+  return guarded([&] {
+    kvbridge::launch_attention(to_shape(s), to_input(in), scratch, m, l, n, as_stream(stream));
+  });
+}
+
+int kvb_launch_attention_mma(const kvb_shape* s, const kvb_device_input* in, float* scratch,
+                             float* m, float* l, float* n, void* stream) {
+  return guarded([&] {
+    kvbridge::launch_attention_mma(to_shape(s), to_input(in), scratch, m, l, n,
+                                   as_stream(stream));
+  });
+}
+
+int kvb_merge_attention(const kvb_shape* s, const float* scratch, unsigned splits, float* m,
+                        float* l, float* n, void* stream) {
+  return guarded([&] {
+    kvbridge::merge_attention(to_shape(s), scratch, splits, m, l, n, as_stream(stream));
+  });
+}
+
+bool kvb_attention_b200_supported(const kvb_shape* s, const kvb_device_input* in) {
+  if (s == nullptr || in == nullptr) return false;
+  return kvbridge::attention_b200_supported(to_shape(s), to_input(in));
+}
+
+int kvb_attention_partitions(const kvb_shape* s, unsigned requested, unsigned* partitions) {
+  return guarded([&] {
+    const unsigned v = kvbridge::attention_partitions(to_shape(s), requested);
+    if (partitions == nullptr) throw std::invalid_argument("output pointer is null");
+    *partitions = v;
+  });
+}
+
+int kvb_launch_attention_ex(const kvb_shape* s, const kvb_device_input* in, unsigned partitions,
+                            void* out_f16, float* scratch, float* m, float* l, float* n,
+                            void* stream) {
+  return guarded([&] {
+    kvbridge::launch_attention_ex(to_shape(s), to_input(in),
+                                  kvbridge::LaunchOptions{partitions, out_f16}, scratch, m, l, n,
+                                  as_stream(stream));
+  });
+}
+
+int kvb_launch_attention_partials(const kvb_shape* s, const kvb_device_input* in,
+                                  unsigned partitions, float* scratch, unsigned* partitions_used,
+                                  void* stream) {
+  return guarded([&] {
+    const unsigned used = kvbridge::launch_attention_partials(to_shape(s), to_input(in), partitions,
+                                                              scratch, as_stream(stream));
+    if (partitions_used != nullptr) *partitions_used = used;
+  });
+}
+
+int kvb_merge_attention_ex(const kvb_shape* s, const float* scratch, unsigned partitions, float* m,
+                           float* l, float* n, void* out_f16, void* stream) {
+  return guarded([&] {
+    kvbridge::merge_attention_ex(to_shape(s), scratch, partitions, m, l, n, out_f16,
+                                 as_stream(stream));
+  });
+}
+
+const char* kvb_batch_shape_error(const kvb_batch_shape* s) {
+  if (s == nullptr) return "shape pointer is null";
+  return kvbridge::batch_shape_error(to_batch_shape(s));
+}
+
+int kvb_batch_workspace_bytes(const kvb_batch_shape* s, size_t* bytes) {
+  return guarded([&] {
+    const size_t v = kvbridge::batch_workspace_bytes(to_batch_shape(s));
+    if (bytes == nullptr) throw std::invalid_argument("output pointer is null");
+    *bytes = v;
+  });
+}
+
+int kvb_launch_attention_batched(const kvb_batch_shape* s, const kvb_batch_input* in,
+                                 void* workspace, size_t workspace_bytes, float* m, float* l,
+                                 float* n, void* out_f16, void* stream) {
+  return guarded([&] {
+    kvbridge::launch_attention_batched(to_batch_shape(s), to_batch_input(in), workspace,
+                                       workspace_bytes, m, l, n, out_f16, as_stream(stream));
+  });
+}
+
+int kvb_merge_attention_shards(unsigned shards, unsigned row_heads, unsigned dim,
+                               const float* m_parts, const float* l_parts, const float* n_parts,
+                               float* m, float* l, float* n, void* out_f16, void* stream) {
+  return guarded([&] {
+    kvbridge::merge_attention_shards(shards, row_heads, dim, m_parts, l_parts, n_parts, m, l, n,
+                                     out_f16, as_stream(stream));
+  });
+}
+
+int kvb_read_device_status(int* status) { return int(kvbridge::read_device_status(status)); }
+
+uint32_t kvb_schedule_cta_of(uint64_t stage, uint64_t total, uint32_t ctas) {
+  if (total == 0 || ctas == 0 || stage >= total) return 0;
+  return kvb::cta_of_stage(stage, total, ctas);
+}
+
+}  // extern "C"

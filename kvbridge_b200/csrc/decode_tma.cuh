@@ -1,0 +1,714 @@
+#pragma once
+// Split-K partial kernel for paged INT8 KV on sm_100a.
+//
+// Computes, for every piece of the split-K schedule (kvb_schedule.h), the
+// partial (m, l, n[dim]) of reference src/attention_shared.cu:42-209 /
+// include/kvbridge/partial_attention_mma.cuh:153-477: scores
+// s = scale * kscale * q.k over the visible tokens of the piece, m = max s,
+// l = sum exp(s - m), n = sum exp(s - m) * vscale * v.
+//
+// Structure (one CTA = 4 consumer warps + 1 producer warp):
+//  * Data movement: the producer warp walks the CTA's pieces, looks the pages
+//    of each 64-token stage up in the page table (a 64-entry register window
+//    prefetched ahead), and issues one bulk asynchronous copy per (page, K|V|
+//    kscale|vscale) into a STAGES-deep shared-memory ring guarded by
+//    mbarriers. K and V are consumed exactly as stored (int8); nothing is
+//    converted before it reaches shared memory.
+//  * Math: each consumer warp owns whole stages (stage g goes to warp g % 4)
+//    and keeps its own online-softmax state. QK and PV both run "swap-AB" on
+//    the f16 m16n8k16 tensor-core MMA so that the query rows of the KV head
+//    (rows * group <= 8 * NT) sit in the narrow N dimension:
+//        S^T[token][qrow] = K[token][d] . Q^T[d][qrow]   (M = 16 tokens)
+//        O^T[d][qrow]     = V[d][token] . P[token][qrow]  (M = 16 dims)
+//    int8 codes are widened to f16 exactly in registers; per-token kscale
+//    multiplies the fp32 scores and per-token vscale rides on P, as in the
+//    reference MMA kernel. The QK accumulator fragments become the PV B
+//    operand through movmatrix (8x8 transposes), never touching shared
+//    memory, because the token order of the QK rows is chosen so that the
+//    PV A operand (V rows, token-contiguous) loads as one 16-byte word per row.
+//  * Precision: Q is scaled per row by a power of two into f16 range and
+//    split into f16 hi + lo parts; the lo MMA is skipped for warps whose Q is
+//    exactly f16 (BASELINE queries are fp16). P is stored relative to a
+//    running power-of-two vscale exponent, so any finite vscale fits f16.
+//  * Pieces end with an in-CTA log-sum-exp combine of the four warps'
+//    states and one (m, l, n) write per query row.
+#include "kvb_device.cuh"
+#include "kvb_schedule.h"
+
+namespace kvb {
+
+struct DecodeParams {
+  const float* q;
+  const int64_t* q_positions;  // single sequence: [rows]; batched: unused
+  const int64_t* k_positions;  // single sequence: [tokens]; batched: unused
+  const uint32_t* table;       // page table (single) or block table (batched)
+  const int8_t* k;
+  const int8_t* v;
+  const float* k_scales;
+  const float* v_scales;
+  const uint32_t* seq_lens;  // batched: [batch]; nullptr for a single sequence
+  float* part;               // partial output
+  uint32_t batch, rows, q_heads, kv_heads, group, qr;
+  uint32_t page_tokens, log2_page, pages, table_stride;
+  uint32_t begin, end;    // single sequence token interval
+  uint32_t seg_stages;    // single sequence: stages per segment
+  uint32_t split_stride;  // single sequence: scratch splits per row-head
+  uint32_t max_tokens;    // batched: clamp for seq_lens
+  uint32_t ctas;
+  uint64_t total_stages;  // single sequence only (batched computes it)
+  float score_scale;
+};
+
+constexpr int kConsumerWarps = 4;
+constexpr int kProducerWarp = kConsumerWarps;
+constexpr int kDecodeThreads = 32 * (kConsumerWarps + 1);
+constexpr int kStatusBadPage = 4;
+constexpr int kStatusSeqLenClamped = 5;
+
+template <int D>
+struct StageLayout {
+  static constexpr uint32_t kK = 0;
+  static constexpr uint32_t kV = 64u * D;
+  static constexpr uint32_t kKs = 128u * D + 128u;
+  static constexpr uint32_t kVs = kKs + 256u;
+  static constexpr uint32_t kBytes = kVs + 256u;
+};
+
+// V page pitch inside a stage: pages of page_tokens < 64 get a 2*page_tokens
+// byte gap so the four 16-token groups of a warp land on distinct banks.
+__device__ __forceinline__ uint32_t v_page_pitch(uint32_t dim, uint32_t page_tokens) {
+  return dim * page_tokens + (page_tokens < 64 ? 2u * page_tokens : 0u);
+}
+
+template <int D, int NT, int STAGES>
+struct DecodeSmem {
+  static constexpr uint32_t kRing = STAGES * StageLayout<D>::kBytes;
+  static constexpr uint32_t kCols = 8 * NT;
+  static constexpr uint32_t kPitch = D + 4;  // floats; breaks bank aliasing of columns
+  static constexpr uint32_t kCombine = kConsumerWarps * kCols * kPitch * 4;
+  static constexpr uint32_t kStats = kConsumerWarps * kCols * 2 * 4;
+  static constexpr uint32_t kBarriers = 2 * STAGES * 8;
+  static constexpr uint32_t kOffCombine = kRing;
+  static constexpr uint32_t kOffStats = kOffCombine + kCombine;
+  static constexpr uint32_t kOffBar = kOffStats + kStats;
+  static constexpr uint32_t kOffAbort = kOffBar + kBarriers;
+  static constexpr uint32_t kBytes = kOffAbort + 16;
+};
+
+// ---------------------------------------------------------------------------
+// Piece walking (identical in producer and consumers).
+
+struct Piece {
+  uint32_t b, h;       // sequence and KV head
+  uint32_t j0, j1;     // stage range within the segment
+  uint32_t lo, hi;     // attended token interval of the sequence
+  uint32_t slot;       // partial slot (see write_partial)
+};
+
+__device__ __forceinline__ uint32_t clamped_len(const DecodeParams& p, uint32_t b) {
+  const uint32_t len = p.seq_lens[b];
+  return len > p.max_tokens ? p.max_tokens : len;
+}
+
+// Warp-cooperative: total stages of a batched call.
+__device__ __forceinline__ uint64_t batched_total(const DecodeParams& p) {
+  const uint32_t lane = threadIdx.x & 31;
+  uint64_t total = 0;
+  for (uint32_t base = 0; base < p.batch; base += 32) {
+    const uint32_t b = base + lane;
+    const uint32_t t = b < p.batch ? stages_of_range(0, clamped_len(p, b)) : 0;
+    uint64_t s = t;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    total += s;
+  }
+  return total * p.kv_heads;
+}
+
+// Warp-cooperative: sequence b whose segments hold global stage x, and the
+// number of stages of all earlier sequences (per KV head).
+__device__ __forceinline__ void batched_locate(const DecodeParams& p, uint64_t x, uint32_t& b_out,
+                                               uint64_t& pref_out) {
+  const uint32_t lane = threadIdx.x & 31;
+  uint64_t pref = 0;
+  for (uint32_t base = 0; base < p.batch; base += 32) {
+    const uint32_t b = base + lane;
+    const uint64_t t = b < p.batch ? stages_of_range(0, clamped_len(p, b)) : 0;
+    uint64_t incl = t;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint64_t y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= uint32_t(o)) incl += y;
+    }
+    const uint32_t hit = __ballot_sync(0xffffffffu, b < p.batch && (pref + incl) * p.kv_heads > x);
+    if (hit) {
+      const uint32_t l = __ffs(hit) - 1;
+      b_out = base + l;
+      const uint64_t incl_l = __shfl_sync(0xffffffffu, incl, l);
+      const uint64_t t_l = __shfl_sync(0xffffffffu, t, l);
+      pref_out = pref + incl_l - t_l;
+      return;
+    }
+    pref += __shfl_sync(0xffffffffu, incl, 31);
+  }
+  b_out = p.batch;  // unreachable for x < total
+  pref_out = pref;
+}
+
+// The piece starting at global stage x of CTA c whose range ends at x_end.
+__device__ __forceinline__ Piece locate_piece(const DecodeParams& p, uint64_t x, uint64_t x_end,
+                                              uint64_t total, uint32_t c) {
+  Piece pc;
+  uint64_t seg_base;
+  uint32_t seg_len;
+  if (p.seq_lens == nullptr) {
+    pc.b = 0;
+    pc.lo = p.begin;
+    pc.hi = p.end;
+    seg_base = 0;
+    seg_len = p.seg_stages;
+  } else {
+    uint64_t pref;
+    batched_locate(p, x, pc.b, pref);
+    pc.lo = 0;
+    pc.hi = clamped_len(p, pc.b);
+    seg_base = pref * p.kv_heads;
+    seg_len = stages_of_range(0, pc.hi);
+  }
+  pc.h = static_cast<uint32_t>((x - seg_base) / seg_len);
+  const uint64_t seg_off = seg_base + uint64_t(pc.h) * seg_len;
+  pc.j0 = static_cast<uint32_t>(x - seg_off);
+  const uint64_t rem = x_end - seg_off;
+  pc.j1 = rem < seg_len ? static_cast<uint32_t>(rem) : seg_len;
+  if (p.seq_lens == nullptr)
+    pc.slot = c - cta_of_stage(seg_off, total, p.ctas);
+  else
+    pc.slot = c + pc.b * p.kv_heads + pc.h;
+  return pc;
+}
+
+__device__ __forceinline__ uint64_t piece_end_stage(const DecodeParams& p, const Piece& pc,
+                                                    uint64_t x) {
+  return x + (pc.j1 - pc.j0);
+}
+
+// ---------------------------------------------------------------------------
+// Producer: one warp, bulk copies of whole pages.
+
+template <int D, int STAGES>
+__device__ void produce(const DecodeParams& p, uint8_t* ring, uint64_t* full, uint64_t* empty,
+                        volatile int* abort_flag, uint64_t x0, uint64_t x1, uint64_t total) {
+  const uint32_t lane = threadIdx.x & 31;
+  const uint64_t policy = l2_evict_first_policy();
+  const uint32_t P = p.page_tokens;
+  const uint32_t page_bytes = 2u * P * D + 8u * P;
+  const uint32_t vpitch = v_page_pitch(D, P);
+  uint32_t g = 0;  // stages issued so far (CTA stage sequence number)
+  bool failed = false;
+  for (uint64_t x = x0; x < x1 && !failed;) {
+    const Piece pc = locate_piece(p, x, x1, total, blockIdx.x);
+    const uint32_t first_stage = pc.lo / kStageTokens;
+    const uint32_t tok_lo = max(pc.lo, (first_stage + pc.j0) * kStageTokens);
+    const uint32_t tok_hi = min(pc.hi, (first_stage + pc.j1) * kStageTokens);
+    const uint32_t page_last = (tok_hi - 1) >> p.log2_page;
+    const uint32_t* trow =
+        p.seq_lens == nullptr ? p.table : p.table + size_t(pc.b) * p.table_stride;
+    // Register window of page-table entries: cur = [wb, wb+32), nxt = [wb+32, wb+64).
+    uint32_t wb = tok_lo >> p.log2_page;
+    uint32_t cur = (wb + lane <= page_last) ? __ldg(trow + wb + lane) : 0u;
+    uint32_t nxt = (wb + 32 + lane <= page_last) ? __ldg(trow + wb + 32 + lane) : 0u;
+    for (uint32_t j = pc.j0; j < pc.j1; ++j) {
+      const uint32_t slot = g % STAGES;
+      const uint32_t use = g / STAGES;
+      if (!mbar_wait_bounded(&empty[slot], (use & 1u) ^ 1u, abort_flag)) {
+        failed = true;
+        if (lane == 0) {
+          *abort_flag = 1;
+          atomicMax(&g_kvb_status, kStatusEmptyWaitTimeout);
+        }
+        break;
+      }
+      const uint32_t tb = (first_stage + j) * kStageTokens;
+      const uint32_t vlo = max(tb, pc.lo), vhi = min(tb + kStageTokens, pc.hi);
+      const uint32_t p0 = vlo >> p.log2_page, p1 = (vhi - 1) >> p.log2_page;
+      while (p0 >= wb + 32) {
+        cur = nxt;
+        wb += 32;
+        nxt = (wb + 32 + lane <= page_last) ? __ldg(trow + wb + 32 + lane) : 0u;
+      }
+      const uint32_t npages = p1 - p0 + 1;
+      const uint32_t idx = (lane < npages) ? (p0 + lane - wb) : 0u;
+      const uint32_t from_cur = __shfl_sync(0xffffffffu, cur, idx & 31u);
+      const uint32_t from_nxt = __shfl_sync(0xffffffffu, nxt, idx & 31u);
+      const uint32_t phys = idx < 32 ? from_cur : from_nxt;
+      const bool mine = lane < npages;
+      const bool ok = mine && phys < p.pages;
+      const uint32_t okmask = __ballot_sync(0xffffffffu, ok);
+      if (__ballot_sync(0xffffffffu, mine && !ok) && lane == 0)
+        atomicMax(&g_kvb_status, kStatusBadPage);
+      if (lane == 0) mbar_arrive_expect_tx(&full[slot], __popc(okmask) * page_bytes);
+      __syncwarp();
+      if (ok) {
+        uint8_t* st = ring + size_t(slot) * StageLayout<D>::kBytes;
+        const uint32_t in_stage = (p0 + lane) * P - tb;  // first token of the page in the stage
+        const size_t unit = size_t(phys) * p.kv_heads + pc.h;  // (page, kv head)
+        bulk_copy_g2s(st + StageLayout<D>::kK + in_stage * D, p.k + unit * P * D, P * D,
+                      &full[slot], policy);
+        bulk_copy_g2s(st + StageLayout<D>::kV + (in_stage >> p.log2_page) * vpitch,
+                      p.v + unit * D * P, D * P, &full[slot], policy);
+        bulk_copy_g2s(st + StageLayout<D>::kKs + in_stage * 4, p.k_scales + unit * P, 4 * P,
+                      &full[slot], policy);
+        bulk_copy_g2s(st + StageLayout<D>::kVs + in_stage * 4, p.v_scales + unit * P, 4 * P,
+                      &full[slot], policy);
+      }
+      ++g;
+    }
+    x = piece_end_stage(p, pc, x);
+  }
+  // Drain: every copy this warp issued (stages 0..g-1) must land before the
+  // CTA can exit; only the last STAGES of them can still be in flight.
+  const uint32_t first = g > STAGES ? g - STAGES : 0u;
+  for (uint32_t s = first; s < g; ++s) {
+    if (!mbar_wait_bounded(&full[s % STAGES], (s / STAGES) & 1u, abort_flag)) {
+      if (lane == 0) atomicMax(&g_kvb_status, kStatusDrainTimeout);
+      break;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Consumers.
+
+template <int D, int NT>
+struct WarpState {
+  float acc[D / 16][NT][4];  // O^T fragments: rows d, columns = query rows
+  float m[NT][2];            // running max (log2 units) of columns 2*tig+e
+  float l[NT][2];            // thread-partial denominators
+  int ev;                    // running vscale exponent of acc
+};
+
+// Per-piece query operands of one warp.
+template <int D, int NT>
+struct QueryFrags {
+  uint32_t hi[NT][D / 16][2];
+  uint32_t lo[NT][D / 16][2];
+  float cf[NT][2];       // score factor of the thread's C columns (log2 units)
+  int64_t qpos[NT][2];   // query position of the thread's C columns
+  bool use_lo;
+};
+
+template <int D, int NT>
+__device__ __forceinline__ void load_query(const DecodeParams& p, const Piece& pc,
+                                           QueryFrags<D, NT>& qf) {
+  const uint32_t lane = threadIdx.x & 31, grp = lane >> 2, tig = lane & 3;
+  bool any_lo = false;
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    const uint32_t col = 8 * nt + grp;
+    const bool valid = col < p.qr;
+    const uint32_t r = valid ? col / p.group : 0, g = valid ? col % p.group : 0;
+    const uint32_t row = p.seq_lens == nullptr ? r : pc.b;
+    const float* qrow = p.q + (size_t(row) * p.q_heads + size_t(pc.h) * p.group + g) * D;
+    float vals[D / 64][16];
+    float amax = 0.f;
+#pragma unroll
+    for (int c = 0; c < D / 64; ++c) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float4 f = valid ? __ldg(reinterpret_cast<const float4*>(qrow + 64 * c + 16 * tig) + i)
+                         : make_float4(0.f, 0.f, 0.f, 0.f);
+        vals[c][4 * i + 0] = f.x;
+        vals[c][4 * i + 1] = f.y;
+        vals[c][4 * i + 2] = f.z;
+        vals[c][4 * i + 3] = f.w;
+        amax = fmaxf(amax, fmaxf(fmaxf(fabsf(f.x), fabsf(f.y)), fmaxf(fabsf(f.z), fabsf(f.w))));
+      }
+    }
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+    // Power-of-two shift putting max|q| in [2^14, 2^15): exact rescaling that
+    // keeps both f16 parts normal and far from overflow.
+    int shift = 0;
+    if (amax > 0.f) {
+      const int e = int((__float_as_uint(amax) >> 23) & 0xffu) - 126;
+      shift = max(-100, min(100, e - 15));
+    }
+    const float down = __uint_as_float(uint32_t(127 - shift) << 23);
+#pragma unroll
+    for (int c = 0; c < D / 64; ++c) {
+#pragma unroll
+      for (int jj = 0; jj < 4; ++jj) {
+        float x[4], h[4], rem[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          x[i] = vals[c][4 * jj + i] * down;
+          h[i] = __half2float(__float2half_rn(x[i]));
+          rem[i] = x[i] - h[i];
+          any_lo |= rem[i] != 0.f;
+        }
+        qf.hi[nt][4 * c + jj][0] = pack_half2(h[0], h[1]);
+        qf.hi[nt][4 * c + jj][1] = pack_half2(h[2], h[3]);
+        qf.lo[nt][4 * c + jj][0] = pack_half2(rem[0], rem[1]);
+        qf.lo[nt][4 * c + jj][1] = pack_half2(rem[2], rem[3]);
+      }
+    }
+    const float cf_b = p.score_scale * kLog2e * __uint_as_float(uint32_t(127 + shift) << 23);
+    // C layout: this thread's columns are 2*tig and 2*tig+1 of the n-tile;
+    // their factor lives in lane 4*column.
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      qf.cf[nt][e] = __shfl_sync(0xffffffffu, cf_b, 4 * (2 * tig + e));
+      const uint32_t ccol = 8 * nt + 2 * tig + e;
+      int64_t qp = INT64_MAX;
+      if (p.seq_lens == nullptr && ccol < p.qr) qp = __ldg(p.q_positions + ccol / p.group);
+      qf.qpos[nt][e] = qp;
+    }
+  }
+  qf.use_lo = __any_sync(0xffffffffu, any_lo);
+}
+
+// One 64-token stage for one warp.
+template <int D, int NT>
+__device__ __forceinline__ void consume_stage(const DecodeParams& p, const uint8_t* st,
+                                              uint32_t tb, uint32_t lo, uint32_t hi,
+                                              bool all_visible, const QueryFrags<D, NT>& qf,
+                                              WarpState<D, NT>& ws) {
+  const uint32_t lane = threadIdx.x & 31, grp = lane >> 2, tig = lane & 3;
+  const uint8_t* sk = st + StageLayout<D>::kK;
+  const uint8_t* sv = st + StageLayout<D>::kV;
+  const float* sks = reinterpret_cast<const float*>(st + StageLayout<D>::kKs);
+  const float* svs = reinterpret_cast<const float*>(st + StageLayout<D>::kVs);
+
+  // ---- S^T = K Q^T. QK row r of m-tile s holds token
+  //      16*((r&7)>>1) + 4*s + 2*(r>>3) + (r&1), so a thread's rows grp and
+  //      grp+8 are tokens t0 and t0+2.
+  float sc[4][NT][4];
+#pragma unroll
+  for (int s = 0; s < 4; ++s) {
+    const uint32_t t0 = 16 * (grp >> 1) + 4 * s + (grp & 1), t1 = t0 + 2;
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) sc[s][nt][i] = 0.f;
+#pragma unroll
+    for (int c = 0; c < D / 64; ++c) {
+      const uint4 ra = *reinterpret_cast<const uint4*>(sk + t0 * D + 64 * c + 16 * tig);
+      const uint4 rb = *reinterpret_cast<const uint4*>(sk + t1 * D + 64 * c + 16 * tig);
+      const uint32_t wa[4] = {ra.x, ra.y, ra.z, ra.w};
+      const uint32_t wb[4] = {rb.x, rb.y, rb.z, rb.w};
+#pragma unroll
+      for (int jj = 0; jj < 4; ++jj) {
+        uint32_t a0, a1, a2, a3;
+        int8x4_to_f16x4(wa[jj], a0, a2);
+        int8x4_to_f16x4(wb[jj], a1, a3);
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          mma_16816(sc[s][nt], a0, a1, a2, a3, qf.hi[nt][4 * c + jj][0], qf.hi[nt][4 * c + jj][1]);
+          if (qf.use_lo)
+            mma_16816(sc[s][nt], a0, a1, a2, a3, qf.lo[nt][4 * c + jj][0],
+                      qf.lo[nt][4 * c + jj][1]);
+        }
+      }
+    }
+  }
+
+  // ---- scores in log2 units, masking.
+  const bool full = all_visible && tb >= lo && tb + kStageTokens <= hi;
+#pragma unroll
+  for (int s = 0; s < 4; ++s) {
+    const uint32_t t0 = 16 * (grp >> 1) + 4 * s + (grp & 1), t1 = t0 + 2;
+    const float k0 = sks[t0], k1 = sks[t1];
+    bool in0 = true, in1 = true;
+    int64_t kp0 = 0, kp1 = 0;
+    if (!full) {
+      in0 = tb + t0 >= lo && tb + t0 < hi;
+      in1 = tb + t1 >= lo && tb + t1 < hi;
+      if (!all_visible) {
+        kp0 = in0 ? __ldg(p.k_positions + tb + t0) : 0;
+        kp1 = in1 ? __ldg(p.k_positions + tb + t1) : 0;
+      }
+    }
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        float x0 = sc[s][nt][e] * k0 * qf.cf[nt][e];
+        float x1 = sc[s][nt][2 + e] * k1 * qf.cf[nt][e];
+        if (!full) {
+          const bool v0 = in0 && (all_visible || kp0 <= qf.qpos[nt][e]);
+          const bool v1 = in1 && (all_visible || kp1 <= qf.qpos[nt][e]);
+          x0 = v0 ? x0 : -INFINITY;
+          x1 = v1 ? x1 : -INFINITY;
+        }
+        sc[s][nt][e] = x0;
+        sc[s][nt][2 + e] = x1;
+      }
+  }
+
+  // ---- vscale exponent of this stage (warp-uniform).
+  float vs_lane[2];
+  {
+    float vmax = 0.f;
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const uint32_t t = lane + 32 * i;
+      const bool in = full || (tb + t >= lo && tb + t < hi);
+      vs_lane[i] = in ? svs[t] : 0.f;
+      vmax = fmaxf(vmax, fabsf(vs_lane[i]));
+    }
+    vmax = warp_max(vmax);
+    int ev_stage = -100;
+    if (vmax > 0.f) ev_stage = max(-100, int((__float_as_uint(vmax) >> 23) & 0xffu) - 141);
+    const int ev_new = max(ws.ev, ev_stage);
+    const float ev_fac = __uint_as_float(uint32_t(127 + max(ws.ev - ev_new, -126)) << 23);
+    const float vmul = __uint_as_float(uint32_t(127 - ev_new) << 23);
+    ws.ev = ev_new;
+    vs_lane[0] *= vmul;
+    vs_lane[1] *= vmul;
+
+    // ---- online softmax update per column.
+    bool rescale = false;
+    float fac[NT][2];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        float cm = -INFINITY;
+#pragma unroll
+        for (int s = 0; s < 4; ++s) cm = fmaxf(cm, fmaxf(sc[s][nt][e], sc[s][nt][2 + e]));
+        cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 4));
+        cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 8));
+        cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 16));
+        const float mold = ws.m[nt][e];
+        const float mnew = fmaxf(mold, cm);
+        const float alpha = mnew == -INFINITY ? 1.f : fast_exp2(mold - mnew);
+        ws.m[nt][e] = mnew;
+        const float msub = mnew == -INFINITY ? 0.f : mnew;
+        float lsum = 0.f;
+#pragma unroll
+        for (int s = 0; s < 4; ++s) {
+          const float w0 = fast_exp2(sc[s][nt][e] - msub);
+          const float w1 = fast_exp2(sc[s][nt][2 + e] - msub);
+          sc[s][nt][e] = w0;
+          sc[s][nt][2 + e] = w1;
+          lsum += w0 + w1;
+        }
+        ws.l[nt][e] = ws.l[nt][e] * alpha + lsum;
+        fac[nt][e] = alpha * ev_fac;
+        rescale |= fac[nt][e] != 1.f;
+      }
+    if (__any_sync(0xffffffffu, rescale)) {
+#pragma unroll
+      for (int md = 0; md < D / 16; ++md)
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          ws.acc[md][nt][0] *= fac[nt][0];
+          ws.acc[md][nt][1] *= fac[nt][1];
+          ws.acc[md][nt][2] *= fac[nt][0];
+          ws.acc[md][nt][3] *= fac[nt][1];
+        }
+    }
+  }
+
+  // ---- P = w * vscale * 2^-ev as f16, transposed into the PV B operand.
+  uint32_t pb[4][NT][2];
+#pragma unroll
+  for (int s = 0; s < 4; ++s) {
+    const uint32_t t0 = 16 * (grp >> 1) + 4 * s + (grp & 1), t1 = t0 + 2;
+    // vscale of token t sits in lane t % 32, register t / 32.
+    const float v0a = __shfl_sync(0xffffffffu, vs_lane[0], t0 & 31);
+    const float v0b = __shfl_sync(0xffffffffu, vs_lane[1], t0 & 31);
+    const float v1a = __shfl_sync(0xffffffffu, vs_lane[0], t1 & 31);
+    const float v1b = __shfl_sync(0xffffffffu, vs_lane[1], t1 & 31);
+    const float vm0 = t0 < 32 ? v0a : v0b;
+    const float vm1 = t1 < 32 ? v1a : v1b;
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      const uint32_t r0 = pack_half2(sc[s][nt][0] * vm0, sc[s][nt][1] * vm0);
+      const uint32_t r1 = pack_half2(sc[s][nt][2] * vm1, sc[s][nt][3] * vm1);
+      pb[s][nt][0] = transpose_8x8_b16(r0);
+      pb[s][nt][1] = transpose_8x8_b16(r1);
+    }
+  }
+
+  // ---- O^T += V P. PV k-step s pairs k = 2*tig+{0,1} with tokens
+  //      16*tig+4*s+{0,1} and k = 2*tig+8+{0,1} with tokens 16*tig+4*s+{2,3}:
+  //      word s of the thread's 16-byte slice of V row d.
+  const uint32_t P = p.page_tokens;
+  const uint32_t vpitch = v_page_pitch(D, P);
+  const uint8_t* vslice = sv + ((16 * tig) >> p.log2_page) * vpitch + ((16 * tig) & (P - 1));
+#pragma unroll
+  for (int md = 0; md < D / 16; ++md) {
+    const uint32_t d0 = 16 * md + grp, d1 = d0 + 8;
+    const uint4 va = *reinterpret_cast<const uint4*>(vslice + d0 * P);
+    const uint4 vb = *reinterpret_cast<const uint4*>(vslice + d1 * P);
+    const uint32_t wa[4] = {va.x, va.y, va.z, va.w};
+    const uint32_t wb[4] = {vb.x, vb.y, vb.z, vb.w};
+#pragma unroll
+    for (int s = 0; s < 4; ++s) {
+      uint32_t a0, a1, a2, a3;
+      int8x4_to_f16x4(wa[s], a0, a2);
+      int8x4_to_f16x4(wb[s], a1, a3);
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+        mma_16816(ws.acc[md][nt], a0, a1, a2, a3, pb[s][nt][0], pb[s][nt][1]);
+    }
+  }
+}
+
+template <int D, int NT, int STAGES>
+__global__ void __launch_bounds__(kDecodeThreads, 2) decode_partial_kernel(DecodeParams p) {
+  using L = DecodeSmem<D, NT, STAGES>;
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint8_t* ring = smem;
+  float* combine = reinterpret_cast<float*>(smem + L::kOffCombine);
+  float* stats = reinterpret_cast<float*>(smem + L::kOffStats);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kOffBar);
+  uint64_t* empty = full + STAGES;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kOffAbort);
+
+  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  // Inputs may be produced by the preceding kernel on the stream.
+  grid_dependency_wait();
+
+  const uint64_t total = p.seq_lens == nullptr ? p.total_stages : batched_total(p);
+  const uint64_t x0 = cta_stage_begin(blockIdx.x, total, p.ctas);
+  const uint64_t x1 = cta_stage_begin(blockIdx.x + 1, total, p.ctas);
+
+  if (warp == kProducerWarp) {
+    produce<D, STAGES>(p, ring, full, empty, abort_flag, x0, x1, total);
+    return;
+  }
+
+  const uint32_t grp = lane >> 2, tig = lane & 3;
+  uint32_t g_base = 0;  // CTA stage sequence number of the piece's first stage
+  for (uint64_t x = x0; x < x1;) {
+    const Piece pc = locate_piece(p, x, x1, total, blockIdx.x);
+    const uint32_t first_stage = pc.lo / kStageTokens;
+    QueryFrags<D, NT> qf;
+    load_query<D, NT>(p, pc, qf);
+    // Causality: k_positions is nondecreasing, so the piece is fully visible
+    // when its last token is visible to every query row.
+    bool all_visible = true;
+    if (p.seq_lens == nullptr) {
+      const uint32_t last = min(pc.hi, (first_stage + pc.j1) * kStageTokens) - 1;
+      const int64_t kp = __ldg(p.k_positions + last);
+      const bool row_ok = lane >= p.rows || kp <= __ldg(p.q_positions + lane);
+      all_visible = __all_sync(0xffffffffu, row_ok);
+    }
+    WarpState<D, NT> ws;
+#pragma unroll
+    for (int md = 0; md < D / 16; ++md)
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) ws.acc[md][nt][i] = 0.f;
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      ws.m[nt][0] = ws.m[nt][1] = -INFINITY;
+      ws.l[nt][0] = ws.l[nt][1] = 0.f;
+    }
+    ws.ev = -100;
+
+    const uint32_t n = pc.j1 - pc.j0;
+    const uint32_t first = (warp + kConsumerWarps - g_base % kConsumerWarps) % kConsumerWarps;
+    for (uint32_t i = first; i < n; i += kConsumerWarps) {
+      const uint32_t g = g_base + i;
+      const uint32_t slot = g % STAGES;
+      if (!mbar_wait_bounded(&full[slot], (g / STAGES) & 1u, abort_flag)) {
+        if (lane == 0) {
+          *abort_flag = 1;
+          atomicMax(&g_kvb_status, kStatusFullWaitTimeout);
+        }
+      }
+      const uint32_t tb = (first_stage + pc.j0 + i) * kStageTokens;
+      consume_stage<D, NT>(p, ring + size_t(slot) * StageLayout<D>::kBytes, tb, pc.lo, pc.hi,
+                           all_visible, qf, ws);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[slot]);
+    }
+    g_base += n;
+
+    // ---- flush this warp's state.
+    const float ev_scale = __uint_as_float(uint32_t(127 + ws.ev) << 23);
+    float* cw = combine + size_t(warp) * L::kCols * L::kPitch;
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        float lsum = ws.l[nt][e];
+        lsum += __shfl_xor_sync(0xffffffffu, lsum, 4);
+        lsum += __shfl_xor_sync(0xffffffffu, lsum, 8);
+        lsum += __shfl_xor_sync(0xffffffffu, lsum, 16);
+        const uint32_t col = 8 * nt + 2 * tig + e;
+        if (grp == 0) {
+          stats[(warp * L::kCols + col) * 2 + 0] = ws.m[nt][e];
+          stats[(warp * L::kCols + col) * 2 + 1] = lsum;
+        }
+#pragma unroll
+        for (int md = 0; md < D / 16; ++md) {
+          cw[col * L::kPitch + 16 * md + grp] = ws.acc[md][nt][e] * ev_scale;
+          cw[col * L::kPitch + 16 * md + grp + 8] = ws.acc[md][nt][2 + e] * ev_scale;
+        }
+      }
+    if (x + n >= x1) grid_launch_dependents();
+    named_barrier(1, 32 * kConsumerWarps);
+
+    // ---- combine the four warps and write one partial per query row.
+    constexpr uint32_t kTpc = 32 * kConsumerWarps / L::kCols;  // threads per column
+    constexpr uint32_t kDpt = D / kTpc;                          // dims per thread
+    const uint32_t col = threadIdx.x / kTpc, part = threadIdx.x % kTpc;
+    if (col < p.qr) {
+      float mw[kConsumerWarps], M = -INFINITY;
+#pragma unroll
+      for (int w = 0; w < kConsumerWarps; ++w) {
+        mw[w] = stats[(w * L::kCols + col) * 2 + 0];
+        M = fmaxf(M, mw[w]);
+      }
+      float ew[kConsumerWarps], Lsum = 0.f;
+#pragma unroll
+      for (int w = 0; w < kConsumerWarps; ++w) {
+        ew[w] = (M == -INFINITY || mw[w] == -INFINITY) ? 0.f : fast_exp2(mw[w] - M);
+        Lsum += ew[w] * stats[(w * L::kCols + col) * 2 + 1];
+      }
+      size_t base;
+      if (p.seq_lens == nullptr) {
+        const uint32_t r = col / p.group, gq = col % p.group;
+        const size_t rh = size_t(r) * p.q_heads + size_t(pc.h) * p.group + gq;
+        base = (rh * p.split_stride + pc.slot) * (D + 2);
+      } else {
+        base = (size_t(pc.slot) * p.qr + col) * (D + 2);
+      }
+      float* out = p.part + base;
+      if (part == 0) {
+        out[0] = M == -INFINITY ? -INFINITY : M * kLn2;
+        out[1] = Lsum;
+      }
+#pragma unroll
+      for (uint32_t i = 0; i < kDpt; i += 2) {
+        const uint32_t d = part * kDpt + i;
+        float2 v = make_float2(0.f, 0.f);
+#pragma unroll
+        for (int w = 0; w < kConsumerWarps; ++w) {
+          const float* src = combine + (size_t(w) * L::kCols + col) * L::kPitch + d;
+          v.x += ew[w] * src[0];
+          v.y += ew[w] * src[1];
+        }
+        *reinterpret_cast<float2*>(out + 2 + d) = v;
+      }
+    }
+    named_barrier(1, 32 * kConsumerWarps);
+    x += n;
+  }
+}
+
+}  // namespace kvb

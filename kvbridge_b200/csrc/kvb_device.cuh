@@ -1,0 +1,175 @@
+#pragma once
+// sm_100a device helpers for the decode-attention kernels: mbarrier
+// pipelines, bulk (TMA) global->shared copies, warp-level f16 tensor-core
+// MMA, fragment transposition and bounded waits. Everything is inline PTX of
+// documented instructions; nothing here restates a CUDA math-library routine.
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <cstdint>
+
+namespace kvb {
+
+// Status codes written to the library's device status word.
+enum : int {
+  kStatusOk = 0,
+  kStatusFullWaitTimeout = 1,   // consumer gave up waiting for a stage
+  kStatusEmptyWaitTimeout = 2,  // producer gave up waiting for a free stage
+  kStatusDrainTimeout = 3,      // copies still in flight at exit
+};
+
+// Device status word of this module (0 = ok; otherwise the largest code any
+// kernel reported since the host last read it). All kernels live in one
+// translation unit, so this is the module's single definition.
+__device__ int g_kvb_status;
+
+// Upper bound of any single pipeline wait. A correct pipeline never waits
+// more than a few microseconds; the bound only keeps a broken one from
+// holding the GPU.
+constexpr unsigned long long kWaitLimitNs = 2000000000ull;
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count)
+               : "memory");
+}
+
+__device__ __forceinline__ void fence_barrier_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+// Wait for phase `parity` of `bar` to complete, giving up after kWaitLimitNs.
+// Returns false on timeout. `abort_flag` (shared memory) short-circuits every
+// later wait of the CTA once one wait has failed.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity,
+                                                  volatile int* abort_flag) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long start = global_ns();
+  for (unsigned spin = 1;; ++spin) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((spin & 255u) == 0) {
+      if (*abort_flag) return false;
+      if (global_ns() - start > kWaitLimitNs) return false;
+    }
+  }
+}
+
+// One bulk asynchronous copy global -> shared, completing `bytes` of
+// transaction count on `bar`. Source, destination and size must be multiples
+// of 16 bytes. The L2 policy marks the streamed KV bytes evict-first.
+__device__ __forceinline__ void bulk_copy_g2s(void* dst, const void* src, uint32_t bytes,
+                                              uint64_t* bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint "
+      "[%0], [%1], %2, [%3], %4;" ::"r"(smem_addr(dst)),
+      "l"(src), "r"(bytes), "r"(smem_addr(bar)), "l"(policy)
+      : "memory");
+}
+
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+  uint64_t policy;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
+  return policy;
+}
+
+// Programmatic dependent launch: wait for the preceding grid's memory, and
+// allow the following grid to start its prologue.
+__device__ __forceinline__ void grid_dependency_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void grid_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// Named barrier over `threads` threads (multiple of 32), id 1..15.
+__device__ __forceinline__ void named_barrier(uint32_t id, uint32_t threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+// D += A * B for one m16n8k16 tile, f16 operands, f32 accumulators.
+__device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                          uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// Transpose an 8x8 b16 matrix held one row-pair per lane (lane holds row
+// lane/4, columns 2*(lane%4) and +1) into the same fragment of its transpose.
+__device__ __forceinline__ uint32_t transpose_8x8_b16(uint32_t x) {
+  uint32_t y;
+  asm("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+  return y;
+}
+
+// 2^x on the MUFU unit (ex2.approx, denormal results flushed to zero).
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Exact int8 -> f16 widening of four packed codes. Biasing each byte by 128
+// gives an unsigned u in [0,255]; the f16 bit pattern 0x6400|u is 1024+u
+// exactly, and subtracting 1152 (0x6480) leaves the signed code. Returns the
+// f16x2 pairs (byte0, byte1) in `lo` and (byte2, byte3) in `hi`, lower byte
+// in the lower half.
+__device__ __forceinline__ void int8x4_to_f16x4(uint32_t packed, uint32_t& lo, uint32_t& hi) {
+  const uint32_t biased = packed ^ 0x80808080u;
+  const uint32_t l = __byte_perm(biased, 0x64646464u, 0x4140u);
+  const uint32_t h = __byte_perm(biased, 0x64646464u, 0x4342u);
+  asm("sub.f16x2 %0, %1, %2;" : "=r"(lo) : "r"(l), "r"(0x64806480u));
+  asm("sub.f16x2 %0, %1, %2;" : "=r"(hi) : "r"(h), "r"(0x64806480u));
+}
+
+__device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
+  const __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+__device__ __forceinline__ float warp_max(float x) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, o));
+  return x;
+}
+__device__ __forceinline__ float warp_sum(float x) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+  return x;
+}
+
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+
+}  // namespace kvb

@@ -1,0 +1,172 @@
+#pragma once
+// Log-sum-exp merge of split-K partials (reference src/attention_shared.cu:
+// 295-335): for each (row, head)
+//   M = max over partials with l_p > 0 of m_p
+//   L = sum_p exp(m_p - M) * l_p,   N[d] = sum_p exp(m_p - M) * n_p[d]
+// with m = -inf, l = 0, n = 0 when no partial has l_p > 0. One warp merges
+// one row-head: lanes reduce over partials with shuffles, then each lane
+// accumulates the dims d = lane + 32k. The optional fp16 epilogue writes
+// out = N / L (0 for empty rows).
+//
+// The same kernel serves three partial layouts:
+//   kScratch - the reference scratch layout [rh][split][dim+2]
+//   kBatched - the batched workspace [piece][qrow][dim+2] (kvb_schedule.h)
+//   kShards  - shard-major m/l/n triples from several GPUs
+#include "kvb_device.cuh"
+#include "kvb_schedule.h"
+
+namespace kvb {
+
+enum MergeMode : int { kMergeScratch = 0, kMergeBatched = 1, kMergeShards = 2 };
+
+struct MergeParams {
+  float* part;  // kScratch / kBatched (kScratch may write empty splits)
+  const float* m_parts;  // kShards
+  const float* l_parts;
+  const float* n_parts;
+  float* m;
+  float* l;
+  float* n;
+  __half* out;
+  uint32_t row_heads, dim;
+  uint32_t np;            // kScratch: partials per row-head; kShards: shards
+  uint32_t split_stride;  // kScratch: S of the layout
+  uint32_t fill_empty;    // kScratch: write empty partials into splits [np, S)
+  // kBatched
+  const uint32_t* seq_lens;
+  uint32_t batch, q_heads, kv_heads, group, max_tokens, ctas;
+};
+
+constexpr int kMergeWarps = 8;
+
+// Warp-cooperative prefix of per-sequence stages for the batched layout.
+__device__ __forceinline__ void merge_batched_geometry(const MergeParams& p, uint32_t b,
+                                                       uint64_t& pref, uint64_t& total) {
+  const uint32_t lane = threadIdx.x & 31;
+  uint64_t before = 0, all = 0;
+  for (uint32_t base = 0; base < p.batch; base += 32) {
+    const uint32_t s = base + lane;
+    uint32_t t = 0;
+    if (s < p.batch) {
+      const uint32_t len = min(p.seq_lens[s], p.max_tokens);
+      t = stages_of_range(0, len);
+    }
+    uint64_t x = s < b ? t : 0, y = t;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      x += __shfl_xor_sync(0xffffffffu, x, o);
+      y += __shfl_xor_sync(0xffffffffu, y, o);
+    }
+    before += x;
+    all += y;
+  }
+  pref = before;
+  total = all * p.kv_heads;
+}
+
+template <int MODE>
+__global__ void __launch_bounds__(32 * kMergeWarps) merge_kernel(MergeParams p) {
+  grid_dependency_wait();
+  const uint32_t lane = threadIdx.x & 31;
+  const uint32_t rh = blockIdx.x * kMergeWarps + (threadIdx.x >> 5);
+  if (rh >= p.row_heads) return;
+  const uint32_t D = p.dim;
+
+  const float *mb, *lb, *nb;
+  size_t ms, ls, ns;
+  uint32_t np = p.np;
+  if (MODE == kMergeScratch) {
+    mb = p.part + size_t(rh) * p.split_stride * (D + 2);
+    lb = mb + 1;
+    nb = mb + 2;
+    ms = ls = ns = D + 2;
+  } else if (MODE == kMergeShards) {
+    mb = p.m_parts + rh;
+    lb = p.l_parts + rh;
+    nb = p.n_parts + size_t(rh) * D;
+    ms = ls = p.row_heads;
+    ns = size_t(p.row_heads) * D;
+  } else {
+    const uint32_t b = rh / p.q_heads, hq = rh % p.q_heads;
+    const uint32_t h = hq / p.group, g = hq % p.group;
+    uint64_t pref, total;
+    merge_batched_geometry(p, b, pref, total);
+    const uint32_t len = min(p.seq_lens[b], p.max_tokens);
+    const uint32_t t = stages_of_range(0, len);
+    np = 0;
+    uint32_t c_first = 0;
+    if (t > 0) {
+      const uint64_t seg_off = pref * p.kv_heads + uint64_t(h) * t;
+      c_first = cta_of_stage(seg_off, total, p.ctas);
+      np = cta_of_stage(seg_off + t - 1, total, p.ctas) - c_first + 1;
+    }
+    const uint32_t seg = b * p.kv_heads + h;
+    mb = p.part + (size_t(c_first + seg) * p.group + g) * (D + 2);
+    lb = mb + 1;
+    nb = mb + 2;
+    ms = ls = ns = size_t(p.group) * (D + 2);
+  }
+
+  // Pass 1: global max over partials with l > 0.
+  float M = -INFINITY;
+  for (uint32_t i = lane; i < np; i += 32) {
+    const float li = lb[i * ls];
+    if (li > 0.f) M = fmaxf(M, mb[i * ms]);
+  }
+  M = warp_max(M);
+
+  // Pass 2: weights, denominator and numerators.
+  constexpr int kMaxPerLane = 8;  // dims per lane, dim <= 256
+  float acc[kMaxPerLane];
+#pragma unroll
+  for (int k = 0; k < kMaxPerLane; ++k) acc[k] = 0.f;
+  float L = 0.f;
+  if (M != -INFINITY) {
+    for (uint32_t base = 0; base < np; base += 32) {
+      const uint32_t i = base + lane;
+      float e = 0.f;
+      if (i < np) {
+        const float li = lb[i * ls];
+        if (li > 0.f) {
+          e = expf(mb[i * ms] - M);
+          L += e * li;
+        }
+      }
+      const uint32_t cnt = min(32u, np - base);
+      for (uint32_t j = 0; j < cnt; ++j) {
+        const float ej = __shfl_sync(0xffffffffu, e, j);
+        if (ej == 0.f) continue;
+        const float* src = nb + size_t(base + j) * ns;
+#pragma unroll
+        for (int k = 0; k < kMaxPerLane; ++k) {
+          const uint32_t d = lane + 32 * k;
+          if (d < D) acc[k] = fmaf(ej, src[d], acc[k]);
+        }
+      }
+    }
+    L = warp_sum(L);
+  }
+  if (lane == 0) {
+    p.m[rh] = L > 0.f ? M : -INFINITY;
+    p.l[rh] = L;
+  }
+  const float inv = L > 0.f ? 1.f / L : 0.f;
+#pragma unroll
+  for (int k = 0; k < kMaxPerLane; ++k) {
+    const uint32_t d = lane + 32 * k;
+    if (d < D) {
+      const float v = L > 0.f ? acc[k] : 0.f;
+      p.n[size_t(rh) * D + d] = v;
+      if (p.out != nullptr) p.out[size_t(rh) * D + d] = __float2half_rn(v * inv);
+    }
+  }
+  if (MODE == kMergeScratch && p.fill_empty) {
+    float* row = p.part + size_t(rh) * p.split_stride * (D + 2);
+    for (uint32_t i = np + lane; i < p.split_stride; i += 32) {
+      row[size_t(i) * (D + 2) + 0] = -INFINITY;
+      row[size_t(i) * (D + 2) + 1] = 0.f;
+    }
+  }
+}
+
+}  // namespace kvb

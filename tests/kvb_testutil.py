@@ -1,0 +1,94 @@
+"""Helpers shared by the GPU tests: run the library on a synthetic case and
+compare with the FP64 oracle."""
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+import kvbridge_b200 as kvb
+from kvbridge_b200 import synth
+
+# Acceptance tolerances of this path against the FP64 oracle: max-abs 2e-3
+# and rel-L2 1e-3. They apply to the fp32 n/l the kernels compute, against
+# the unrounded oracle. The fp16 output is held to the same numbers against
+# the oracle rounded to fp16: for |out| >= 4 fp16's own rounding (half an ulp,
+# up to 2^-8 at |out| < 8 and more above) exceeds 2e-3, and the outlier
+# configuration reaches |out| ~ 32.
+MAX_ABS = 2e-3
+REL_L2 = 1e-3
+
+
+def to_device(case: synth.SingleCase, device) -> synth.SingleCase:
+    return synth.SingleCase(
+        case.shape,
+        *(getattr(case, f).to(device) for f in ("q", "q_positions", "k_positions", "page_table", "k", "v", "k_scales", "v_scales")),
+    )
+
+
+def outputs_for(shape: kvb.Shape, device):
+    scratch = torch.full((kvb.scratch_elements(shape),), float("nan"), device=device)
+    rh = kvb.output_scalar_elements(shape)
+    m = torch.full((rh,), float("nan"), device=device)
+    l = torch.full((rh,), float("nan"), device=device)
+    n = torch.full((kvb.output_numerator_elements(shape),), float("nan"), device=device)
+    return scratch, m, l, n
+
+
+def run_single(case: synth.SingleCase, partitions: int = 0, fp16_out: bool = True, api: str = "ex"):
+    """Runs one call; returns dict of host tensors (m, l, n, out, scratch)."""
+    device = case.q.device
+    scratch, m, l, n = outputs_for(case.shape, device)
+    out = torch.full((kvb.output_numerator_elements(case.shape),), float("nan"), device=device,
+                     dtype=torch.float16) if fp16_out else None
+    inp = case.device_input()
+    if api == "ex":
+        kvb.launch_attention_ex(case.shape, inp, scratch, m, l, n, partitions=partitions, out_f16=out)
+    elif api == "ref":
+        kvb.launch_attention(case.shape, inp, scratch, m, l, n)
+    elif api == "mma":
+        kvb.launch_attention_mma(case.shape, inp, scratch, m, l, n)
+    torch.cuda.synchronize()
+    res = {"m": m.cpu(), "l": l.cpu(), "n": n.cpu(), "scratch": scratch}
+    if out is not None:
+        res["out"] = out.cpu()
+    return res
+
+
+def normalized(res, shape) -> np.ndarray:
+    n = res["n"].double().numpy().reshape(shape.rows, shape.q_heads, shape.dim)
+    l = res["l"].double().numpy().reshape(shape.rows, shape.q_heads, 1)
+    return np.where(l > 0, n / np.where(l > 0, l, 1.0), 0.0)
+
+
+def errors(actual: np.ndarray, expected: np.ndarray):
+    diff = actual.astype(np.float64) - expected
+    max_abs = float(np.max(np.abs(diff))) if diff.size else 0.0
+    denom = float(np.linalg.norm(expected))
+    rel_l2 = float(np.linalg.norm(diff) / denom) if denom > 0 else float(np.linalg.norm(diff))
+    return max_abs, rel_l2
+
+
+def check_against_oracle(res, shape, ref, label=""):
+    """Asserts n/l (fp32) and the fp16 output against the oracle; checks the
+    empty-row convention (m=-inf, l=0, n=0) row by row."""
+    vis = ref["visible"]
+    m = res["m"].numpy().reshape(shape.rows, shape.q_heads)
+    l = res["l"].numpy().reshape(shape.rows, shape.q_heads)
+    n = res["n"].numpy().reshape(shape.rows, shape.q_heads, shape.dim)
+    assert np.array_equal(l > 0, vis), f"{label}: visibility differs"
+    assert np.all(np.isneginf(m[~vis])), f"{label}: empty rows must have m=-inf"
+    assert np.all(n[~vis] == 0), f"{label}: empty rows must have n=0"
+    assert np.all(np.isfinite(m[vis])) and np.all(np.isfinite(n)), f"{label}: non-finite output"
+    got = normalized(res, shape)
+    ma, rl = errors(got, ref["normalized"])
+    assert ma <= MAX_ABS and rl <= REL_L2, f"{label}: n/l max_abs={ma:.3e} rel_l2={rl:.3e}"
+    if vis.any():
+        # m is the max logit and l the softmax denominator of the same row.
+        assert np.allclose(m[vis], ref["m"][vis], rtol=1e-5, atol=1e-5), f"{label}: m differs"
+        assert np.allclose(l[vis], ref["l"][vis], rtol=2e-3, atol=0), f"{label}: l differs"
+    if "out" in res:
+        out = res["out"].double().numpy().reshape(shape.rows, shape.q_heads, shape.dim)
+        ref16 = ref["normalized"].astype(np.float16).astype(np.float64)
+        ma16, rl16 = errors(out, ref16)
+        assert ma16 <= MAX_ABS and rl16 <= REL_L2, f"{label}: fp16 out max_abs={ma16:.3e} rel_l2={rl16:.3e}"
+    return ma, rl

@@ -1,0 +1,306 @@
+"""GPU parity of the sm_100a kernels against the FP64 oracle (through the C ABI).
+
+Covers the BASELINE configurations at sizes the oracle finishes in seconds,
+the reference's own GPU self-test cases (examples/attention_bench.cu:156-186:
+identity/reversed pages, partial range, fully masked, empty range, causal
+prefix, three splits with a partial last page) restated at the B200 geometry,
+and the general-geometry kernel (fp32 KV, odd dims, wide groups, unaligned
+buffers, the reference's native rows-8/group-6/dim-256 shape).
+"""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import pytest
+import torch
+
+import kvbridge_b200 as kvb
+import oracle
+from kvbridge_b200 import synth
+from kvb_testutil import MAX_ABS, REL_L2, check_against_oracle, errors, normalized, outputs_for, run_single, to_device
+
+pytestmark = pytest.mark.gpu
+
+
+def make(device, **kw):
+    return synth.make_single(device=device, **kw)
+
+
+@pytest.fixture(autouse=True)
+def _status_clean(cuda_device):
+    kvb.read_device_status()
+    yield
+    assert kvb.read_device_status() == 0, "a kernel reported a bounded-wait timeout or bad page"
+
+
+def test_cfg1_eight_partitions(cuda_device):
+    """BASELINE cfg1: B1, ctx 4096, 32/8 heads, dim 128, Page64 shuffled, 8 partitions."""
+    case = make(cuda_device, rows=1, q_heads=32, kv_heads=8, dim=128, page_tokens=64, tokens=4096, seed=0xC0FFEE + 1)
+    assert kvb.attention_b200_supported(case.shape, case.device_input())
+    assert kvb.attention_partitions(case.shape, 8) == 8
+    res = run_single(case, partitions=8)
+    ref = oracle.reference_case(case, threads=8)
+    check_against_oracle(res, case.shape, ref, "cfg1")
+
+
+@pytest.mark.parametrize("page_tokens", [16, 32, 64])
+@pytest.mark.parametrize("partitions", [0, 1, 3])
+def test_pages_and_partitions(cuda_device, page_tokens, partitions):
+    case = make(cuda_device, rows=1, q_heads=32, kv_heads=8, dim=128, page_tokens=page_tokens,
+                tokens=3000, seed=11 + page_tokens)
+    res = run_single(case, partitions=partitions)
+    check_against_oracle(res, case.shape, oracle.reference_case(case, threads=8), f"P{page_tokens}/{partitions}")
+
+
+SELF_TEST = [
+    ("identity-pages", dict(tokens=256)),
+    ("partial-range", dict(tokens=256, begin=32, end=239)),
+    ("fully-masked", dict(tokens=256, q_positions=[-1])),
+    ("empty-range", dict(tokens=256, begin=256, end=256)),
+    ("causal-prefix", dict(tokens=256, q_positions=[17])),
+    ("three-splits-partial-last-page", dict(tokens=513, q_positions=[250])),
+    ("mid-page-begin", dict(tokens=700, begin=77, end=611)),
+    ("one-token", dict(tokens=300, begin=150, end=151)),
+]
+
+
+@pytest.mark.parametrize("name,kw", SELF_TEST, ids=[s[0] for s in SELF_TEST])
+@pytest.mark.parametrize("page_tokens", [16, 64])
+def test_reference_self_test_cases(cuda_device, name, kw, page_tokens):
+    case = make(cuda_device, rows=1, q_heads=32, kv_heads=8, dim=128, page_tokens=page_tokens, seed=5, **kw)
+    res = run_single(case)
+    check_against_oracle(res, case.shape, oracle.reference_case(case, threads=8), name)
+
+
+@pytest.mark.parametrize(
+    "rows,q_heads,kv_heads,dim,qpos",
+    [
+        (2, 32, 8, 128, [1000, 1300]),  # 8 query rows per KV head
+        (4, 32, 8, 128, [900, 1100, 1300, 1499]),  # 16 query rows: two n-tiles
+        (1, 64, 8, 128, None),  # GQA 8
+        (1, 16, 2, 64, None),  # dim 64
+        (2, 8, 4, 64, [600, 1499]),  # dim 64, two rows
+        (1, 32, 4, 256, None),  # dim 256
+    ],
+)
+def test_geometries(cuda_device, rows, q_heads, kv_heads, dim, qpos):
+    case = make(cuda_device, rows=rows, q_heads=q_heads, kv_heads=kv_heads, dim=dim, page_tokens=32,
+                tokens=1500, seed=rows * 100 + dim, q_positions=qpos)
+    assert kvb.attention_b200_supported(case.shape, case.device_input())
+    res = run_single(case)
+    check_against_oracle(res, case.shape, oracle.reference_case(case, threads=8), f"{rows}x{q_heads}/{kv_heads}d{dim}")
+
+
+def test_outlier_scales_page16_gqa8(cuda_device):
+    """cfg4 flavour: GQA 8, Page16, 1% of tokens with 10x scales."""
+    case = make(cuda_device, rows=1, q_heads=64, kv_heads=8, dim=128, page_tokens=16, tokens=4096,
+                seed=0xC0FFEE + 4, outlier_frac=0.01)
+    res = run_single(case)
+    check_against_oracle(res, case.shape, oracle.reference_case(case, threads=8), "cfg4-small")
+
+
+def test_large_and_tiny_scales(cuda_device):
+    """P is kept relative to a running power-of-two vscale exponent and Q is
+    rescaled by a power of two, so scales far outside f16 range still work."""
+    case = make(cuda_device, rows=1, q_heads=32, kv_heads=8, dim=128, page_tokens=64, tokens=2000, seed=77)
+    case.v_scales.mul_(1e6)
+    case.k_scales.mul_(1e-6)
+    case.q.mul_(3e4)
+    res = run_single(case)
+    ref = oracle.reference_case(case, threads=8)
+    got = normalized(res, case.shape)
+    ma, rl = errors(got, ref["normalized"])
+    assert rl <= REL_L2, rl
+
+
+def test_fp32_query_not_fp16_exact(cuda_device):
+    """Q that is not fp16-exact takes the hi/lo split path."""
+    case = make(cuda_device, rows=1, q_heads=32, kv_heads=8, dim=128, page_tokens=64, tokens=2048, seed=9)
+    case.q.add_(torch.randn_like(case.q) * 1e-3)
+    res = run_single(case)
+    check_against_oracle(res, case.shape, oracle.reference_case(case, threads=8), "fp32-q")
+
+
+def test_repeatable_bitwise(cuda_device):
+    case = make(cuda_device, rows=1, q_heads=32, kv_heads=8, dim=128, page_tokens=64, tokens=5000, seed=3)
+    a = run_single(case)
+    b = run_single(case)
+    for k in ("m", "l", "n", "out"):
+        assert torch.equal(a[k], b[k]), k
+
+
+def test_reference_api_and_merge_compat(cuda_device):
+    """launch_attention (reference signature) and merge_attention over the full
+    split_count of the scratch it leaves behind reproduce the same m/l/n."""
+    case = make(cuda_device, rows=1, q_heads=32, kv_heads=8, dim=128, page_tokens=64, tokens=4096, seed=21)
+    res = run_single(case, api="ref", fp16_out=False)
+    check_against_oracle(res, case.shape, oracle.reference_case(case, threads=8), "ref-api")
+    _, m2, l2, n2 = outputs_for(case.shape, cuda_device)
+    kvb.merge_attention(case.shape, res["scratch"], kvb.split_count(case.shape), m2, l2, n2)
+    torch.cuda.synchronize()
+    assert torch.equal(m2.cpu(), res["m"]) and torch.equal(l2.cpu(), res["l"]) and torch.equal(n2.cpu(), res["n"])
+
+
+def test_page_permutation_invariance_full_cfg2(cuda_device):
+    """BASELINE cfg2 at full size (64K ctx): a different physical placement of
+    the same logical KV gives bitwise-identical outputs, and the result
+    matches the FP64 oracle."""
+    case = make(cuda_device, rows=1, q_heads=32, kv_heads=8, dim=128, page_tokens=64, tokens=65536, seed=0xC0FFEE + 2)
+    res = run_single(case)
+    ref = oracle.reference_case(case, threads=16)
+    check_against_oracle(res, case.shape, ref, "cfg2")
+    # Move every logical page to a new physical slot.
+    g = torch.Generator(device="cpu").manual_seed(1234)
+    perm = torch.randperm(case.shape.pages, generator=g).to(cuda_device)
+    inv = torch.empty_like(perm)
+    inv[perm] = torch.arange(perm.numel(), device=cuda_device)
+    moved = synth.SingleCase(case.shape, case.q, case.q_positions, case.k_positions,
+                             perm[case.page_table.long()].to(torch.int32),
+                             case.k[inv], case.v[inv], case.k_scales[inv], case.v_scales[inv])
+    res2 = run_single(moved)
+    for k in ("m", "l", "n", "out"):
+        assert torch.equal(res[k], res2[k]), k
+
+
+def test_general_geometry_kernel(cuda_device):
+    """Shapes outside the tensor-core kernel run the general kernel."""
+    cases = [
+        dict(rows=1, q_heads=12, kv_heads=1, dim=96, page_tokens=8, tokens=700),  # group 12, dim 96, P8
+        dict(rows=8, q_heads=24, kv_heads=4, dim=256, page_tokens=32, tokens=1100),  # reference native shape
+        dict(rows=1, q_heads=4, kv_heads=2, dim=33, page_tokens=5, tokens=123),  # odd everything
+    ]
+    for i, kw in enumerate(cases):
+        qpos = None
+        if kw["rows"] > 1:
+            qpos = [kw["tokens"] - kw["rows"] + r for r in range(kw["rows"])]
+        case = make(cuda_device, seed=40 + i, q_positions=qpos, **kw)
+        assert not kvb.attention_b200_supported(case.shape, case.device_input())
+        res = run_single(case)
+        check_against_oracle(res, case.shape, oracle.reference_case(case, threads=8), f"general{i}")
+
+
+def test_mma_launcher_contract(cuda_device):
+    """launch_attention_mma keeps the reference predicate: its native shape
+    runs, BASELINE shapes are rejected with ValueError before launch."""
+    native = make(cuda_device, rows=8, q_heads=24, kv_heads=4, dim=256, page_tokens=32, tokens=600, seed=8,
+                  q_positions=[592 + r for r in range(8)])
+    assert kvb.attention_mma_supported(native.shape)
+    res = run_single(native, api="mma", fp16_out=False)
+    check_against_oracle(res, native.shape, oracle.reference_case(native, threads=8), "mma-native")
+    base = make(cuda_device, rows=1, q_heads=32, kv_heads=8, dim=128, page_tokens=64, tokens=256, seed=8)
+    with pytest.raises(ValueError):
+        run_single(base, api="mma", fp16_out=False)
+
+
+def test_fp32_kv(cuda_device):
+    case = make(cuda_device, rows=1, q_heads=8, kv_heads=2, dim=64, page_tokens=16, tokens=800, seed=12)
+    kf = (case.k.float() * case.k_scales.unsqueeze(-1)).contiguous()
+    vf = (case.v.float() * case.v_scales.unsqueeze(-2)).contiguous()
+    shape = kvb.Shape(**{**case.shape.__dict__, "int8": False})
+    fcase = synth.SingleCase(shape, case.q, case.q_positions, case.k_positions, case.page_table, kf, vf, None, None)
+    res = run_single(fcase)
+    ref = oracle.reference(shape, case.q, case.q_positions, case.k_positions, case.page_table, kf, vf)
+    check_against_oracle(res, shape, ref, "fp32-kv")
+
+
+def test_unaligned_buffers_use_general_kernel(cuda_device):
+    case = make(cuda_device, rows=1, q_heads=8, kv_heads=2, dim=128, page_tokens=64, tokens=500, seed=13)
+    kbuf = torch.empty(case.k.numel() + 4, dtype=torch.int8, device=cuda_device)
+    kbuf[4:] = case.k.reshape(-1)
+    shifted = synth.SingleCase(case.shape, case.q, case.q_positions, case.k_positions, case.page_table,
+                               kbuf[4:], case.v, case.k_scales, case.v_scales)
+    assert not kvb.attention_b200_supported(shifted.shape, shifted.device_input())
+    res = run_single(shifted)
+    check_against_oracle(res, case.shape, oracle.reference_case(case, threads=8), "unaligned")
+
+
+def test_invalid_arguments_raise_before_launch(cuda_device):
+    case = make(cuda_device, rows=1, q_heads=32, kv_heads=8, dim=128, page_tokens=64, tokens=256, seed=1)
+    scratch, m, l, n = outputs_for(case.shape, cuda_device)
+    bad = kvb.Shape(**{**case.shape.__dict__, "dim": 257})
+    with pytest.raises(ValueError, match="dim must be in"):
+        kvb.launch_attention(bad, case.device_input(), scratch, m, l, n)
+    inp = case.device_input()
+    inp.k = None
+    with pytest.raises(ValueError, match="non-null"):
+        kvb.launch_attention(case.shape, inp, scratch, m, l, n)
+    with pytest.raises(ValueError, match="split count"):
+        kvb.merge_attention(case.shape, scratch, 7, m, l, n)
+
+
+def test_batched_ragged(cuda_device):
+    """cfg3 flavour: ragged batch over one shared shuffled page pool."""
+    lens = synth.ragged_lengths(12, 1, 5000, seed=31) + [0, 64, 65]
+    bc = synth.make_batched(32, 8, 128, 64, lens, seed=0xC0FFEE + 3, device=cuda_device)
+    ws_bytes = kvb.batch_workspace_bytes(bc.shape)
+    ws = torch.empty(ws_bytes // 4 + 1, dtype=torch.float32, device=cuda_device)
+    B, H, D = bc.shape.batch, bc.shape.q_heads, bc.shape.dim
+    m = torch.empty(B * H, device=cuda_device)
+    l = torch.empty(B * H, device=cuda_device)
+    n = torch.empty(B * H * D, device=cuda_device)
+    out = torch.empty(B * H * D, dtype=torch.float16, device=cuda_device)
+    kvb.launch_attention_batched(bc.shape, bc.batch_input(), ws, ws_bytes, m, l, n, out)
+    torch.cuda.synchronize()
+    m, l, n, out = m.cpu(), l.cpu(), n.cpu(), out.cpu()
+    for b, length in enumerate(lens):
+        sl = slice(b * H, (b + 1) * H)
+        if length == 0:
+            assert torch.all(l[sl] == 0) and torch.all(torch.isneginf(m[sl]))
+            continue
+        npg = (length + 63) // 64
+        table = bc.block_table[b, :npg].cpu()
+        shape = kvb.Shape(1, H, 8, D, 64, bc.shape.pages, length, 0, length, bc.shape.scale, True)
+        ref = oracle.reference(shape, bc.q[b].cpu(), torch.tensor([length - 1]), torch.arange(length),
+                               torch.cat([table, torch.zeros(bc.shape.pages - npg, dtype=torch.int32)]),
+                               bc.k.cpu(), bc.v.cpu(), bc.k_scales.cpu(), bc.v_scales.cpu(), threads=8)
+        res = {"m": m[sl], "l": l[sl], "n": n[b * H * D:(b + 1) * H * D],
+               "out": out[b * H * D:(b + 1) * H * D]}
+        check_against_oracle(res, shape, ref, f"batch{b}")
+
+
+def test_shard_merge_matches_full_range(cuda_device):
+    """Sequence sharding: four disjoint page-aligned ranges computed
+    separately and merged with merge_attention_shards equal the full call."""
+    case = make(cuda_device, rows=1, q_heads=32, kv_heads=8, dim=128, page_tokens=64, tokens=8192, seed=55)
+    cuts = [0, 2048, 4096, 6144, 8192]
+    parts = []
+    for a, b in zip(cuts[:-1], cuts[1:]):
+        shape = kvb.Shape(**{**case.shape.__dict__, "begin": a, "end": b})
+        sub = synth.SingleCase(shape, case.q, case.q_positions, case.k_positions, case.page_table,
+                               case.k, case.v, case.k_scales, case.v_scales)
+        parts.append(run_single(sub, fp16_out=False))
+    mp = torch.stack([p["m"] for p in parts]).to(cuda_device)
+    lp = torch.stack([p["l"] for p in parts]).to(cuda_device)
+    npart = torch.stack([p["n"] for p in parts]).to(cuda_device)
+    rh, D = 32, 128
+    m = torch.empty(rh, device=cuda_device)
+    l = torch.empty(rh, device=cuda_device)
+    n = torch.empty(rh * D, device=cuda_device)
+    out = torch.empty(rh * D, dtype=torch.float16, device=cuda_device)
+    kvb.merge_attention_shards(4, rh, D, mp, lp, npart, m, l, n, out)
+    torch.cuda.synchronize()
+    res = {"m": m.cpu(), "l": l.cpu(), "n": n.cpu(), "out": out.cpu()}
+    check_against_oracle(res, case.shape, oracle.reference_case(case, threads=8), "shards")
+
+
+@pytest.mark.skipif(not oracle.RefCuda.available(), reason="reference CUDA build absent")
+def test_matches_reference_simt_kernel(cuda_device):
+    """Same device inputs through the reference's own SIMT launcher (compiled
+    for sm_100a from its sources) and through ours: n/l agree within the
+    path tolerance."""
+    case = make(cuda_device, rows=1, q_heads=32, kv_heads=8, dim=128, page_tokens=64, tokens=4096, seed=0xC0FFEE + 1)
+    ours = run_single(case)
+    ref_gpu = oracle.RefCuda()
+    scratch, m, l, n = outputs_for(case.shape, cuda_device)
+    ptrs = [t.data_ptr() for t in (case.q, case.q_positions, case.k_positions, case.page_table,
+                                   case.k, case.v, case.k_scales, case.v_scales)]
+    rc = ref_gpu.launch(case.shape, ptrs, scratch.data_ptr(), m.data_ptr(), l.data_ptr(), n.data_ptr(), 0)
+    assert rc == 0
+    torch.cuda.synchronize()
+    theirs = {"m": m.cpu(), "l": l.cpu(), "n": n.cpu()}
+    ma, rl = errors(normalized(ours, case.shape), normalized(theirs, case.shape))
+    assert ma <= MAX_ABS and rl <= REL_L2, (ma, rl)
+    ref = oracle.reference_case(case, threads=8)
+    ma_ref, rl_ref = errors(normalized(theirs, case.shape), ref["normalized"])
+    assert ma_ref <= MAX_ABS and rl_ref <= REL_L2, (ma_ref, rl_ref)
