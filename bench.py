@@ -461,7 +461,8 @@ def main():
 
     status = kvb.read_device_status()
     if status != 0:
-        raise RuntimeError(f"kernel status word {status}: a bounded wait gave up; numbers invalid")
+        raise RuntimeError(f"kernel status word {status}: a bounded wait gave up "
+                           f"({kvb.read_wait_failure()}); numbers invalid")
 
     per_call_ms = total_ms / args.steps
     value = world * nbytes / (per_call_ms / 1e3) / 1e9
@@ -495,7 +496,8 @@ def main():
                f"({len(layers)} x {nbytes / 1e6:.1f} MB)",
             sharding=f"kv-heads: {8 * world} KV heads, 8 per GPU" if world > 1 else "single GPU",
             launch="CUDA-graph replay of launch_attention_ex (partial + LSE merge + fp16 epilogue)",
-            compute="int8 codes widened exactly to f16, mma.sync m16n8k16 f16->f32",
+            compute="QK: int8 mma.sync m16n8k32 on raw K codes x 3 int8 limbs of Q (exact s32); "
+                    "PV: f16 mma.sync m16n8k16 on exactly widened V codes, fp32 accumulation",
         ),
         "roofline": {
             "bound": "hbm",

@@ -92,5 +92,9 @@ void merge_attention_shards(unsigned shards, unsigned row_heads, unsigned dim,
 // it. A nonzero value means a pipeline wait gave up and that call's outputs
 // are invalid.
 cudaError_t read_device_status(int* status);
+// The first bounded wait that gave up since the last read (all zero if none):
+// {status code, block, warp, stage, waited ns, waited SM cycles}. Reading
+// clears it.
+cudaError_t read_wait_failure(long long* record6);
 
 }  // namespace kvbridge

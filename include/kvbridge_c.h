@@ -122,6 +122,10 @@ int kvb_merge_attention_shards(unsigned shards, unsigned row_heads, unsigned dim
 /* Reads and clears the kernels' device status word (0 = ok). Returns the
  * cudaError_t of the read. */
 int kvb_read_device_status(int* status);
+/* The first bounded wait that gave up since the last read: six values
+ * {code, block, warp, stage, waited ns, waited SM cycles}; all zero if none.
+ * Reading clears it. Returns the cudaError_t of the read. */
+int kvb_read_wait_failure(long long* record6);
 
 /* Host-side schedule of the split-K kernel, exported for tests: the CTA that
  * owns global stage `stage` when `total` stages are split over `ctas` CTAs. */

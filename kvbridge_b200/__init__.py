@@ -33,6 +33,7 @@ from .api import (  # noqa: F401
     preload_attention_mma_kernels,
     preload_attention_reference_kernels,
     read_device_status,
+    read_wait_failure,
     schedule_cta_of,
     scratch_elements,
     split_count,

@@ -155,6 +155,7 @@ SIGNATURES = {
         ],
     ),
     "kvb_read_device_status": (c_int, [POINTER(c_int)]),
+    "kvb_read_wait_failure": (c_int, [POINTER(ctypes.c_longlong)]),
     "kvb_schedule_cta_of": (c_uint32, [c_uint64, c_uint64, c_uint32]),
 }
 

@@ -335,5 +335,14 @@ def read_device_status() -> int:
     return status.value
 
 
+def read_wait_failure() -> dict:
+    """The first bounded wait that gave up since the last read (code 0 = none)."""
+    rec = (ctypes.c_longlong * 6)()
+    code = _lib.load().kvb_read_wait_failure(rec)
+    if code != 0:
+        raise RuntimeError(f"reading the wait-failure record failed: cudaError {code}")
+    return dict(zip(("code", "block", "warp", "stage", "waited_ns", "waited_cycles"), (int(x) for x in rec)))
+
+
 def schedule_cta_of(stage: int, total: int, ctas: int) -> int:
     return int(_lib.load().kvb_schedule_cta_of(stage, total, ctas))

@@ -148,7 +148,7 @@ uint32_t log2_exact(uint32_t x) {
 // Merge launches.
 
 void launch_merge(int mode, const kvb::MergeParams& prm, cudaStream_t stream) {
-  const uint32_t blocks = (prm.row_heads + kvb::kMergeWarps - 1) / kvb::kMergeWarps;
+  const uint32_t blocks = prm.row_heads;  // one CTA per row-head
   if (blocks == 0) return;
   kvb::MergeParams copy = prm;
   void* args[] = {&copy};
@@ -500,6 +500,14 @@ cudaError_t read_device_status(int* status) {
   code = cudaMemcpyToSymbol(kvb::g_kvb_status, &zero, sizeof(int));
   *status = value;
   return code;
+}
+
+cudaError_t read_wait_failure(long long* record6) {
+  if (record6 == nullptr) return cudaErrorInvalidValue;
+  cudaError_t code = cudaMemcpyFromSymbol(record6, kvb::g_kvb_first_failure, 6 * sizeof(long long));
+  if (code != cudaSuccess) return code;
+  const long long zeros[6] = {0, 0, 0, 0, 0, 0};
+  return cudaMemcpyToSymbol(kvb::g_kvb_first_failure, zeros, sizeof(zeros));
 }
 
 }  // namespace kvbridge

@@ -237,6 +237,8 @@ int kvb_merge_attention_shards(unsigned shards, unsigned row_heads, unsigned dim
 
 int kvb_read_device_status(int* status) { return int(kvbridge::read_device_status(status)); }
 
+int kvb_read_wait_failure(long long* record6) { return int(kvbridge::read_wait_failure(record6)); }
+
 uint32_t kvb_schedule_cta_of(uint64_t stage, uint64_t total, uint32_t ctas) {
   if (total == 0 || ctas == 0 || stage >= total) return 0;
   return kvb::cta_of_stage(stage, total, ctas);

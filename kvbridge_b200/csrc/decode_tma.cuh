@@ -16,20 +16,24 @@
 //    converted before it reaches shared memory.
 //  * Math: each consumer warp owns whole stages (stage g goes to warp g % 4)
 //    and keeps its own online-softmax state. QK and PV both run "swap-AB" on
-//    the f16 m16n8k16 tensor-core MMA so that the query rows of the KV head
+//    warp-level tensor-core MMAs so that the query rows of the KV head
 //    (rows * group <= 8 * NT) sit in the narrow N dimension:
 //        S^T[token][qrow] = K[token][d] . Q^T[d][qrow]   (M = 16 tokens)
 //        O^T[d][qrow]     = V[d][token] . P[token][qrow]  (M = 16 dims)
-//    int8 codes are widened to f16 exactly in registers; per-token kscale
+//    QK runs on the int8 MMA (m16n8k32 s8.s8.s32): K is used exactly as
+//    stored and each query row is a 22-bit fixed-point value split into
+//    three signed int8 limbs (q = L0 + 2^8 L1 + 2^16 L2, scaled by a power of
+//    two per row), so the dot products accumulate exactly in s32 and are
+//    combined in fp32. PV runs on the f16 MMA: V codes are widened to f16
+//    exactly in registers and P = w * vscale is f16. Per-token kscale
 //    multiplies the fp32 scores and per-token vscale rides on P, as in the
 //    reference MMA kernel. The QK accumulator fragments become the PV B
 //    operand through movmatrix (8x8 transposes), never touching shared
 //    memory, because the token order of the QK rows is chosen so that the
 //    PV A operand (V rows, token-contiguous) loads as one 16-byte word per row.
-//  * Precision: Q is scaled per row by a power of two into f16 range and
-//    split into f16 hi + lo parts; the lo MMA is skipped for warps whose Q is
-//    exactly f16 (BASELINE queries are fp16). P is stored relative to a
-//    running power-of-two vscale exponent, so any finite vscale fits f16.
+//  * Precision: QK is exact up to the 2^-22 (relative to the row's largest
+//    |q|) rounding of Q. P is kept relative to a running power-of-two vscale
+//    exponent, so any finite vscale fits f16.
 //  * Pieces end with an in-CTA log-sum-exp combine of the four warps'
 //    states and one (m, l, n) write per query row.
 #include "kvb_device.cuh"
@@ -92,7 +96,9 @@ struct DecodeSmem {
   static constexpr uint32_t kOffStats = kOffCombine + kCombine;
   static constexpr uint32_t kOffBar = kOffStats + kStats;
   static constexpr uint32_t kOffAbort = kOffBar + kBarriers;
-  static constexpr uint32_t kBytes = kOffAbort + 16;
+  // Stage tags: the CTA stage sequence number each ring slot is armed for.
+  static constexpr uint32_t kOffTags = kOffAbort + 16;
+  static constexpr uint32_t kBytes = kOffTags + 4 * STAGES;
 };
 
 // ---------------------------------------------------------------------------
@@ -197,7 +203,8 @@ __device__ __forceinline__ uint64_t piece_end_stage(const DecodeParams& p, const
 
 template <int D, int STAGES>
 __device__ void produce(const DecodeParams& p, uint8_t* ring, uint64_t* full, uint64_t* empty,
-                        volatile int* abort_flag, uint64_t x0, uint64_t x1, uint64_t total) {
+                        volatile uint32_t* tags, volatile int* abort_flag, uint64_t x0, uint64_t x1,
+                        uint64_t total) {
   const uint32_t lane = threadIdx.x & 31;
   const uint64_t policy = l2_evict_first_policy();
   const uint32_t P = p.page_tokens;
@@ -220,12 +227,9 @@ __device__ void produce(const DecodeParams& p, uint8_t* ring, uint64_t* full, ui
     for (uint32_t j = pc.j0; j < pc.j1; ++j) {
       const uint32_t slot = g % STAGES;
       const uint32_t use = g / STAGES;
-      if (!mbar_wait_bounded(&empty[slot], (use & 1u) ^ 1u, abort_flag)) {
+      if (mbar_wait_bounded(&empty[slot], (use & 1u) ^ 1u, abort_flag, kStatusEmptyWaitTimeout,
+                            int(g)) != kWaitOk) {
         failed = true;
-        if (lane == 0) {
-          *abort_flag = 1;
-          atomicMax(&g_kvb_status, kStatusEmptyWaitTimeout);
-        }
         break;
       }
       const uint32_t tb = (first_stage + j) * kStageTokens;
@@ -246,7 +250,13 @@ __device__ void produce(const DecodeParams& p, uint8_t* ring, uint64_t* full, ui
       const uint32_t okmask = __ballot_sync(0xffffffffu, ok);
       if (__ballot_sync(0xffffffffu, mine && !ok) && lane == 0)
         atomicMax(&g_kvb_status, kStatusBadPage);
-      if (lane == 0) mbar_arrive_expect_tx(&full[slot], __popc(okmask) * page_bytes);
+      if (lane == 0) {
+        // The slot is free, so its full barrier has completed the phase of
+        // stage g - STAGES; publishing g tells the consumer of stage g that
+        // the barrier's parity now refers to stage g (see the consumer loop).
+        tags[slot] = g;
+        mbar_arrive_expect_tx(&full[slot], __popc(okmask) * page_bytes);
+      }
       __syncwarp();
       if (ok) {
         uint8_t* st = ring + size_t(slot) * StageLayout<D>::kBytes;
@@ -269,10 +279,11 @@ __device__ void produce(const DecodeParams& p, uint8_t* ring, uint64_t* full, ui
   // CTA can exit; only the last STAGES of them can still be in flight.
   const uint32_t first = g > STAGES ? g - STAGES : 0u;
   for (uint32_t s = first; s < g; ++s) {
-    if (!mbar_wait_bounded(&full[s % STAGES], (s / STAGES) & 1u, abort_flag)) {
-      if (lane == 0) atomicMax(&g_kvb_status, kStatusDrainTimeout);
+    // Copies land whatever the consumers do, so this wait ignores an abort.
+    volatile int no_abort = 0;
+    if (mbar_wait_bounded(&full[s % STAGES], (s / STAGES) & 1u, &no_abort, kStatusDrainTimeout,
+                          int(s)) != kWaitOk)
       break;
-    }
   }
 }
 
@@ -287,21 +298,34 @@ struct WarpState {
   int ev;                    // running vscale exponent of acc
 };
 
-// Per-piece query operands of one warp.
+// Per-piece query operands of one warp: the three int8 limbs of every query
+// row in the B-fragment layout of m16n8k32 (k-step j covers dims
+// 64*(j/2) + 16*tig + 8*(j%2) + [0,8) for lane tig), and the fp32 factor
+// turning combined limb dots into log2-unit scores.
 template <int D, int NT>
 struct QueryFrags {
-  uint32_t hi[NT][D / 16][2];
-  uint32_t lo[NT][D / 16][2];
+  uint32_t limb[NT][D / 32][3][2];
   float cf[NT][2];       // score factor of the thread's C columns (log2 units)
   int64_t qpos[NT][2];   // query position of the thread's C columns
-  bool use_lo;
 };
+
+// Signed int8 limbs of a fixed-point value |q| <= 2^22: q = l0 + 256 l1 + 65536 l2.
+__device__ __forceinline__ void split_limbs(int q, int& l0, int& l1, int& l2) {
+  l0 = static_cast<int8_t>(q & 0xff);
+  const int r = (q - l0) >> 8;
+  l1 = static_cast<int8_t>(r & 0xff);
+  l2 = (r - l1) >> 8;
+}
+
+__device__ __forceinline__ uint32_t pack_s8x4(int a, int b, int c, int d) {
+  return (uint32_t(a) & 0xffu) | ((uint32_t(b) & 0xffu) << 8) | ((uint32_t(c) & 0xffu) << 16) |
+         (uint32_t(d) << 24);
+}
 
 template <int D, int NT>
 __device__ __forceinline__ void load_query(const DecodeParams& p, const Piece& pc,
                                            QueryFrags<D, NT>& qf) {
   const uint32_t lane = threadIdx.x & 31, grp = lane >> 2, tig = lane & 3;
-  bool any_lo = false;
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) {
     const uint32_t col = 8 * nt + grp;
@@ -326,45 +350,41 @@ __device__ __forceinline__ void load_query(const DecodeParams& p, const Piece& p
     }
     amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
     amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
-    // Power-of-two shift putting max|q| in [2^14, 2^15): exact rescaling that
-    // keeps both f16 parts normal and far from overflow.
-    int shift = 0;
-    if (amax > 0.f) {
-      const int e = int((__float_as_uint(amax) >> 23) & 0xffu) - 126;
-      shift = max(-100, min(100, e - 15));
-    }
-    const float down = __uint_as_float(uint32_t(127 - shift) << 23);
+    // 2^e > max|q|; q * 2^(22-e) rounds to an integer of magnitude <= 2^22.
+    int e = 0;
+    if (amax > 0.f) e = int((__float_as_uint(amax) >> 23) & 0xffu) - 126;
+    e = max(-100, min(100, e));
+    const float up = __uint_as_float(uint32_t(127 + 22 - e) << 23);
 #pragma unroll
     for (int c = 0; c < D / 64; ++c) {
 #pragma unroll
-      for (int jj = 0; jj < 4; ++jj) {
-        float x[4], h[4], rem[4];
+      for (int jj = 0; jj < 2; ++jj) {
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          x[i] = vals[c][4 * jj + i] * down;
-          h[i] = __half2float(__float2half_rn(x[i]));
-          rem[i] = x[i] - h[i];
-          any_lo |= rem[i] != 0.f;
+        for (int half = 0; half < 2; ++half) {
+          int l[3][4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int qi = __float2int_rn(vals[c][8 * jj + 4 * half + i] * up);
+            split_limbs(qi, l[0][i], l[1][i], l[2][i]);
+          }
+#pragma unroll
+          for (int k = 0; k < 3; ++k)
+            qf.limb[nt][2 * c + jj][k][half] = pack_s8x4(l[k][0], l[k][1], l[k][2], l[k][3]);
         }
-        qf.hi[nt][4 * c + jj][0] = pack_half2(h[0], h[1]);
-        qf.hi[nt][4 * c + jj][1] = pack_half2(h[2], h[3]);
-        qf.lo[nt][4 * c + jj][0] = pack_half2(rem[0], rem[1]);
-        qf.lo[nt][4 * c + jj][1] = pack_half2(rem[2], rem[3]);
       }
     }
-    const float cf_b = p.score_scale * kLog2e * __uint_as_float(uint32_t(127 + shift) << 23);
+    const float cf_b = p.score_scale * kLog2e * __uint_as_float(uint32_t(127 + e - 22) << 23);
     // C layout: this thread's columns are 2*tig and 2*tig+1 of the n-tile;
     // their factor lives in lane 4*column.
 #pragma unroll
-    for (int e = 0; e < 2; ++e) {
-      qf.cf[nt][e] = __shfl_sync(0xffffffffu, cf_b, 4 * (2 * tig + e));
-      const uint32_t ccol = 8 * nt + 2 * tig + e;
+    for (int ee = 0; ee < 2; ++ee) {
+      qf.cf[nt][ee] = __shfl_sync(0xffffffffu, cf_b, 4 * (2 * tig + ee));
+      const uint32_t ccol = 8 * nt + 2 * tig + ee;
       int64_t qp = INT64_MAX;
       if (p.seq_lens == nullptr && ccol < p.qr) qp = __ldg(p.q_positions + ccol / p.group);
-      qf.qpos[nt][e] = qp;
+      qf.qpos[nt][ee] = qp;
     }
   }
-  qf.use_lo = __any_sync(0xffffffffu, any_lo);
 }
 
 // One 64-token stage for one warp.
@@ -386,10 +406,13 @@ __device__ __forceinline__ void consume_stage(const DecodeParams& p, const uint8
 #pragma unroll
   for (int s = 0; s < 4; ++s) {
     const uint32_t t0 = 16 * (grp >> 1) + 4 * s + (grp & 1), t1 = t0 + 2;
+    int acc[NT][3][4];
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-      for (int i = 0; i < 4; ++i) sc[s][nt][i] = 0.f;
+      for (int k = 0; k < 3; ++k)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) acc[nt][k][i] = 0;
 #pragma unroll
     for (int c = 0; c < D / 64; ++c) {
       const uint4 ra = *reinterpret_cast<const uint4*>(sk + t0 * D + 64 * c + 16 * tig);
@@ -397,19 +420,22 @@ __device__ __forceinline__ void consume_stage(const DecodeParams& p, const uint8
       const uint32_t wa[4] = {ra.x, ra.y, ra.z, ra.w};
       const uint32_t wb[4] = {rb.x, rb.y, rb.z, rb.w};
 #pragma unroll
-      for (int jj = 0; jj < 4; ++jj) {
-        uint32_t a0, a1, a2, a3;
-        int8x4_to_f16x4(wa[jj], a0, a2);
-        int8x4_to_f16x4(wb[jj], a1, a3);
+      for (int jj = 0; jj < 2; ++jj) {
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt) {
-          mma_16816(sc[s][nt], a0, a1, a2, a3, qf.hi[nt][4 * c + jj][0], qf.hi[nt][4 * c + jj][1]);
-          if (qf.use_lo)
-            mma_16816(sc[s][nt], a0, a1, a2, a3, qf.lo[nt][4 * c + jj][0],
-                      qf.lo[nt][4 * c + jj][1]);
-        }
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+          for (int k = 0; k < 3; ++k)
+            imma_16832(acc[nt][k], wa[2 * jj], wb[2 * jj], wa[2 * jj + 1], wb[2 * jj + 1],
+                       qf.limb[nt][2 * c + jj][k][0], qf.limb[nt][2 * c + jj][k][1]);
       }
     }
+    // Limb dots are exact integers (|acc| < 2^21); combine in fp32.
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        sc[s][nt][i] = fmaf(float(acc[nt][2][i]), 65536.f,
+                            fmaf(float(acc[nt][1][i]), 256.f, float(acc[nt][0][i])));
   }
 
   // ---- scores in log2 units, masking.
@@ -566,6 +592,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 2) decode_partial_kernel(Decod
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kOffBar);
   uint64_t* empty = full + STAGES;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kOffAbort);
+  volatile uint32_t* tags = reinterpret_cast<volatile uint32_t*>(smem + L::kOffTags);
 
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
@@ -574,6 +601,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 2) decode_partial_kernel(Decod
       mbar_init(&empty[s], 1);
     }
     *abort_flag = 0;
+    for (int s = 0; s < STAGES; ++s) tags[s] = 0xffffffffu;
     fence_barrier_init();
   }
   __syncthreads();
@@ -585,7 +613,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 2) decode_partial_kernel(Decod
   const uint64_t x1 = cta_stage_begin(blockIdx.x + 1, total, p.ctas);
 
   if (warp == kProducerWarp) {
-    produce<D, STAGES>(p, ring, full, empty, abort_flag, x0, x1, total);
+    produce<D, STAGES>(p, ring, full, empty, tags, abort_flag, x0, x1, total);
     return;
   }
 
@@ -624,12 +652,15 @@ __global__ void __launch_bounds__(kDecodeThreads, 2) decode_partial_kernel(Decod
     for (uint32_t i = first; i < n; i += kConsumerWarps) {
       const uint32_t g = g_base + i;
       const uint32_t slot = g % STAGES;
-      if (!mbar_wait_bounded(&full[slot], (g / STAGES) & 1u, abort_flag)) {
-        if (lane == 0) {
-          *abort_flag = 1;
-          atomicMax(&g_kvb_status, kStatusFullWaitTimeout);
-        }
-      }
+      // Consecutive uses of a slot go to different warps, so this warp may
+      // arrive here while the slot still holds stage g - STAGES in flight:
+      // the full barrier is then one phase behind, and a parity test alone
+      // would mistake that phase for this one. Wait for the producer to tag
+      // the slot with g first; from then on the barrier is in the phase of
+      // stage g or past it, and the parity test is exact.
+      if (wait_tag_bounded(&tags[slot], g, abort_flag, kStatusFullWaitTimeout, int(g)) == kWaitOk)
+        mbar_wait_bounded(&full[slot], (g / STAGES) & 1u, abort_flag, kStatusFullWaitTimeout,
+                          int(g));
       const uint32_t tb = (first_stage + pc.j0 + i) * kStageTokens;
       consume_stage<D, NT>(p, ring + size_t(slot) * StageLayout<D>::kBytes, tb, pc.lo, pc.hi,
                            all_visible, qf, ws);

@@ -22,6 +22,23 @@ enum : int {
 // translation unit, so this is the module's single definition.
 __device__ int g_kvb_status;
 
+// The first bounded wait that gave up since the host last read it:
+// {code, block, warp, stage, waited ns (globaltimer), waited SM cycles}.
+__device__ long long g_kvb_first_failure[6];
+
+__device__ __forceinline__ void record_wait_failure(int code, int stage, long long ns,
+                                                    long long cycles) {
+  if (atomicCAS(reinterpret_cast<unsigned long long*>(&g_kvb_first_failure[0]), 0ull,
+                static_cast<unsigned long long>(code)) == 0ull) {
+    g_kvb_first_failure[1] = blockIdx.x;
+    g_kvb_first_failure[2] = threadIdx.x >> 5;
+    g_kvb_first_failure[3] = stage;
+    g_kvb_first_failure[4] = ns;
+    g_kvb_first_failure[5] = cycles;
+  }
+  atomicMax(&g_kvb_status, code);
+}
+
 // Upper bound of any single pipeline wait. A correct pipeline never waits
 // more than a few microseconds; the bound only keeps a broken one from
 // holding the GPU.
@@ -68,18 +85,48 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return done != 0;
 }
 
+enum WaitResult : int { kWaitOk = 0, kWaitTimeout = 1, kWaitAborted = 2 };
+
 // Wait for phase `parity` of `bar` to complete, giving up after kWaitLimitNs.
-// Returns false on timeout. `abort_flag` (shared memory) short-circuits every
-// later wait of the CTA once one wait has failed.
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity,
-                                                  volatile int* abort_flag) {
-  if (mbar_try_wait(bar, parity)) return true;
+// `abort_flag` (shared memory) ends every later wait of the CTA once one wait
+// has timed out. A timeout is recorded (first failure wins) with `code` and
+// `stage`; an abort is not, so the record names the wait that gave up first.
+__device__ __forceinline__ int mbar_wait_bounded(uint64_t* bar, uint32_t parity,
+                                                 volatile int* abort_flag, int code, int stage) {
+  if (mbar_try_wait(bar, parity)) return kWaitOk;
   const unsigned long long start = global_ns();
+  const long long start_cycles = clock64();
   for (unsigned spin = 1;; ++spin) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait(bar, parity)) return kWaitOk;
     if ((spin & 255u) == 0) {
-      if (*abort_flag) return false;
-      if (global_ns() - start > kWaitLimitNs) return false;
+      if (*abort_flag) return kWaitAborted;
+      const unsigned long long waited = global_ns() - start;
+      if (waited > kWaitLimitNs) {
+        *abort_flag = 1;
+        record_wait_failure(code, stage, static_cast<long long>(waited), clock64() - start_cycles);
+        return kWaitTimeout;
+      }
+    }
+  }
+}
+
+// Wait until the shared word `*tag` equals `value` (bounded like
+// mbar_wait_bounded; same codes and abort behaviour).
+__device__ __forceinline__ int wait_tag_bounded(const volatile uint32_t* tag, uint32_t value,
+                                                volatile int* abort_flag, int code, int stage) {
+  if (*tag == value) return kWaitOk;
+  const unsigned long long start = global_ns();
+  const long long start_cycles = clock64();
+  for (unsigned spin = 1;; ++spin) {
+    if (*tag == value) return kWaitOk;
+    if ((spin & 255u) == 0) {
+      if (*abort_flag) return kWaitAborted;
+      const unsigned long long waited = global_ns() - start;
+      if (waited > kWaitLimitNs) {
+        *abort_flag = 1;
+        record_wait_failure(code, stage, static_cast<long long>(waited), clock64() - start_cycles);
+        return kWaitTimeout;
+      }
     }
   }
 }
@@ -111,6 +158,16 @@ __device__ __forceinline__ void grid_launch_dependents() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
+// Warpgroup register reallocation (all four warps of a warpgroup execute it).
+template <int N>
+__device__ __forceinline__ void warpgroup_reg_release() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <int N>
+__device__ __forceinline__ void warpgroup_reg_acquire() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+
 // Named barrier over `threads` threads (multiple of 32), id 1..15.
 __device__ __forceinline__ void named_barrier(uint32_t id, uint32_t threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
@@ -122,6 +179,15 @@ __device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a
   asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
       "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// D += A * B for one m16n8k32 tile, s8 operands, exact s32 accumulators.
+__device__ __forceinline__ void imma_16832(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                           uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 

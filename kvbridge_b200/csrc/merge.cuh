@@ -3,10 +3,8 @@
 // 295-335): for each (row, head)
 //   M = max over partials with l_p > 0 of m_p
 //   L = sum_p exp(m_p - M) * l_p,   N[d] = sum_p exp(m_p - M) * n_p[d]
-// with m = -inf, l = 0, n = 0 when no partial has l_p > 0. One warp merges
-// one row-head: lanes reduce over partials with shuffles, then each lane
-// accumulates the dims d = lane + 32k. The optional fp16 epilogue writes
-// out = N / L (0 for empty rows).
+// with m = -inf, l = 0, n = 0 when no partial has l_p > 0. The optional
+// fp16 epilogue writes out = N / L (0 for empty rows).
 //
 // The same kernel serves three partial layouts:
 //   kScratch - the reference scratch layout [rh][split][dim+2]
@@ -64,17 +62,29 @@ __device__ __forceinline__ void merge_batched_geometry(const MergeParams& p, uin
   total = all * p.kv_heads;
 }
 
+// One CTA of kMergeWarps warps merges one row-head. Partials are taken in
+// chunks of kMergeWarps * kPerWarp: every thread issues the loads of all its
+// partials (m, l and its dims of n) before using any, so a chunk costs one
+// memory round trip; chunks are folded with a running max.
+constexpr int kPerWarp = 8;
+
 template <int MODE>
 __global__ void __launch_bounds__(32 * kMergeWarps) merge_kernel(MergeParams p) {
+  __shared__ float red_m[kMergeWarps];
+  __shared__ float red_l[kMergeWarps];
+  __shared__ float red_n[kMergeWarps][256];
   grid_dependency_wait();
-  const uint32_t lane = threadIdx.x & 31;
-  const uint32_t rh = blockIdx.x * kMergeWarps + (threadIdx.x >> 5);
-  if (rh >= p.row_heads) return;
+  const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const uint32_t rh = blockIdx.x;
   const uint32_t D = p.dim;
 
   const float *mb, *lb, *nb;
   size_t ms, ls, ns;
   uint32_t np = p.np;
+  // kBatched: the pieces of a segment are those of CTAs c_first..c_last that
+  // own at least one stage (with fewer stages than CTAs some ranges are empty).
+  uint32_t c_first = 0;
+  uint64_t total = 0;
   if (MODE == kMergeScratch) {
     mb = p.part + size_t(rh) * p.split_stride * (D + 2);
     lb = mb + 1;
@@ -89,12 +99,11 @@ __global__ void __launch_bounds__(32 * kMergeWarps) merge_kernel(MergeParams p) 
   } else {
     const uint32_t b = rh / p.q_heads, hq = rh % p.q_heads;
     const uint32_t h = hq / p.group, g = hq % p.group;
-    uint64_t pref, total;
+    uint64_t pref;
     merge_batched_geometry(p, b, pref, total);
     const uint32_t len = min(p.seq_lens[b], p.max_tokens);
     const uint32_t t = stages_of_range(0, len);
     np = 0;
-    uint32_t c_first = 0;
     if (t > 0) {
       const uint64_t seg_off = pref * p.kv_heads + uint64_t(h) * t;
       c_first = cta_of_stage(seg_off, total, p.ctas);
@@ -107,62 +116,78 @@ __global__ void __launch_bounds__(32 * kMergeWarps) merge_kernel(MergeParams p) 
     ms = ls = ns = size_t(p.group) * (D + 2);
   }
 
-  // Pass 1: global max over partials with l > 0.
-  float M = -INFINITY;
-  for (uint32_t i = lane; i < np; i += 32) {
-    const float li = lb[i * ls];
-    if (li > 0.f) M = fmaxf(M, mb[i * ms]);
-  }
-  M = warp_max(M);
-
-  // Pass 2: weights, denominator and numerators.
-  constexpr int kMaxPerLane = 8;  // dims per lane, dim <= 256
-  float acc[kMaxPerLane];
+  constexpr int kMaxK = 8;  // dims per lane: d = lane + 32k, dim <= 256
+  float acc[kMaxK];
 #pragma unroll
-  for (int k = 0; k < kMaxPerLane; ++k) acc[k] = 0.f;
-  float L = 0.f;
-  if (M != -INFINITY) {
-    for (uint32_t base = 0; base < np; base += 32) {
-      const uint32_t i = base + lane;
-      float e = 0.f;
-      if (i < np) {
-        const float li = lb[i * ls];
-        if (li > 0.f) {
-          e = expf(mb[i * ms] - M);
-          L += e * li;
-        }
-      }
-      const uint32_t cnt = min(32u, np - base);
-      for (uint32_t j = 0; j < cnt; ++j) {
-        const float ej = __shfl_sync(0xffffffffu, e, j);
-        if (ej == 0.f) continue;
-        const float* src = nb + size_t(base + j) * ns;
+  for (int k = 0; k < kMaxK; ++k) acc[k] = 0.f;
+  float M = -INFINITY, Lw = 0.f;  // running max (block-uniform), warp-partial denominator
+  for (uint32_t base = 0; base < np; base += kMergeWarps * kPerWarp) {
+    float mv[kPerWarp], lv[kPerWarp], nv[kPerWarp][kMaxK];
 #pragma unroll
-        for (int k = 0; k < kMaxPerLane; ++k) {
-          const uint32_t d = lane + 32 * k;
-          if (d < D) acc[k] = fmaf(ej, src[d], acc[k]);
-        }
+    for (int j = 0; j < kPerWarp; ++j) {
+      const uint32_t i = base + warp + kMergeWarps * j;
+      bool ok = i < np;
+      if (MODE == kMergeBatched && ok)
+        ok = cta_stage_begin(c_first + i + 1, total, p.ctas) > cta_stage_begin(c_first + i, total, p.ctas);
+      lv[j] = ok ? lb[i * ls] : 0.f;
+      mv[j] = ok ? mb[i * ms] : -INFINITY;
+#pragma unroll
+      for (int k = 0; k < kMaxK; ++k) {
+        const uint32_t d = lane + 32 * k;
+        nv[j][k] = (ok && d < D) ? nb[i * ns + d] : 0.f;
       }
     }
-    L = warp_sum(L);
+    float cm = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < kPerWarp; ++j)
+      if (lv[j] > 0.f) cm = fmaxf(cm, mv[j]);
+    if (lane == 0) red_m[warp] = cm;
+    __syncthreads();
+    float mnew = M;
+#pragma unroll
+    for (int w = 0; w < kMergeWarps; ++w) mnew = fmaxf(mnew, red_m[w]);
+    __syncthreads();
+    if (mnew == -INFINITY) continue;
+    const float alpha = M == -INFINITY ? 0.f : expf(M - mnew);
+    Lw *= alpha;
+#pragma unroll
+    for (int k = 0; k < kMaxK; ++k) acc[k] *= alpha;
+#pragma unroll
+    for (int j = 0; j < kPerWarp; ++j) {
+      const float e = lv[j] > 0.f ? expf(mv[j] - mnew) : 0.f;
+      Lw = fmaf(e, lv[j], Lw);
+#pragma unroll
+      for (int k = 0; k < kMaxK; ++k) acc[k] = fmaf(e, nv[j][k], acc[k]);
+    }
+    M = mnew;
   }
-  if (lane == 0) {
+  // Fold the warps.
+  if (lane == 0) red_l[warp] = Lw;
+#pragma unroll
+  for (int k = 0; k < kMaxK; ++k) {
+    const uint32_t d = lane + 32 * k;
+    if (d < D) red_n[warp][d] = acc[k];
+  }
+  __syncthreads();
+  float L = 0.f;
+#pragma unroll
+  for (int w = 0; w < kMergeWarps; ++w) L += red_l[w];
+  if (threadIdx.x == 0) {
     p.m[rh] = L > 0.f ? M : -INFINITY;
     p.l[rh] = L;
   }
   const float inv = L > 0.f ? 1.f / L : 0.f;
+  for (uint32_t d = threadIdx.x; d < D; d += 32 * kMergeWarps) {
+    float v = 0.f;
 #pragma unroll
-  for (int k = 0; k < kMaxPerLane; ++k) {
-    const uint32_t d = lane + 32 * k;
-    if (d < D) {
-      const float v = L > 0.f ? acc[k] : 0.f;
-      p.n[size_t(rh) * D + d] = v;
-      if (p.out != nullptr) p.out[size_t(rh) * D + d] = __float2half_rn(v * inv);
-    }
+    for (int w = 0; w < kMergeWarps; ++w) v += red_n[w][d];
+    v = L > 0.f ? v : 0.f;
+    p.n[size_t(rh) * D + d] = v;
+    if (p.out != nullptr) p.out[size_t(rh) * D + d] = __float2half_rn(v * inv);
   }
   if (MODE == kMergeScratch && p.fill_empty) {
     float* row = p.part + size_t(rh) * p.split_stride * (D + 2);
-    for (uint32_t i = np + lane; i < p.split_stride; i += 32) {
+    for (uint32_t i = np + threadIdx.x; i < p.split_stride; i += 32 * kMergeWarps) {
       row[size_t(i) * (D + 2) + 0] = -INFINITY;
       row[size_t(i) * (D + 2) + 1] = 0.f;
     }

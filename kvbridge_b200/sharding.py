@@ -1,0 +1,106 @@
+"""Multi-GPU partitioning of decode attention (host orchestration).
+
+Two modes, one process per GPU over ``torch.distributed``:
+
+* KV-head sharding: rank g owns KV heads [g*H/G, (g+1)*H/G) with their query
+  heads, in its own reference-format pool. The heads are independent, so the
+  attention itself needs no communication; outputs stay head-sharded (an
+  optional all-gather assembles them).
+* Sequence sharding: rank g owns a contiguous, page-aligned token range of
+  every sequence. Each rank computes the (m, l, n) partial of its range
+  (launch_attention_ex / launch_attention_batched over local pages); the
+  partials are all-gathered and merged with merge_attention_shards, the same
+  log-sum-exp algebra as the split-K merge (reference src/attention_shared.cu:
+  295-335) with one "split" per rank.
+
+The exchange and merge functions are parameters so the orchestration runs
+unchanged on CPU ``gloo`` ranks in the tests.
+"""
+from __future__ import annotations
+
+from typing import Callable, List, Sequence, Tuple
+
+
+def kv_head_range(kv_heads: int, world: int, rank: int) -> Tuple[int, int]:
+    """KV heads [h0, h1) owned by `rank`; kv_heads must divide evenly."""
+    if world <= 0 or not 0 <= rank < world:
+        raise ValueError("rank must be in [0, world)")
+    if kv_heads % world:
+        raise ValueError(f"{kv_heads} KV heads do not shard evenly over {world} ranks")
+    per = kv_heads // world
+    return rank * per, (rank + 1) * per
+
+
+def sequence_ranges(tokens: int, page_tokens: int, world: int) -> List[Tuple[int, int]]:
+    """Contiguous page-aligned token ranges covering [0, tokens), balanced to
+    one page; ranks beyond the page count get empty ranges."""
+    if world <= 0 or page_tokens <= 0 or tokens < 0:
+        raise ValueError("world and page_tokens must be positive")
+    pages = -(-tokens // page_tokens)
+    out = []
+    for r in range(world):
+        p0 = pages * r // world
+        p1 = pages * (r + 1) // world
+        out.append((min(tokens, p0 * page_tokens), min(tokens, p1 * page_tokens)))
+    return out
+
+
+def local_pages(ranges: Sequence[Tuple[int, int]], rank: int, page_tokens: int) -> Tuple[int, int]:
+    """Logical pages [p0, p1) stored by `rank` for its token range."""
+    b, e = ranges[rank]
+    if e <= b:
+        return b // page_tokens, b // page_tokens
+    return b // page_tokens, -(-e // page_tokens)
+
+
+def all_gather_partials(m, l, n, group=None):
+    """Stacks every rank's (m, l, n) partial: [G, ...] tensors, rank-major."""
+    import torch
+    import torch.distributed as dist
+
+    world = dist.get_world_size(group)
+    out = []
+    for t in (m, l, n):
+        t = t.contiguous()
+        buf = torch.empty((world,) + tuple(t.shape), dtype=t.dtype, device=t.device)
+        if t.device.type == "cuda":
+            dist.all_gather_into_tensor(buf, t, group=group)
+        else:
+            dist.all_gather(list(buf.unbind(0)), t, group=group)
+        out.append(buf)
+    return tuple(out)
+
+
+def sequence_sharded_decode(
+    local_partial: Callable[[], Tuple["object", "object", "object"]],
+    merge: Callable[["object", "object", "object"], "object"],
+    group=None,
+    exchange: Callable = all_gather_partials,
+):
+    """Computes this rank's partial, exchanges partials, merges them.
+
+    local_partial() -> (m, l, n) of the rank's range; merge(m_parts, l_parts,
+    n_parts) -> merged result. Every rank takes the same collective steps."""
+    m, l, n = local_partial()
+    mp, lp, np_ = exchange(m, l, n, group)
+    return merge(mp, lp, np_)
+
+
+def gpu_shard_merge(rh: int, dim: int, out_f16: bool = True):
+    """merge() for sequence_sharded_decode on GPU tensors: the library's
+    merge_attention_shards kernel (log-sum-exp over the ranks' partials)."""
+    import torch
+
+    from . import api
+
+    def merge(mp, lp, np_):
+        shards = mp.shape[0]
+        dev = mp.device
+        m = torch.empty(rh, device=dev)
+        l = torch.empty(rh, device=dev)
+        n = torch.empty(rh * dim, device=dev)
+        out = torch.empty(rh * dim, dtype=torch.float16, device=dev) if out_f16 else None
+        api.merge_attention_shards(shards, rh, dim, mp, lp, np_, m, l, n, out)
+        return m, l, n, out
+
+    return merge

@@ -9,11 +9,10 @@ import kvbridge_b200 as kvb
 from kvbridge_b200 import synth
 
 # Acceptance tolerances of this path against the FP64 oracle: max-abs 2e-3
-# and rel-L2 1e-3. They apply to the fp32 n/l the kernels compute, against
-# the unrounded oracle. The fp16 output is held to the same numbers against
-# the oracle rounded to fp16: for |out| >= 4 fp16's own rounding (half an ulp,
-# up to 2^-8 at |out| < 8 and more above) exceeds 2e-3, and the outlier
-# configuration reaches |out| ~ 32.
+# and rel-L2 1e-3. They apply as stated to the fp32 n/l the kernels compute.
+# The fp16 output also carries its own rounding (half an fp16 ulp of the
+# value, 2^-9 at |out| in [4, 8) and more above; the outlier configuration
+# reaches |out| ~ 32), so its max-abs bound is 2e-3 plus that half ulp.
 MAX_ABS = 2e-3
 REL_L2 = 1e-3
 
@@ -88,7 +87,10 @@ def check_against_oracle(res, shape, ref, label=""):
         assert np.allclose(l[vis], ref["l"][vis], rtol=2e-3, atol=0), f"{label}: l differs"
     if "out" in res:
         out = res["out"].double().numpy().reshape(shape.rows, shape.q_heads, shape.dim)
-        ref16 = ref["normalized"].astype(np.float16).astype(np.float64)
-        ma16, rl16 = errors(out, ref16)
-        assert ma16 <= MAX_ABS and rl16 <= REL_L2, f"{label}: fp16 out max_abs={ma16:.3e} rel_l2={rl16:.3e}"
+        expect = ref["normalized"]
+        half_ulp = np.spacing(np.abs(expect).astype(np.float16)).astype(np.float64) / 2
+        excess = np.abs(out - expect) - half_ulp
+        ma16 = float(excess.max()) if excess.size else 0.0
+        _, rl16 = errors(out, expect)
+        assert ma16 <= MAX_ABS and rl16 <= REL_L2, f"{label}: fp16 out max_abs-halfulp={ma16:.3e} rel_l2={rl16:.3e}"
     return ma, rl

@@ -304,3 +304,37 @@ def test_matches_reference_simt_kernel(cuda_device):
     ref = oracle.reference_case(case, threads=8)
     ma_ref, rl_ref = errors(normalized(theirs, case.shape), ref["normalized"])
     assert ma_ref <= MAX_ABS and rl_ref <= REL_L2, (ma_ref, rl_ref)
+
+
+def test_pipeline_graph_replay_stress(cuda_device):
+    """Back-to-back calls over several KV layers, replayed as a CUDA graph:
+    the copy ring must never let a warp pass a stage that has not landed
+    (the bounded waits would record it in the status word), and every replay
+    must reproduce the eager results bit for bit."""
+    layers = [make(cuda_device, rows=1, q_heads=32, kv_heads=8, dim=128, page_tokens=64, tokens=65536,
+                   seed=900 + i) for i in range(3)]
+    shape = layers[0].shape
+    scratch, m, l, n = outputs_for(shape, cuda_device)
+    outs = [torch.empty(kvb.output_numerator_elements(shape), dtype=torch.float16, device=cuda_device)
+            for _ in layers]
+    inputs = [c.device_input() for c in layers]
+    stream = torch.cuda.Stream(device=cuda_device)
+    with torch.cuda.stream(stream):
+        for i, inp in enumerate(inputs):
+            kvb.launch_attention_ex(shape, inp, scratch, m, l, n, out_f16=outs[i])
+    torch.cuda.synchronize()
+    eager = [o.clone() for o in outs]
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for rep in range(8):
+            for i, inp in enumerate(inputs):
+                kvb.launch_attention_ex(shape, inp, scratch, m, l, n, out_f16=outs[i])
+    for o in outs:
+        o.zero_()
+    with torch.cuda.stream(stream):
+        for _ in range(10):
+            graph.replay()
+    torch.cuda.synchronize()
+    assert kvb.read_device_status() == 0, kvb.read_wait_failure()
+    for a, b in zip(outs, eager):
+        assert torch.equal(a, b)
