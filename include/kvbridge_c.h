@@ -127,6 +127,30 @@ int kvb_read_device_status(int* status);
  * Reading clears it. Returns the cudaError_t of the read. */
 int kvb_read_wait_failure(long long* record6);
 
+/* Decode call that allocates nothing. It has no counterpart in the
+ * reference. kvb_launch_attention_ex needs a caller-provided scratch buffer
+ * of scratch_elements(shape) floats; callers that cannot allocate device
+ * memory when they make the call - a serving loop whose HBM is fully
+ * reserved up front by its KV-cache allocator, or code that issues the call
+ * inside CUDA-graph stream capture, where cudaMalloc is not permitted - use
+ * this one instead. It is kvb_launch_attention_ex (same inputs, outputs,
+ * partitions and optional fp16 output) with the split-K partials kept in a
+ * static device array of KVB_NOALLOC_SCRATCH_FLOATS floats (2 MiB) that
+ * every GPU loading the library holds until process exit.
+ *   - Limits: the tensor-core geometry only (kvb_attention_b200_supported);
+ *     partitions are clamped so rows * q_heads * partitions * (dim + 2)
+ *     fits the array; larger shapes return KVB_EINVAL with a message.
+ *   - The first call on each device looks up the array's device address
+ *     (cudaGetSymbolAddress); make that first call outside stream capture.
+ *   - It calls no cudaMalloc, cudaFree or other allocating routine.
+ *   - All calls share the array: calls that can overlap on the GPU (other
+ *     streams, concurrent graph replays) race and must be serialised. No
+ *     part of the array needs clearing between calls. */
+#define KVB_NOALLOC_SCRATCH_FLOATS 524288
+int kvb_launch_attention_noalloc(const kvb_shape* s, const kvb_device_input* in,
+                                 unsigned partitions, float* m, float* l, float* n,
+                                 void* out_f16, void* stream);
+
 /* Host-side schedule of the split-K kernel, exported for tests: the CTA that
  * owns global stage `stage` when `total` stages are split over `ctas` CTAs. */
 uint32_t kvb_schedule_cta_of(uint64_t stage, uint64_t total, uint32_t ctas);

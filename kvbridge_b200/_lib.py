@@ -157,6 +157,10 @@ SIGNATURES = {
     "kvb_read_device_status": (c_int, [POINTER(c_int)]),
     "kvb_read_wait_failure": (c_int, [POINTER(ctypes.c_longlong)]),
     "kvb_schedule_cta_of": (c_uint32, [c_uint64, c_uint64, c_uint32]),
+    "kvb_launch_attention_noalloc": (
+        c_int,
+        [POINTER(KvbShape), POINTER(KvbDeviceInput), ctypes.c_uint, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p],
+    ),
 }
 
 _lib = None

@@ -510,4 +510,103 @@ cudaError_t read_wait_failure(long long* record6) {
   return cudaMemcpyToSymbol(kvb::g_kvb_first_failure, zeros, sizeof(zeros));
 }
 
+// ---------------------------------------------------------------------------
+// Decode call that allocates nothing (kvb_launch_attention_noalloc in
+// include/kvbridge_c.h). For callers that cannot obtain device memory at call
+// time - e.g. a serving loop whose every byte of HBM is pre-reserved by its
+// KV-cache allocator, or code running inside CUDA-graph stream capture, where
+// cudaMalloc is not permitted - the split-K partials live in this file-scope
+// device array instead of a caller-provided scratch buffer.
+//
+// Every GPU that loads the library holds the array (2 MiB) until process
+// exit. All calls share it and it keeps the last call's contents; nothing in
+// it needs to start at zero, because the partial kernel of a call writes
+// every slot that call's merge reads. Calls that may run concurrently on the
+// GPU (different streams, or graphs replayed in parallel) race on the array
+// and must be serialised by the caller.
+
+namespace {
+
+constexpr size_t kNoAllocScratchFloats = size_t(1) << 19;  // 2 MiB
+static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchFloats];
+
+// Device address of g_noalloc_scratch on the current device. In host code the
+// array's name is only a host-side stand-in, so the address is looked up with
+// cudaGetSymbolAddress once per device, with that device current, and cached.
+float* noalloc_scratch_on_current_device() {
+  static std::mutex mu;
+  static std::map<int, float*> cache;
+  int dev = 0;
+  cuda_ok(cudaGetDevice(&dev), "cudaGetDevice");
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = cache.find(dev);
+  if (it != cache.end()) return it->second;
+  void* ptr = nullptr;
+  cuda_ok(cudaGetSymbolAddress(&ptr, g_noalloc_scratch), "cudaGetSymbolAddress(static scratch)");
+  cache.emplace(dev, static_cast<float*>(ptr));
+  return static_cast<float*>(ptr);
+}
+
+}  // namespace
+
+namespace detail {
+
+void launch_attention_noalloc(const Shape& s, const DeviceInput& in, unsigned partitions,
+                              float* m, float* l, float* n, void* out_f16, cudaStream_t stream) {
+  validate_shape(s);
+  if (m == nullptr || l == nullptr || n == nullptr)
+    throw std::invalid_argument("m, l and n must be non-null device buffers");
+  check_inputs(s, in, m, m, l, n);  // input buffers; the scratch is internal
+  if (!attention_b200_supported(s, in))
+    throw std::invalid_argument(
+        "the no-allocation call needs the tensor-core geometry (attention_b200_supported)");
+  const size_t per_partition = size_t(s.rows) * s.q_heads * (size_t(s.dim) + 2);
+  const size_t fit = kNoAllocScratchFloats / per_partition;
+  if (fit == 0)
+    throw std::invalid_argument(
+        "rows * q_heads * (dim + 2) exceeds the 524288-float static scratch of the "
+        "no-allocation call");
+  uint32_t parts = attention_partitions(s, partitions);
+  parts = uint32_t(std::min<size_t>(parts, fit));
+  float* scratch = noalloc_scratch_on_current_device();
+  if (parts > 0) {
+    const uint32_t nt = (query_rows(s) + 7) / 8;
+    const FastVariant v = fast_variant(s.dim, nt);
+    kvb::DecodeParams prm{};
+    prm.q = in.q;
+    prm.q_positions = in.q_positions;
+    prm.k_positions = in.k_positions;
+    prm.table = in.page_table;
+    prm.k = static_cast<const int8_t*>(in.k);
+    prm.v = static_cast<const int8_t*>(in.v);
+    prm.k_scales = in.k_scales;
+    prm.v_scales = in.v_scales;
+    prm.seq_lens = nullptr;
+    prm.part = scratch;
+    prm.batch = 1;
+    prm.rows = s.rows;
+    prm.q_heads = s.q_heads;
+    prm.kv_heads = s.kv_heads;
+    prm.group = s.q_heads / s.kv_heads;
+    prm.qr = query_rows(s);
+    prm.page_tokens = s.page_tokens;
+    prm.log2_page = log2_exact(s.page_tokens);
+    prm.pages = s.pages;
+    prm.table_stride = 0;
+    prm.begin = s.begin;
+    prm.end = s.end;
+    prm.seg_stages = kvb::stages_of_range(s.begin, s.end);
+    prm.split_stride = parts;  // partials packed [row-head][partition]
+    prm.max_tokens = s.tokens;
+    prm.ctas = parts * s.kv_heads;
+    prm.total_stages = uint64_t(prm.seg_stages) * s.kv_heads;
+    prm.score_scale = s.scale;
+    v.launch(prm, stream);
+  }
+  launch_merge(kvb::kMergeScratch,
+               scratch_merge_params(s, scratch, parts, parts, false, m, l, n, out_f16), stream);
+}
+
+}  // namespace detail
+
 }  // namespace kvbridge

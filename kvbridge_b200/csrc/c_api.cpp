@@ -13,6 +13,11 @@
 #include "kvbridge_c.h"
 #include "kvb_schedule.h"
 
+namespace kvbridge::detail {
+void launch_attention_noalloc(const Shape&, const DeviceInput&, unsigned partitions, float* m,
+                              float* l, float* n, void* out_f16, cudaStream_t);
+}  // namespace kvbridge::detail
+
 namespace {
 
 thread_local std::string g_last_error;
@@ -238,6 +243,15 @@ int kvb_merge_attention_shards(unsigned shards, unsigned row_heads, unsigned dim
 int kvb_read_device_status(int* status) { return int(kvbridge::read_device_status(status)); }
 
 int kvb_read_wait_failure(long long* record6) { return int(kvbridge::read_wait_failure(record6)); }
+
+int kvb_launch_attention_noalloc(const kvb_shape* s, const kvb_device_input* in,
+                                 unsigned partitions, float* m, float* l, float* n,
+                                 void* out_f16, void* stream) {
+  return guarded([&] {
+    kvbridge::detail::launch_attention_noalloc(to_shape(s), to_input(in), partitions, m, l, n,
+                                               out_f16, as_stream(stream));
+  });
+}
 
 uint32_t kvb_schedule_cta_of(uint64_t stage, uint64_t total, uint32_t ctas) {
   if (total == 0 || ctas == 0 || stage >= total) return 0;
