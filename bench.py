@@ -66,6 +66,8 @@ def parse_args():
     ap.add_argument("--layers", type=int, default=4, help="resident KV layers rotated over steps")
     ap.add_argument("--graph-steps", type=int, default=100, help="calls captured per CUDA graph")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--config", choices=["cfg2", "cfg1", "cfg3", "cfg4", "cfg5"], default="cfg2",
+                    help="BASELINE workload; the headline line is cfg2, the others are informational")
     return ap.parse_args()
 
 
@@ -299,6 +301,8 @@ def main():
     rc = kvb.preload_attention_kernels()
     if rc != 0:
         raise RuntimeError(f"preload_attention_kernels failed: cudaError {rc}")
+    if args.config != "cfg2":
+        return run_other_config(args, world, rank, local_rank, device)
 
     # Resident KV layers of this rank.
     layers = []
@@ -532,6 +536,164 @@ def main():
     if rank == 0:
         print(json.dumps(line), flush=True)
     del g_call, g_partial, g_e2e
+    if world > 1:
+        dist.barrier(device_ids=[local_rank])
+        dist.destroy_process_group()
+    return 0
+
+
+# ---------------------------------------------------------------------------
+# Informational configurations (3, 4, 5).
+
+
+def run_other_config(args, world, rank, local_rank, device):
+    """cfg1: 4,096-token single call with 8 partitions. cfg3: ragged batch of
+    32 (lengths U[1024, 32768]) with the 8 KV heads split over the ranks.
+    cfg4: batch 64 x 16,384, 64 q / 8 kv heads, Page16, 1 % 10x outliers, KV
+    heads split over the ranks. cfg5: batch 4 x 1,048,576 tokens, sequence
+    split over the ranks; each rank's (m, l, n) partial is all-gathered and
+    merged with merge_attention_shards. Value = all ranks' KV bytes / time."""
+    import torch
+    import torch.distributed as dist
+
+    import kvbridge_b200 as kvb
+    from kvbridge_b200 import sharding, synth
+
+    stream = torch.cuda.Stream(device=device)
+    steps, warmup = args.steps, max(args.warmup, 3)
+    cfg = args.config
+    if cfg == "cfg1":
+        case = synth.make_single(rows=1, q_heads=32, kv_heads=8, dim=128, page_tokens=64, tokens=4096,
+                                 seed=0xC0FFEE + 1 + rank, device=device)
+        scratch = torch.empty(kvb.scratch_elements(case.shape), device=device)
+        m = torch.empty(32, device=device)
+        l = torch.empty(32, device=device)
+        n = torch.empty(32 * 128, device=device)
+        out = torch.empty(32 * 128, dtype=torch.float16, device=device)
+        inp = case.device_input()
+
+        def step(i):
+            kvb.launch_attention_ex(case.shape, inp, scratch, m, l, n, partitions=8, out_f16=out)
+
+        total_bytes = world * case.kv_bytes()
+        desc = dict(workload="cfg1: B1, 4,096 ctx, 32/8, dim 128, Page64 shuffled, 8 partitions",
+                    scaling="weak (one call per GPU)")
+        use_graph = True
+    elif cfg in ("cfg3", "cfg4"):
+        if cfg == "cfg3":
+            lens = synth.ragged_lengths(32, 1024, 32768, seed=0xC0FFEE + 3)
+            q_heads, kv_heads, page, outl = 32, 8, 64, 0.0
+        else:
+            lens = [16384] * 64
+            q_heads, kv_heads, page, outl = 64, 8, 16, 0.01
+        h0, h1 = sharding.kv_head_range(kv_heads, world, rank)
+        kv_local = h1 - h0
+        q_local = q_heads // kv_heads * kv_local
+        bc = synth.make_batched(q_local, kv_local, 128, page, lens, seed=0xC0FFEE + 10 * rank + (3 if cfg == "cfg3" else 4),
+                                device=device, outlier_frac=outl)
+        ws_bytes = kvb.batch_workspace_bytes(bc.shape)
+        ws = torch.empty(ws_bytes // 4 + 16, device=device)
+        B = bc.shape.batch
+        m = torch.empty(B * q_local, device=device)
+        l = torch.empty(B * q_local, device=device)
+        n = torch.empty(B * q_local * 128, device=device)
+        out = torch.empty(B * q_local * 128, dtype=torch.float16, device=device)
+        binp = bc.batch_input()
+
+        def step(i):
+            kvb.launch_attention_batched(bc.shape, binp, ws, ws_bytes, m, l, n, out)
+
+        total_bytes = sum(lens) * kv_heads * (2 * 128 + 8)
+        desc = dict(workload=f"{cfg}: batch {len(lens)}, {q_heads}/{kv_heads} heads, dim 128, Page{page}"
+                             + (", ragged U[1024,32768]" if cfg == "cfg3" else ", 16,384 ctx, 1% 10x outliers"),
+                    sharding=f"kv-heads: {kv_local} of {kv_heads} per GPU", scaling="strong")
+        use_graph = True
+    else:  # cfg5
+        tokens = 1 << 20
+        ranges = sharding.sequence_ranges(tokens, 64, world)
+        b0, b1 = ranges[rank]
+        local = b1 - b0
+        bc = synth.make_batched(32, 8, 128, 64, [local] * 4, seed=0xC0FFEE + 50 + rank, device=device)
+        ws_bytes = kvb.batch_workspace_bytes(bc.shape)
+        ws = torch.empty(ws_bytes // 4 + 16, device=device)
+        rh = 4 * 32
+        m = torch.empty(rh, device=device)
+        l = torch.empty(rh, device=device)
+        n = torch.empty(rh * 128, device=device)
+        binp = bc.batch_input()
+        merge = sharding.gpu_shard_merge(rh, 128)
+
+        def step(i):
+            kvb.launch_attention_batched(bc.shape, binp, ws, ws_bytes, m, l, n, None)
+            if world > 1:
+                mp, lp, np_ = sharding.all_gather_partials(m, l, n)
+                merge(mp, lp, np_.reshape(world, rh * 128))
+
+        total_bytes = 4 * tokens * 8 * (2 * 128 + 8)
+        desc = dict(workload="cfg5: batch 4 x 1,048,576 ctx, 32/8 heads, dim 128, Page64",
+                    sharding=f"sequence: {local} tokens of each sequence per GPU, NCCL all-gather "
+                             "of (m, l, n) + merge_attention_shards",
+                    scaling="strong")
+        use_graph = world == 1
+
+    def run(count):
+        with torch.cuda.stream(stream):
+            for i in range(count):
+                step(i)
+
+    run(2)
+    torch.cuda.synchronize()
+    graph = None
+    if use_graph:
+        gsteps = max(1, min(args.graph_steps, steps))
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            for i in range(gsteps):
+                step(i)
+
+        def run(count):  # noqa: F811 - graph replays from here on
+            full, rest = divmod(count, gsteps)
+            with torch.cuda.stream(stream):
+                for _ in range(full):
+                    graph.replay()
+                for i in range(rest):
+                    step(i)
+
+    run(warmup)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier(device_ids=[local_rank])
+    torch.cuda.synchronize()
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    run(steps)
+    b.record(stream)
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b)
+    if world > 1:
+        t = torch.tensor([ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    status = kvb.read_device_status()
+    if status != 0:
+        raise RuntimeError(f"kernel status word {status} ({kvb.read_wait_failure()}); numbers invalid")
+    per = ms / steps
+    peak, peak_kind = measured_peak()
+    value = total_bytes / (per / 1e3) / 1e9
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": steps,
+        "warmup": warmup, "ms_per_step": round(per, 6), "higher_is_better": True,
+        "scaling": desc.pop("scaling"), "vs_baseline": None, "dtype": "int8",
+        "data": "synthetic (seeded; BASELINE value distributions)",
+        "pct_of_hbm_peak_per_gpu": round(100 * value / world / peak, 2), "peak": f"{peak} GB/s ({peak_kind})",
+        "config": dict(desc, kv_bytes_per_step=total_bytes,
+                       launch="CUDA-graph replays" if graph is not None else "eager launches + NCCL"),
+        "informational": "not the headline workload (cfg2)",
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    del graph
     if world > 1:
         dist.barrier(device_ids=[local_rank])
         dist.destroy_process_group()

@@ -55,7 +55,8 @@ void merge_attention_ex(const Shape&, const float* scratch, unsigned partitions,
 // Ragged batch: sequence b attends its tokens [0, seq_lens[b]) (all visible;
 // the query is the next token). Logical page j of sequence b lives at physical
 // page block_table[b * table_stride + j] of the shared pool, whose K/V/scale
-// layout is the one of attention_common.h with `pages` physical pages.
+// layout is the one of attention_common.h with `pages` physical pages. Unlike
+// the single-sequence Shape, the pool may exceed 2^32 elements (64-bit offsets).
 struct BatchShape {
   uint32_t batch, q_heads, kv_heads, dim, page_tokens, pages, table_stride;
   uint32_t max_tokens;  // host-known upper bound of every seq_lens[b]

@@ -398,9 +398,10 @@ const char* batch_shape_error(const BatchShape& s) noexcept {
     return "max_tokens exceeds the block-table row capacity";
   if (!std::isfinite(s.scale)) return "score scale must be finite";
   if (uint64_t(s.batch) * s.q_heads > 0x7fffffffull) return "batch/head product too large";
+  // The batched kernel addresses the pool with 64-bit offsets; a pool is
+  // bounded only by device memory (kept below 2^48 bytes here).
   const uint64_t extent = uint64_t(s.pages) * s.kv_heads * s.page_tokens * s.dim;
-  if (extent > std::numeric_limits<uint32_t>::max())
-    return "physical KV extent exceeds 32-bit kernel offsets";
+  if (extent >= (uint64_t(1) << 48)) return "physical KV pool exceeds 2^48 bytes";
   if (uint64_t(s.batch) * s.table_stride > std::numeric_limits<uint32_t>::max())
     return "block table exceeds 32-bit indexing";
   return nullptr;

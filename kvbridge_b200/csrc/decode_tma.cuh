@@ -20,20 +20,23 @@
 //    (rows * group <= 8 * NT) sit in the narrow N dimension:
 //        S^T[token][qrow] = K[token][d] . Q^T[d][qrow]   (M = 16 tokens)
 //        O^T[d][qrow]     = V[d][token] . P[token][qrow]  (M = 16 dims)
-//    QK runs on the int8 MMA (m16n8k32 s8.s8.s32): K is used exactly as
-//    stored and each query row is a 22-bit fixed-point value split into
-//    three signed int8 limbs (q = L0 + 2^8 L1 + 2^16 L2, scaled by a power of
-//    two per row), so the dot products accumulate exactly in s32 and are
-//    combined in fp32. PV runs on the f16 MMA: V codes are widened to f16
-//    exactly in registers and P = w * vscale is f16. Per-token kscale
-//    multiplies the fp32 scores and per-token vscale rides on P, as in the
-//    reference MMA kernel. The QK accumulator fragments become the PV B
-//    operand through movmatrix (8x8 transposes), never touching shared
-//    memory, because the token order of the QK rows is chosen so that the
-//    PV A operand (V rows, token-contiguous) loads as one 16-byte word per row.
+//    Both run on the int8 MMA (m16n8k32, exact s32 accumulation) with K and
+//    V used exactly as stored. QK: each query row is a 22-bit fixed-point
+//    value split into three signed int8 limbs (q = L0 + 2^8 L1 + 2^16 L2,
+//    scaled by a power of two per row). PV: P = w * vscale is a 15-bit
+//    signed fixed-point value per (stage, column) split into a u8 low and an
+//    s8 high limb; the
+//    exact sums are folded into fp32 accumulators with the power-of-two
+//    scale. Per-token kscale multiplies the fp32 scores and per-token vscale
+//    rides on P, as in the reference MMA kernel. The QK accumulator
+//    fragments become the PV B operand through movmatrix (8x8 transposes of
+//    16-bit P pairs) and byte permutes, never touching shared memory, because
+//    the token order of the QK rows is chosen so that each thread's PV A
+//    operand is its own 16-byte word of each V row.
 //  * Precision: QK is exact up to the 2^-22 (relative to the row's largest
-//    |q|) rounding of Q. P is kept relative to a running power-of-two vscale
-//    exponent, so any finite vscale fits f16.
+//    |q|) rounding of Q; P is exact up to 2^-15 of the stage's largest |P|
+//    of the column (its power-of-two scale adapts per stage and column, so
+//    any finite vscale works).
 //  * Pieces end with an in-CTA log-sum-exp combine of the four warps'
 //    states and one (m, l, n) write per query row.
 #include "kvb_device.cuh"
@@ -295,7 +298,6 @@ struct WarpState {
   float acc[D / 16][NT][4];  // O^T fragments: rows d, columns = query rows
   float m[NT][2];            // running max (log2 units) of columns 2*tig+e
   float l[NT][2];            // thread-partial denominators
-  int ev;                    // running vscale exponent of acc
 };
 
 // Per-piece query operands of one warp: the three int8 limbs of every query
@@ -471,27 +473,17 @@ __device__ __forceinline__ void consume_stage(const DecodeParams& p, const uint8
       }
   }
 
-  // ---- vscale exponent of this stage (warp-uniform).
+  // ---- vscale of the stage's tokens (token t sits in lane t % 32, register
+  //      t / 32); tokens outside [lo, hi) read as 0 (their slots may hold
+  //      anything).
   float vs_lane[2];
-  {
-    float vmax = 0.f;
 #pragma unroll
-    for (int i = 0; i < 2; ++i) {
-      const uint32_t t = lane + 32 * i;
-      const bool in = full || (tb + t >= lo && tb + t < hi);
-      vs_lane[i] = in ? svs[t] : 0.f;
-      vmax = fmaxf(vmax, fabsf(vs_lane[i]));
-    }
-    vmax = warp_max(vmax);
-    int ev_stage = -100;
-    if (vmax > 0.f) ev_stage = max(-100, int((__float_as_uint(vmax) >> 23) & 0xffu) - 141);
-    const int ev_new = max(ws.ev, ev_stage);
-    const float ev_fac = __uint_as_float(uint32_t(127 + max(ws.ev - ev_new, -126)) << 23);
-    const float vmul = __uint_as_float(uint32_t(127 - ev_new) << 23);
-    ws.ev = ev_new;
-    vs_lane[0] *= vmul;
-    vs_lane[1] *= vmul;
-
+  for (int i = 0; i < 2; ++i) {
+    const uint32_t t = lane + 32 * i;
+    const bool in = full || (tb + t >= lo && tb + t < hi);
+    vs_lane[i] = in ? svs[t] : 0.f;
+  }
+  {
     // ---- online softmax update per column.
     bool rescale = false;
     float fac[NT][2];
@@ -520,8 +512,8 @@ __device__ __forceinline__ void consume_stage(const DecodeParams& p, const uint8
           lsum += w0 + w1;
         }
         ws.l[nt][e] = ws.l[nt][e] * alpha + lsum;
-        fac[nt][e] = alpha * ev_fac;
-        rescale |= fac[nt][e] != 1.f;
+        fac[nt][e] = alpha;
+        rescale |= alpha != 1.f;
       }
     if (__any_sync(0xffffffffu, rescale)) {
 #pragma unroll
@@ -536,30 +528,85 @@ __device__ __forceinline__ void consume_stage(const DecodeParams& p, const uint8
     }
   }
 
-  // ---- P = w * vscale * 2^-ev as f16, transposed into the PV B operand.
-  uint32_t pb[4][NT][2];
+  // ---- P = w * vscale in fp32, and per column the power of two that puts
+  //      the stage's largest |P| in [2^13, 2^14): pscale scales P into the
+  //      fixed point below, inv_pscale scales the exact sums back.
+  float pscale[NT][2], inv_pscale[NT][2];
+  {
+    float pmax[NT][2];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) pmax[nt][0] = pmax[nt][1] = 0.f;
+#pragma unroll
+    for (int s = 0; s < 4; ++s) {
+      const uint32_t t0 = 16 * (grp >> 1) + 4 * s + (grp & 1), t1 = t0 + 2;
+      const float v0a = __shfl_sync(0xffffffffu, vs_lane[0], t0 & 31);
+      const float v0b = __shfl_sync(0xffffffffu, vs_lane[1], t0 & 31);
+      const float v1a = __shfl_sync(0xffffffffu, vs_lane[0], t1 & 31);
+      const float v1b = __shfl_sync(0xffffffffu, vs_lane[1], t1 & 31);
+      const float vm0 = t0 < 32 ? v0a : v0b;
+      const float vm1 = t1 < 32 ? v1a : v1b;
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        sc[s][nt][0] *= vm0;
+        sc[s][nt][1] *= vm0;
+        sc[s][nt][2] *= vm1;
+        sc[s][nt][3] *= vm1;
+        pmax[nt][0] = fmaxf(pmax[nt][0], fmaxf(fabsf(sc[s][nt][0]), fabsf(sc[s][nt][2])));
+        pmax[nt][1] = fmaxf(pmax[nt][1], fmaxf(fabsf(sc[s][nt][1]), fabsf(sc[s][nt][3])));
+      }
+    }
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        float pm = pmax[nt][e];
+        pm = fmaxf(pm, __shfl_xor_sync(0xffffffffu, pm, 4));
+        pm = fmaxf(pm, __shfl_xor_sync(0xffffffffu, pm, 8));
+        pm = fmaxf(pm, __shfl_xor_sync(0xffffffffu, pm, 16));
+        // pm < 2^(x - 126) for biased exponent x; pscale = 2^(140 - x), kept
+        // a normal float (stages with |P| below ~2^-113 lose precision).
+        const int x = int((__float_as_uint(pm) >> 23) & 0xffu);
+        const int sh = max(-126, min(126, 140 - x));
+        pscale[nt][e] = pm > 0.f ? __uint_as_float(uint32_t(127 + sh) << 23) : 1.f;
+        inv_pscale[nt][e] = pm > 0.f ? __uint_as_float(uint32_t(127 - sh) << 23) : 1.f;
+      }
+  }
+
+  // ---- P as signed fixed point per (stage, column): u = rint(P * pscale),
+  //      |u| < 2^14, split into a u8 low limb and an s8 high limb
+  //      (u = 256 * hi + lo, two's complement). Rows grp/grp+8 of QK m-tile s
+  //      are packed as 16-bit pairs (columns 2*tig, 2*tig+1) and transposed
+  //      with movmatrix, so the thread then holds column grp of tokens
+  //      16*tig+4*s+{0,1} (t01) and 16*tig+4*s+{2,3} (t23).
+  uint32_t t01[4][NT], t23[4][NT];
 #pragma unroll
   for (int s = 0; s < 4; ++s) {
-    const uint32_t t0 = 16 * (grp >> 1) + 4 * s + (grp & 1), t1 = t0 + 2;
-    // vscale of token t sits in lane t % 32, register t / 32.
-    const float v0a = __shfl_sync(0xffffffffu, vs_lane[0], t0 & 31);
-    const float v0b = __shfl_sync(0xffffffffu, vs_lane[1], t0 & 31);
-    const float v1a = __shfl_sync(0xffffffffu, vs_lane[0], t1 & 31);
-    const float v1b = __shfl_sync(0xffffffffu, vs_lane[1], t1 & 31);
-    const float vm0 = t0 < 32 ? v0a : v0b;
-    const float vm1 = t1 < 32 ? v1a : v1b;
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
-      const uint32_t r0 = pack_half2(sc[s][nt][0] * vm0, sc[s][nt][1] * vm0);
-      const uint32_t r1 = pack_half2(sc[s][nt][2] * vm1, sc[s][nt][3] * vm1);
-      pb[s][nt][0] = transpose_8x8_b16(r0);
-      pb[s][nt][1] = transpose_8x8_b16(r1);
+      const uint32_t u00 = uint32_t(__float2int_rn(sc[s][nt][0] * pscale[nt][0]));
+      const uint32_t u01 = uint32_t(__float2int_rn(sc[s][nt][1] * pscale[nt][1]));
+      const uint32_t u10 = uint32_t(__float2int_rn(sc[s][nt][2] * pscale[nt][0]));
+      const uint32_t u11 = uint32_t(__float2int_rn(sc[s][nt][3] * pscale[nt][1]));
+      t01[s][nt] = transpose_8x8_b16(__byte_perm(u00, u01, 0x5410));
+      t23[s][nt] = transpose_8x8_b16(__byte_perm(u10, u11, 0x5410));
     }
   }
 
-  // ---- O^T += V P. PV k-step s pairs k = 2*tig+{0,1} with tokens
-  //      16*tig+4*s+{0,1} and k = 2*tig+8+{0,1} with tokens 16*tig+4*s+{2,3}:
-  //      word s of the thread's 16-byte slice of V row d.
+  // ---- O^T += V P on the int8 MMA (m16n8k32: s8 V x u8 low / s8 high P
+  //      limbs, exact s32).
+  //      k-step ks covers QK m-tiles 2ks (k = 4*tig + j) and 2ks+1
+  //      (k = 16 + 4*tig + j), i.e. tokens 16*tig + 8*ks + [0,8): words 2ks
+  //      and 2ks+1 of the thread's 16-byte slice of each V row, used as stored.
+  uint32_t blo[2][NT][2], bhi[2][NT][2];
+#pragma unroll
+  for (int ks = 0; ks < 2; ++ks)
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        blo[ks][nt][h] = __byte_perm(t01[2 * ks + h][nt], t23[2 * ks + h][nt], 0x6420);
+        bhi[ks][nt][h] = __byte_perm(t01[2 * ks + h][nt], t23[2 * ks + h][nt], 0x7531);
+      }
   const uint32_t P = p.page_tokens;
   const uint32_t vpitch = v_page_pitch(D, P);
   const uint8_t* vslice = sv + ((16 * tig) >> p.log2_page) * vpitch + ((16 * tig) & (P - 1));
@@ -571,13 +618,20 @@ __device__ __forceinline__ void consume_stage(const DecodeParams& p, const uint8
     const uint32_t wa[4] = {va.x, va.y, va.z, va.w};
     const uint32_t wb[4] = {vb.x, vb.y, vb.z, vb.w};
 #pragma unroll
-    for (int s = 0; s < 4; ++s) {
-      uint32_t a0, a1, a2, a3;
-      int8x4_to_f16x4(wa[s], a0, a2);
-      int8x4_to_f16x4(wb[s], a1, a3);
+    for (int nt = 0; nt < NT; ++nt) {
+      int lo[4] = {0, 0, 0, 0}, hi[4] = {0, 0, 0, 0};
 #pragma unroll
-      for (int nt = 0; nt < NT; ++nt)
-        mma_16816(ws.acc[md][nt], a0, a1, a2, a3, pb[s][nt][0], pb[s][nt][1]);
+      for (int ks = 0; ks < 2; ++ks) {
+        imma_16832_s8u8(lo, wa[2 * ks], wb[2 * ks], wa[2 * ks + 1], wb[2 * ks + 1], blo[ks][nt][0],
+                        blo[ks][nt][1]);
+        imma_16832(hi, wa[2 * ks], wb[2 * ks], wa[2 * ks + 1], wb[2 * ks + 1], bhi[ks][nt][0],
+                   bhi[ks][nt][1]);
+      }
+      // |lo| <= 64 * 128 * 255 and |hi| <= 64 * 128 * 64, so hi * 256 + lo
+      // (< 2^28) is exact in s32.
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        ws.acc[md][nt][i] = fmaf(float(hi[i] * 256 + lo[i]), inv_pscale[nt][i & 1], ws.acc[md][nt][i]);
     }
   }
 }
@@ -645,7 +699,6 @@ __global__ void __launch_bounds__(kDecodeThreads, 2) decode_partial_kernel(Decod
       ws.m[nt][0] = ws.m[nt][1] = -INFINITY;
       ws.l[nt][0] = ws.l[nt][1] = 0.f;
     }
-    ws.ev = -100;
 
     const uint32_t n = pc.j1 - pc.j0;
     const uint32_t first = (warp + kConsumerWarps - g_base % kConsumerWarps) % kConsumerWarps;
@@ -670,7 +723,6 @@ __global__ void __launch_bounds__(kDecodeThreads, 2) decode_partial_kernel(Decod
     g_base += n;
 
     // ---- flush this warp's state.
-    const float ev_scale = __uint_as_float(uint32_t(127 + ws.ev) << 23);
     float* cw = combine + size_t(warp) * L::kCols * L::kPitch;
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
@@ -687,8 +739,8 @@ __global__ void __launch_bounds__(kDecodeThreads, 2) decode_partial_kernel(Decod
         }
 #pragma unroll
         for (int md = 0; md < D / 16; ++md) {
-          cw[col * L::kPitch + 16 * md + grp] = ws.acc[md][nt][e] * ev_scale;
-          cw[col * L::kPitch + 16 * md + grp + 8] = ws.acc[md][nt][2 + e] * ev_scale;
+          cw[col * L::kPitch + 16 * md + grp] = ws.acc[md][nt][e];
+          cw[col * L::kPitch + 16 * md + grp + 8] = ws.acc[md][nt][2 + e];
         }
       }
     if (x + n >= x1) grid_launch_dependents();

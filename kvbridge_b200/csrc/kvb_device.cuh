@@ -191,6 +191,15 @@ __device__ __forceinline__ void imma_16832(int (&d)[4], uint32_t a0, uint32_t a1
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+// D += A * B for one m16n8k32 tile, s8 A and u8 B, exact s32 accumulators.
+__device__ __forceinline__ void imma_16832_s8u8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                                uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.u8.s32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
 // Transpose an 8x8 b16 matrix held one row-pair per lane (lane holds row
 // lane/4, columns 2*(lane%4) and +1) into the same fragment of its transpose.
 __device__ __forceinline__ uint32_t transpose_8x8_b16(uint32_t x) {

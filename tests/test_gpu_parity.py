@@ -338,3 +338,40 @@ def test_pipeline_graph_replay_stress(cuda_device):
     assert kvb.read_device_status() == 0, kvb.read_wait_failure()
     for a, b in zip(outs, eager):
         assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("name", __import__("golden_util").golden_names())
+def test_golden_vectors(cuda_device, name):
+    """The committed golden vectors (expected outputs computed by the
+    reference's own FP64 oracle) through the C ABI."""
+    from golden_util import load
+
+    g = load(name)
+    s = kvb.Shape(**g["shape"])
+    dev = cuda_device
+    case = synth.SingleCase(
+        s, torch.from_numpy(g["q"]).to(dev), torch.from_numpy(g["q_positions"]).to(dev),
+        torch.from_numpy(g["k_positions"]).to(dev),
+        torch.from_numpy(g["page_table"].astype(np.int64)).to(torch.int32).to(dev),
+        torch.from_numpy(g["k"]).to(dev), torch.from_numpy(g["v"]).to(dev),
+        torch.from_numpy(g["k_scales"]).to(dev), torch.from_numpy(g["v_scales"]).to(dev))
+    for api in ("ex", "ref"):
+        res = run_single(case, fp16_out=(api == "ex"), api=api)
+        ref = {"normalized": g["normalized"], "visible": g["visible"],
+               "m": None, "l": None}
+        got = normalized(res, s)
+        vis = res["l"].numpy().reshape(s.rows, s.q_heads) > 0
+        assert np.array_equal(vis, g["visible"]), name
+        ma, rl = errors(got, g["normalized"])
+        assert ma <= MAX_ABS and rl <= REL_L2, (name, api, ma, rl)
+
+
+def test_negative_and_mixed_sign_v_scales(cuda_device):
+    """The contract asks for finite scales only; negative V scales flip the
+    sign of P, which the signed fixed-point P limbs carry."""
+    case = make(cuda_device, rows=1, q_heads=32, kv_heads=8, dim=128, page_tokens=32, tokens=3000, seed=61)
+    flip = torch.rand(case.v_scales.shape, generator=torch.Generator(device=cuda_device).manual_seed(5),
+                      device=cuda_device) < 0.3
+    case.v_scales[flip] *= -1.0
+    res = run_single(case)
+    check_against_oracle(res, case.shape, oracle.reference_case(case, threads=8), "neg-vscale")
