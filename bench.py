@@ -499,9 +499,11 @@ def main():
             l2="inputs larger than L2: each step reads another of the resident KV layers "
                f"({len(layers)} x {nbytes / 1e6:.1f} MB)",
             sharding=f"kv-heads: {8 * world} KV heads, 8 per GPU" if world > 1 else "single GPU",
-            launch="CUDA-graph replay of launch_attention_ex (partial + LSE merge + fp16 epilogue)",
+            launch="CUDA-graph replay of launch_attention_ex (partial kernel, then LSE merge kernel with "
+                   "the fp16 epilogue; programmatic dependent launch between them)",
             compute="QK: int8 mma.sync m16n8k32 on raw K codes x 3 int8 limbs of Q (exact s32); "
-                    "PV: f16 mma.sync m16n8k16 on exactly widened V codes, fp32 accumulation",
+                    "PV: int8 mma.sync m16n8k32 on raw V codes x 2 int8 limbs of 14-bit fixed-point "
+                    "P = softmax weight x V scale (exact s32), fp32 accumulation",
         ),
         "roofline": {
             "bound": "hbm",

@@ -284,18 +284,15 @@ cudaError_t preload_attention_kernels() {
   return code == cudaSuccess ? preload_attention_mma_kernels() : code;
 }
 
-unsigned launch_attention_partials(const Shape& s, const DeviceInput& in, unsigned partitions,
-                                   float* scratch, cudaStream_t stream) {
-  if (scratch == nullptr) throw std::invalid_argument("scratch must be a non-null device buffer");
-  detail::check_inputs(s, in, scratch, scratch, scratch, scratch);
-  if (!attention_b200_supported(s, in))
-    throw std::invalid_argument("launch_attention_partials needs the tensor-core geometry "
-                                "(attention_b200_supported)");
-  const uint32_t splits = split_count(s);
-  const uint32_t parts = attention_partitions(s, partitions);
-  if (parts == 0) return 0;
-  const uint32_t nt = (query_rows(s) + 7) / 8;
-  const FastVariant v = fast_variant(s.dim, nt);
+namespace {
+
+// Stages per CTA prefetched into L2 while the preceding grid finishes.
+constexpr uint32_t kPrefetchStages = 4;
+
+// Kernel parameters of the single-sequence tensor-core path; partials go to
+// `scratch` with `split_stride` slots per row-head.
+kvb::DecodeParams single_params(const Shape& s, const DeviceInput& in, uint32_t parts,
+                                float* scratch, uint32_t split_stride) {
   kvb::DecodeParams prm{};
   prm.q = in.q;
   prm.q_positions = in.q_positions;
@@ -320,12 +317,30 @@ unsigned launch_attention_partials(const Shape& s, const DeviceInput& in, unsign
   prm.begin = s.begin;
   prm.end = s.end;
   prm.seg_stages = kvb::stages_of_range(s.begin, s.end);
-  prm.split_stride = splits;
+  prm.split_stride = split_stride;
   prm.max_tokens = s.tokens;
   prm.ctas = parts * s.kv_heads;
   prm.total_stages = uint64_t(prm.seg_stages) * s.kv_heads;
   prm.score_scale = s.scale;
-  v.launch(prm, stream);
+  return prm;
+}
+
+}  // namespace
+
+unsigned launch_attention_partials(const Shape& s, const DeviceInput& in, unsigned partitions,
+                                   float* scratch, cudaStream_t stream) {
+  if (scratch == nullptr) throw std::invalid_argument("scratch must be a non-null device buffer");
+  detail::check_inputs(s, in, scratch, scratch, scratch, scratch);
+  if (!attention_b200_supported(s, in))
+    throw std::invalid_argument("launch_attention_partials needs the tensor-core geometry "
+                                "(attention_b200_supported)");
+  const uint32_t splits = split_count(s);
+  const uint32_t parts = attention_partitions(s, partitions);
+  if (parts == 0) return 0;
+  const uint32_t nt = (query_rows(s) + 7) / 8;
+  kvb::DecodeParams prm = single_params(s, in, parts, scratch, splits);
+  prm.prefetch_stages = kPrefetchStages;
+  fast_variant(s.dim, nt).launch(prm, stream);
   return parts;
 }
 

@@ -64,6 +64,9 @@ struct DecodeParams {
   uint32_t ctas;
   uint64_t total_stages;  // single sequence only (batched computes it)
   float score_scale;
+  // Single sequence: L2 prefetch of the CTA's first `prefetch_stages` stages
+  // before the dependency wait on the preceding grid (0 = none).
+  uint32_t prefetch_stages;
 };
 
 constexpr int kConsumerWarps = 4;
@@ -204,6 +207,35 @@ __device__ __forceinline__ uint64_t piece_end_stage(const DecodeParams& p, const
 // ---------------------------------------------------------------------------
 // Producer: one warp, bulk copies of whole pages.
 
+// Single sequence, before the dependency wait on the preceding grid: L2
+// prefetch of the K/V pages and scales of the CTA's first `count` stages.
+// The preceding grid may still be writing the page table or the pages, so
+// nothing read here is used as data: table entries only steer prefetches
+// (read through L2, so that no stale copy stays in L1), out-of-range entries
+// are skipped, and the copies proper re-read everything after the wait.
+template <int D>
+__device__ void prefetch_first_stages(const DecodeParams& p, uint64_t x0, uint64_t x1,
+                                      uint32_t count) {
+  const uint32_t lane = threadIdx.x & 31;
+  const Piece pc = locate_piece(p, x0, x1, p.total_stages, blockIdx.x);
+  const uint32_t first_stage = pc.lo / kStageTokens;
+  const uint32_t j_end = min(pc.j1, pc.j0 + count);
+  const uint32_t tok_lo = max(pc.lo, (first_stage + pc.j0) * kStageTokens);
+  const uint32_t tok_hi = min(pc.hi, (first_stage + j_end) * kStageTokens);
+  if (tok_hi <= tok_lo) return;
+  const uint32_t P = p.page_tokens;
+  const uint32_t pg1 = (tok_hi - 1) >> p.log2_page;
+  for (uint32_t pg = (tok_lo >> p.log2_page) + lane; pg <= pg1; pg += 32) {
+    const uint32_t phys = __ldcg(p.table + pg);
+    if (phys >= p.pages) continue;
+    const size_t unit = size_t(phys) * p.kv_heads + pc.h;
+    prefetch_l2(p.k + unit * P * D, P * D);
+    prefetch_l2(p.v + unit * D * P, D * P);
+    prefetch_l2(p.k_scales + unit * P, 4 * P);
+    prefetch_l2(p.v_scales + unit * P, 4 * P);
+  }
+}
+
 template <int D, int STAGES>
 __device__ void produce(const DecodeParams& p, uint8_t* ring, uint64_t* full, uint64_t* empty,
                         volatile uint32_t* tags, volatile int* abort_flag, uint64_t x0, uint64_t x1,
@@ -213,68 +245,89 @@ __device__ void produce(const DecodeParams& p, uint8_t* ring, uint64_t* full, ui
   const uint32_t P = p.page_tokens;
   const uint32_t page_bytes = 2u * P * D + 8u * P;
   const uint32_t vpitch = v_page_pitch(D, P);
+  // Work is handed out 8 pages at a time, four lanes per page: lane l
+  // copies part l % 4 (K, V, K scales, V scales) of page l / 4 of the batch.
+  // A batch covers spb stages of pps pages each. Table entries, page checks
+  // and copy addresses are worked out for the whole batch at once, so that
+  // issuing a stage is only: wait for its slot, arm its barrier, and one
+  // warp instruction that starts all of the stage's copies.
+  const uint32_t pps = kStageTokens >> p.log2_page;  // 1, 2 or 4
+  const uint32_t spb = 8u / pps;
+  const uint32_t lane_page = lane >> 2, part = lane & 3;
+  const uint32_t lane_stage = lane_page / pps;
+  const uint32_t page_in_stage = lane_page - lane_stage * pps;
+  uint32_t part_bytes, dst_off;
+  if (part == 0) {
+    part_bytes = P * D;
+    dst_off = StageLayout<D>::kK + page_in_stage * P * D;
+  } else if (part == 1) {
+    part_bytes = D * P;
+    dst_off = StageLayout<D>::kV + page_in_stage * vpitch;
+  } else {
+    part_bytes = 4 * P;
+    dst_off = (part == 2 ? StageLayout<D>::kKs : StageLayout<D>::kVs) + page_in_stage * P * 4;
+  }
   uint32_t g = 0;  // stages issued so far (CTA stage sequence number)
   bool failed = false;
   for (uint64_t x = x0; x < x1 && !failed;) {
     const Piece pc = locate_piece(p, x, x1, total, blockIdx.x);
     const uint32_t first_stage = pc.lo / kStageTokens;
-    const uint32_t tok_lo = max(pc.lo, (first_stage + pc.j0) * kStageTokens);
-    const uint32_t tok_hi = min(pc.hi, (first_stage + pc.j1) * kStageTokens);
-    const uint32_t page_last = (tok_hi - 1) >> p.log2_page;
+    const uint32_t page_lo = max(pc.lo, (first_stage + pc.j0) * kStageTokens) >> p.log2_page;
+    const uint32_t page_hi = (min(pc.hi, (first_stage + pc.j1) * kStageTokens) - 1) >> p.log2_page;
     const uint32_t* trow =
         p.seq_lens == nullptr ? p.table : p.table + size_t(pc.b) * p.table_stride;
-    // Register window of page-table entries: cur = [wb, wb+32), nxt = [wb+32, wb+64).
-    uint32_t wb = tok_lo >> p.log2_page;
-    uint32_t cur = (wb + lane <= page_last) ? __ldg(trow + wb + lane) : 0u;
-    uint32_t nxt = (wb + 32 + lane <= page_last) ? __ldg(trow + wb + 32 + lane) : 0u;
-    for (uint32_t j = pc.j0; j < pc.j1; ++j) {
-      const uint32_t slot = g % STAGES;
-      const uint32_t use = g / STAGES;
-      if (mbar_wait_bounded(&empty[slot], (use & 1u) ^ 1u, abort_flag, kStatusEmptyWaitTimeout,
-                            int(g)) != kWaitOk) {
-        failed = true;
-        break;
-      }
-      const uint32_t tb = (first_stage + j) * kStageTokens;
-      const uint32_t vlo = max(tb, pc.lo), vhi = min(tb + kStageTokens, pc.hi);
-      const uint32_t p0 = vlo >> p.log2_page, p1 = (vhi - 1) >> p.log2_page;
-      while (p0 >= wb + 32) {
-        cur = nxt;
-        wb += 32;
-        nxt = (wb + 32 + lane <= page_last) ? __ldg(trow + wb + 32 + lane) : 0u;
-      }
-      const uint32_t npages = p1 - p0 + 1;
-      const uint32_t idx = (lane < npages) ? (p0 + lane - wb) : 0u;
-      const uint32_t from_cur = __shfl_sync(0xffffffffu, cur, idx & 31u);
-      const uint32_t from_nxt = __shfl_sync(0xffffffffu, nxt, idx & 31u);
-      const uint32_t phys = idx < 32 ? from_cur : from_nxt;
-      const bool mine = lane < npages;
+    // This lane's page of the batch starting at stage j, if the piece reads it.
+    auto batch_page = [&](uint32_t j, uint32_t& pg) {
+      pg = (first_stage + j) * pps + lane_page;
+      return j < pc.j1 && pg >= page_lo && pg <= page_hi;
+    };
+    uint32_t pg;
+    bool mine = batch_page(pc.j0, pg);
+    uint32_t cur = mine ? __ldg(trow + pg) : 0u;
+    bool in_nxt = batch_page(pc.j0 + spb, pg);
+    uint32_t nxt = in_nxt ? __ldg(trow + pg) : 0u;
+    for (uint32_t jb = pc.j0; jb < pc.j1 && !failed; jb += spb) {
+      const uint32_t phys = cur;
       const bool ok = mine && phys < p.pages;
-      const uint32_t okmask = __ballot_sync(0xffffffffu, ok);
       if (__ballot_sync(0xffffffffu, mine && !ok) && lane == 0)
         atomicMax(&g_kvb_status, kStatusBadPage);
-      if (lane == 0) {
-        // The slot is free, so its full barrier has completed the phase of
-        // stage g - STAGES; publishing g tells the consumer of stage g that
-        // the barrier's parity now refers to stage g (see the consumer loop).
-        tags[slot] = g;
-        mbar_arrive_expect_tx(&full[slot], __popc(okmask) * page_bytes);
+      const uint32_t okmask = __ballot_sync(0xffffffffu, ok && part == 0);
+      // Table entries two batches ahead, so that they are in registers in time.
+      cur = nxt;
+      mine = in_nxt;
+      in_nxt = batch_page(jb + 2 * spb, pg);
+      nxt = in_nxt ? __ldg(trow + pg) : 0u;
+      const size_t unit = size_t(ok ? phys : 0u) * p.kv_heads + pc.h;  // (page, kv head)
+      const uint8_t* src;
+      if (part == 0)
+        src = reinterpret_cast<const uint8_t*>(p.k + unit * P * D);
+      else if (part == 1)
+        src = reinterpret_cast<const uint8_t*>(p.v + unit * D * P);
+      else
+        src = reinterpret_cast<const uint8_t*>((part == 2 ? p.k_scales : p.v_scales) + unit * P);
+      const uint32_t nstages = min(spb, pc.j1 - jb);
+      for (uint32_t sb = 0; sb < nstages; ++sb) {
+        const uint32_t slot = g % STAGES;
+        const uint32_t use = g / STAGES;
+        if (mbar_wait_bounded(&empty[slot], (use & 1u) ^ 1u, abort_flag, kStatusEmptyWaitTimeout,
+                              int(g)) != kWaitOk) {
+          failed = true;
+          break;
+        }
+        if (lane == 0) {
+          // The slot is free, so its full barrier has completed the phase of
+          // stage g - STAGES; publishing g tells the consumer of stage g that
+          // the barrier's parity now refers to stage g (see the consumer loop).
+          tags[slot] = g;
+          const uint32_t stage_lanes = (pps == 4 ? 0xffffu : (1u << (4 * pps)) - 1u) << (4 * pps * sb);
+          mbar_arrive_expect_tx(&full[slot], __popc(okmask & stage_lanes) * page_bytes);
+        }
+        __syncwarp();
+        if (ok && lane_stage == sb)
+          bulk_copy_g2s(ring + size_t(slot) * StageLayout<D>::kBytes + dst_off, src, part_bytes,
+                        &full[slot], policy);
+        ++g;
       }
-      __syncwarp();
-      if (ok) {
-        uint8_t* st = ring + size_t(slot) * StageLayout<D>::kBytes;
-        const uint32_t in_stage = (p0 + lane) * P - tb;  // first token of the page in the stage
-        const size_t unit = size_t(phys) * p.kv_heads + pc.h;  // (page, kv head)
-        bulk_copy_g2s(st + StageLayout<D>::kK + in_stage * D, p.k + unit * P * D, P * D,
-                      &full[slot], policy);
-        bulk_copy_g2s(st + StageLayout<D>::kV + (in_stage >> p.log2_page) * vpitch,
-                      p.v + unit * D * P, D * P, &full[slot], policy);
-        bulk_copy_g2s(st + StageLayout<D>::kKs + in_stage * 4, p.k_scales + unit * P, 4 * P,
-                      &full[slot], policy);
-        bulk_copy_g2s(st + StageLayout<D>::kVs + in_stage * 4, p.v_scales + unit * P, 4 * P,
-                      &full[slot], policy);
-      }
-      ++g;
     }
     x = piece_end_stage(p, pc, x);
   }
@@ -659,6 +712,10 @@ __global__ void __launch_bounds__(kDecodeThreads, 2) decode_partial_kernel(Decod
     fence_barrier_init();
   }
   __syncthreads();
+  if (warp == kProducerWarp && p.prefetch_stages != 0 && p.seq_lens == nullptr)
+    prefetch_first_stages<D>(p, cta_stage_begin(blockIdx.x, p.total_stages, p.ctas),
+                             cta_stage_begin(blockIdx.x + 1, p.total_stages, p.ctas),
+                             p.prefetch_stages);
   // Inputs may be produced by the preceding kernel on the stream.
   grid_dependency_wait();
 

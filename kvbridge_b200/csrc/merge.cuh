@@ -73,6 +73,9 @@ __global__ void __launch_bounds__(32 * kMergeWarps) merge_kernel(MergeParams p) 
   __shared__ float red_m[kMergeWarps];
   __shared__ float red_l[kMergeWarps];
   __shared__ float red_n[kMergeWarps][256];
+  // The next kernel on the stream may start its prologue now; its own
+  // dependency wait still waits for this grid to finish.
+  grid_launch_dependents();
   grid_dependency_wait();
   const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const uint32_t rh = blockIdx.x;
@@ -154,10 +157,13 @@ __global__ void __launch_bounds__(32 * kMergeWarps) merge_kernel(MergeParams p) 
     for (int k = 0; k < kMaxK; ++k) acc[k] *= alpha;
 #pragma unroll
     for (int j = 0; j < kPerWarp; ++j) {
-      const float e = lv[j] > 0.f ? expf(mv[j] - mnew) : 0.f;
+      // A partial with l = 0 contributes nothing; its n is not read (an
+      // empty-split marker leaves n undefined).
+      const bool live = lv[j] > 0.f;
+      const float e = live ? expf(mv[j] - mnew) : 0.f;
       Lw = fmaf(e, lv[j], Lw);
 #pragma unroll
-      for (int k = 0; k < kMaxK; ++k) acc[k] = fmaf(e, nv[j][k], acc[k]);
+      for (int k = 0; k < kMaxK; ++k) acc[k] = live ? fmaf(e, nv[j][k], acc[k]) : acc[k];
     }
     M = mnew;
   }

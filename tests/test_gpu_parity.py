@@ -82,14 +82,19 @@ def test_reference_self_test_cases(cuda_device, name, kw, page_tokens):
         (1, 16, 2, 64, None),  # dim 64
         (2, 8, 4, 64, [600, 1499]),  # dim 64, two rows
         (1, 32, 4, 256, None),  # dim 256
+        (1, 32, 32, 64, None),  # group 1, 32 KV heads
     ],
 )
-def test_geometries(cuda_device, rows, q_heads, kv_heads, dim, qpos):
+@pytest.mark.parametrize("partitions", [0, 3])
+def test_geometries(cuda_device, rows, q_heads, kv_heads, dim, qpos, partitions):
+    """Auto partitions (= split_count here) and three partitions (fewer than
+    split_count: the merge also marks the unused splits empty)."""
     case = make(cuda_device, rows=rows, q_heads=q_heads, kv_heads=kv_heads, dim=dim, page_tokens=32,
                 tokens=1500, seed=rows * 100 + dim, q_positions=qpos)
     assert kvb.attention_b200_supported(case.shape, case.device_input())
-    res = run_single(case)
-    check_against_oracle(res, case.shape, oracle.reference_case(case, threads=8), f"{rows}x{q_heads}/{kv_heads}d{dim}")
+    res = run_single(case, partitions=partitions)
+    check_against_oracle(res, case.shape, oracle.reference_case(case, threads=8),
+                         f"{rows}x{q_heads}/{kv_heads}d{dim}/P{partitions}")
 
 
 def test_outlier_scales_page16_gqa8(cuda_device):
@@ -375,3 +380,83 @@ def test_negative_and_mixed_sign_v_scales(cuda_device):
     case.v_scales[flip] *= -1.0
     res = run_single(case)
     check_against_oracle(res, case.shape, oracle.reference_case(case, threads=8), "neg-vscale")
+
+
+def _scratch_garbage(shape, device, seed):
+    """A scratch full of arbitrary bit patterns (NaNs and infinities included)."""
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    bits = torch.randint(-2**31, 2**31 - 1, (kvb.scratch_elements(shape),), generator=g, dtype=torch.int32)
+    return bits.view(torch.float32).to(device)
+
+
+def _close(a, b):
+    """Same partials merged over more (empty) splits: equal to fp32 rounding."""
+    return torch.allclose(a, b, rtol=1e-5, atol=1e-6 * float(b.abs().max()))
+
+
+def test_uninitialised_scratch_repeats_and_full_remerge(cuda_device):
+    """An arbitrary initial scratch (NaN and infinity bit patterns included),
+    repeated calls on the same scratch and the two halves called separately
+    (partials, then merge_attention_ex) all agree bit for bit; merge_attention
+    over all split_count splits of the scratch afterwards (live partials plus
+    the empty-split markers, whose n is left undefined) reproduces the
+    result."""
+    case = make(cuda_device, rows=1, q_heads=32, kv_heads=8, dim=128, page_tokens=64, tokens=16384, seed=77)
+    shape = case.shape
+    splits = kvb.split_count(shape)
+    inp = case.device_input()
+    assert kvb.attention_partitions(shape, 0) < splits
+    ref = oracle.reference_case(case, threads=8)
+    results = []
+    for seed in (1, 2):
+        scratch = _scratch_garbage(shape, cuda_device, seed)
+        _, m, l, n = outputs_for(shape, cuda_device)
+        out = torch.empty(kvb.output_numerator_elements(shape), dtype=torch.float16, device=cuda_device)
+        for _ in range(3):
+            kvb.launch_attention_ex(shape, inp, scratch, m, l, n, out_f16=out)
+            torch.cuda.synchronize()
+            res = {"m": m.cpu(), "l": l.cpu(), "n": n.cpu(), "out": out.cpu()}
+            check_against_oracle(res, shape, ref, "garbage-scratch")
+            results.append(res)
+        # Re-merge everything the scratch holds (live partials + empty markers).
+        _, m2, l2, n2 = outputs_for(shape, cuda_device)
+        kvb.merge_attention(shape, scratch, splits, m2, l2, n2)
+        torch.cuda.synchronize()
+        assert torch.equal(m2.cpu(), res["m"])
+        assert _close(l2.cpu(), res["l"]) and _close(n2.cpu(), res["n"])
+    for r in results[1:]:
+        for k in ("m", "l", "n", "out"):
+            assert torch.equal(r[k], results[0][k]), k
+    # The two halves called separately.
+    scratch, m3, l3, n3 = outputs_for(shape, cuda_device)
+    parts = kvb.launch_attention_partials(shape, inp, scratch)
+    kvb.merge_attention_ex(shape, scratch, parts, m3, l3, n3)
+    torch.cuda.synchronize()
+    for k, v in (("m", m3), ("l", l3), ("n", n3)):
+        assert torch.equal(v.cpu(), results[0][k]), k
+
+
+def test_independent_streams(cuda_device):
+    """Calls on two streams with their own scratch buffers run concurrently
+    without sharing state: interleaved launches reproduce each case's own
+    result bit for bit."""
+    cases = [make(cuda_device, rows=1, q_heads=32, kv_heads=8, dim=128, page_tokens=64, tokens=32768,
+                  seed=500 + i) for i in range(2)]
+    shape = cases[0].shape
+    bufs = [outputs_for(shape, cuda_device) for _ in cases]
+    outs = [torch.empty(kvb.output_numerator_elements(shape), dtype=torch.float16, device=cuda_device)
+            for _ in cases]
+    for c, (sc, m, l, n), o in zip(cases, bufs, outs):
+        kvb.launch_attention_ex(shape, c.device_input(), sc, m, l, n, out_f16=o)
+    torch.cuda.synchronize()
+    expect = [o.clone() for o in outs]
+    for o in outs:
+        o.zero_()
+    streams = [torch.cuda.Stream(device=cuda_device) for _ in cases]
+    for _ in range(20):
+        for c, (sc, m, l, n), o, st in zip(cases, bufs, outs, streams):
+            with torch.cuda.stream(st):
+                kvb.launch_attention_ex(shape, c.device_input(), sc, m, l, n, out_f16=o)
+    torch.cuda.synchronize()
+    for o, e in zip(outs, expect):
+        assert torch.equal(o, e)
