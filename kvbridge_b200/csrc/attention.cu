@@ -147,18 +147,26 @@ uint32_t log2_exact(uint32_t x) {
 // ---------------------------------------------------------------------------
 // Merge launches.
 
+// The merge kernel for a layout and a head dim (dims per lane 2, 4 or 8).
+template <int KD>
+const void* merge_fn_kd(int mode) {
+  if (mode == kvb::kMergeScratch)
+    return reinterpret_cast<const void*>(&kvb::merge_kernel<kvb::kMergeScratch, KD>);
+  if (mode == kvb::kMergeBatched)
+    return reinterpret_cast<const void*>(&kvb::merge_kernel<kvb::kMergeBatched, KD>);
+  return reinterpret_cast<const void*>(&kvb::merge_kernel<kvb::kMergeShards, KD>);
+}
+
+const void* merge_fn(int mode, uint32_t dim) {
+  return dim <= 64 ? merge_fn_kd<2>(mode) : dim <= 128 ? merge_fn_kd<4>(mode) : merge_fn_kd<8>(mode);
+}
+
 void launch_merge(int mode, const kvb::MergeParams& prm, cudaStream_t stream) {
   const uint32_t blocks = prm.row_heads;  // one CTA per row-head
   if (blocks == 0) return;
   kvb::MergeParams copy = prm;
   void* args[] = {&copy};
-  const void* fn = nullptr;
-  if (mode == kvb::kMergeScratch)
-    fn = reinterpret_cast<const void*>(&kvb::merge_kernel<kvb::kMergeScratch>);
-  else if (mode == kvb::kMergeBatched)
-    fn = reinterpret_cast<const void*>(&kvb::merge_kernel<kvb::kMergeBatched>);
-  else
-    fn = reinterpret_cast<const void*>(&kvb::merge_kernel<kvb::kMergeShards>);
+  const void* fn = merge_fn(mode, prm.dim);
   launch_pdl(fn, dim3(blocks), dim3(32 * kvb::kMergeWarps), 0, stream, args,
              "attention merge launch");
 }
@@ -249,9 +257,11 @@ cudaError_t preload_attention_reference_kernels() {
   const void* fns[] = {
       reinterpret_cast<const void*>(&kvb::decode_simt_kernel<true>),
       reinterpret_cast<const void*>(&kvb::decode_simt_kernel<false>),
-      reinterpret_cast<const void*>(&kvb::merge_kernel<kvb::kMergeScratch>),
-      reinterpret_cast<const void*>(&kvb::merge_kernel<kvb::kMergeBatched>),
-      reinterpret_cast<const void*>(&kvb::merge_kernel<kvb::kMergeShards>),
+      merge_fn(kvb::kMergeScratch, 64),  merge_fn(kvb::kMergeScratch, 128),
+      merge_fn(kvb::kMergeScratch, 256), merge_fn(kvb::kMergeBatched, 64),
+      merge_fn(kvb::kMergeBatched, 128), merge_fn(kvb::kMergeBatched, 256),
+      merge_fn(kvb::kMergeShards, 64),   merge_fn(kvb::kMergeShards, 128),
+      merge_fn(kvb::kMergeShards, 256),
   };
   for (const void* fn : fns) {
     const cudaError_t code = cudaFuncGetAttributes(&a, fn);

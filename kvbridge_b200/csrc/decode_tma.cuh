@@ -223,6 +223,12 @@ __device__ void prefetch_first_stages(const DecodeParams& p, uint64_t x0, uint64
   const uint32_t tok_lo = max(pc.lo, (first_stage + pc.j0) * kStageTokens);
   const uint32_t tok_hi = min(pc.hi, (first_stage + j_end) * kStageTokens);
   if (tok_hi <= tok_lo) return;
+  // The table entries of the producer's first two batches of 8 pages.
+  const uint32_t piece_hi =
+      (min(pc.hi, (first_stage + pc.j1) * kStageTokens) - 1) >> p.log2_page;
+  const uint32_t batch_pg = (first_stage + pc.j0) * (kStageTokens >> p.log2_page) + lane;
+  if (lane < 16 && batch_pg >= (tok_lo >> p.log2_page) && batch_pg <= piece_hi)
+    prefetch_line_l2(p.table + batch_pg);
   const uint32_t P = p.page_tokens;
   const uint32_t pg1 = (tok_hi - 1) >> p.log2_page;
   for (uint32_t pg = (tok_lo >> p.log2_page) + lane; pg <= pg1; pg += 32) {

@@ -35,7 +35,10 @@ struct MergeParams {
   uint32_t batch, q_heads, kv_heads, group, max_tokens, ctas;
 };
 
-constexpr int kMergeWarps = 8;
+// Four warps per CTA with at most 80 registers a thread, so that a merge CTA
+// fits on an SM beside two partial-kernel CTAs: with programmatic dependent
+// launch it becomes resident early without holding back a partial CTA.
+constexpr int kMergeWarps = 4;
 
 // Warp-cooperative prefix of per-sequence stages for the batched layout.
 __device__ __forceinline__ void merge_batched_geometry(const MergeParams& p, uint32_t b,
@@ -64,12 +67,13 @@ __device__ __forceinline__ void merge_batched_geometry(const MergeParams& p, uin
 
 // One CTA of kMergeWarps warps merges one row-head. Partials are taken in
 // chunks of kMergeWarps * kPerWarp: every thread issues the loads of all its
-// partials (m, l and its dims of n) before using any, so a chunk costs one
-// memory round trip; chunks are folded with a running max.
-constexpr int kPerWarp = 8;
-
-template <int MODE>
-__global__ void __launch_bounds__(32 * kMergeWarps) merge_kernel(MergeParams p) {
+// partials (m, l and its KD dims of n, d = lane + 32k) before using any, so
+// a chunk costs one memory round trip; chunks are folded with a running max.
+// KD = ceil(dim / 32) is 2, 4 or 8; kPerWarp keeps up to 40 n values a
+// thread in flight (fewer where the registers would not hold them).
+template <int MODE, int KD>
+__global__ void __launch_bounds__(32 * kMergeWarps, 6) merge_kernel(MergeParams p) {
+  constexpr int kPerWarp = KD == 2 ? 12 : (MODE == kMergeBatched ? 32 : 40) / KD;
   __shared__ float red_m[kMergeWarps];
   __shared__ float red_l[kMergeWarps];
   __shared__ float red_n[kMergeWarps][256];
@@ -119,7 +123,7 @@ __global__ void __launch_bounds__(32 * kMergeWarps) merge_kernel(MergeParams p) 
     ms = ls = ns = size_t(p.group) * (D + 2);
   }
 
-  constexpr int kMaxK = 8;  // dims per lane: d = lane + 32k, dim <= 256
+  constexpr int kMaxK = KD;
   float acc[kMaxK];
 #pragma unroll
   for (int k = 0; k < kMaxK; ++k) acc[k] = 0.f;
