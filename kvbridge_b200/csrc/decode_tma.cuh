@@ -167,9 +167,30 @@ __device__ __forceinline__ void batched_locate(const DecodeParams& p, uint64_t x
   pref_out = pref;
 }
 
+// Single sequence (ctas = parts * kv_heads): CTA c = h * parts + j owns the
+// one piece of head h with stages [floor(j*T/parts), floor((j+1)*T/parts)),
+// T = seg_stages -- the global schedule of kvb_schedule.h restricted to a
+// segment, in 32-bit arithmetic: floor(j*T/parts) = j*(T/parts) +
+// floor(j*(T%parts)/parts).
+__device__ __forceinline__ Piece single_piece(const DecodeParams& p, uint32_t c) {
+  const uint32_t parts = p.ctas / p.kv_heads;
+  const uint32_t h = c / parts, j = c - h * parts;
+  const uint32_t T = p.seg_stages, q = T / parts, r = T - q * parts;
+  Piece pc;
+  pc.b = 0;
+  pc.h = h;
+  pc.j0 = j * q + (j * r) / parts;
+  pc.j1 = (j + 1) * q + ((j + 1) * r) / parts;
+  pc.lo = p.begin;
+  pc.hi = p.end;
+  pc.slot = j;
+  return pc;
+}
+
 // The piece starting at global stage x of CTA c whose range ends at x_end.
 __device__ __forceinline__ Piece locate_piece(const DecodeParams& p, uint64_t x, uint64_t x_end,
                                               uint64_t total, uint32_t c) {
+  if (p.seq_lens == nullptr) return single_piece(p, c);
   Piece pc;
   uint64_t seg_base;
   uint32_t seg_len;
@@ -214,10 +235,9 @@ __device__ __forceinline__ uint64_t piece_end_stage(const DecodeParams& p, const
 // (read through L2, so that no stale copy stays in L1), out-of-range entries
 // are skipped, and the copies proper re-read everything after the wait.
 template <int D>
-__device__ void prefetch_first_stages(const DecodeParams& p, uint64_t x0, uint64_t x1,
-                                      uint32_t count) {
+__device__ void prefetch_first_stages(const DecodeParams& p, uint32_t count) {
   const uint32_t lane = threadIdx.x & 31;
-  const Piece pc = locate_piece(p, x0, x1, p.total_stages, blockIdx.x);
+  const Piece pc = single_piece(p, blockIdx.x);
   const uint32_t first_stage = pc.lo / kStageTokens;
   const uint32_t j_end = min(pc.j1, pc.j0 + count);
   const uint32_t tok_lo = max(pc.lo, (first_stage + pc.j0) * kStageTokens);
@@ -719,15 +739,20 @@ __global__ void __launch_bounds__(kDecodeThreads, 2) decode_partial_kernel(Decod
   }
   __syncthreads();
   if (warp == kProducerWarp && p.prefetch_stages != 0 && p.seq_lens == nullptr)
-    prefetch_first_stages<D>(p, cta_stage_begin(blockIdx.x, p.total_stages, p.ctas),
-                             cta_stage_begin(blockIdx.x + 1, p.total_stages, p.ctas),
-                             p.prefetch_stages);
+    prefetch_first_stages<D>(p, p.prefetch_stages);
   // Inputs may be produced by the preceding kernel on the stream.
   grid_dependency_wait();
 
   const uint64_t total = p.seq_lens == nullptr ? p.total_stages : batched_total(p);
-  const uint64_t x0 = cta_stage_begin(blockIdx.x, total, p.ctas);
-  const uint64_t x1 = cta_stage_begin(blockIdx.x + 1, total, p.ctas);
+  uint64_t x0, x1;
+  if (p.seq_lens == nullptr) {
+    const Piece only = single_piece(p, blockIdx.x);
+    x0 = uint64_t(only.h) * p.seg_stages + only.j0;
+    x1 = x0 + (only.j1 - only.j0);
+  } else {
+    x0 = cta_stage_begin(blockIdx.x, total, p.ctas);
+    x1 = cta_stage_begin(blockIdx.x + 1, total, p.ctas);
+  }
 
   if (warp == kProducerWarp) {
     produce<D, STAGES>(p, ring, full, empty, tags, abort_flag, x0, x1, total);
