@@ -89,6 +89,31 @@ void merge_attention_shards(unsigned shards, unsigned row_heads, unsigned dim,
                             const float* m_parts, const float* l_parts, const float* n_parts,
                             float* m, float* l, float* n, void* out_f16, cudaStream_t);
 
+// Paged KV append (the step before decode; no counterpart in the reference,
+// whose fixtures write codes and scales directly): quantises new K and V rows
+// with the symmetric per-(token, kv-head) absmax rule -- scale = max|x| / 127,
+// code = clamp(rint(x / scale), -127, 127), fp32, ties to even; scale 0 and
+// codes 0 for an all-zero row -- and writes codes and scales into the pool
+// layout of attention_common.h. Row t goes to physical slot slots[t] =
+// page * page_tokens + position in page (negative: skipped); a slot at or
+// beyond pages * page_tokens is skipped and reported through
+// read_device_status. Rows of one call must target distinct slots.
+struct AppendShape {
+  uint32_t tokens;  // rows to append (0: nothing is launched)
+  uint32_t kv_heads, dim, page_tokens, pages;
+};
+struct AppendInput {
+  const float* k_new;    // float[tokens * kv_heads * dim]
+  const float* v_new;    // float[tokens * kv_heads * dim]
+  const int64_t* slots;  // int64[tokens]
+  int8_t* k;             // the pool (attention_common.h layout)
+  int8_t* v;
+  float* k_scales;
+  float* v_scales;
+};
+const char* append_shape_error(const AppendShape&) noexcept;
+void append_kv(const AppendShape&, const AppendInput&, cudaStream_t);
+
 // Status word written by the kernels' bounded waits (0 = ok). Reading clears
 // it. A nonzero value means a pipeline wait gave up and that call's outputs
 // are invalid.

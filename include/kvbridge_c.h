@@ -115,6 +115,24 @@ int kvb_batch_workspace_bytes(const kvb_batch_shape* s, size_t* bytes);
 int kvb_launch_attention_batched(const kvb_batch_shape* s, const kvb_batch_input* in,
                                  void* workspace, size_t workspace_bytes, float* m, float* l,
                                  float* n, void* out_f16, void* stream);
+/* paged KV append: quantise and write new K/V rows (kvbridge/attention_b200.h) */
+typedef struct kvb_append_shape {
+  uint32_t tokens, kv_heads, dim, page_tokens, pages;
+} kvb_append_shape;
+
+typedef struct kvb_append_input {
+  const float* k_new;
+  const float* v_new;
+  const int64_t* slots;
+  int8_t* k;
+  int8_t* v;
+  float* k_scales;
+  float* v_scales;
+} kvb_append_input;
+
+const char* kvb_append_shape_error(const kvb_append_shape* s);
+int kvb_append_kv(const kvb_append_shape* s, const kvb_append_input* in, void* stream);
+
 int kvb_merge_attention_shards(unsigned shards, unsigned row_heads, unsigned dim,
                                const float* m_parts, const float* l_parts,
                                const float* n_parts, float* m, float* l, float* n,

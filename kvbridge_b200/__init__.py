@@ -7,6 +7,10 @@ reference's interface names (``Shape``, ``DeviceInput``, ``launch_attention``,
 ``merge_attention``, ...).
 """
 from .api import (  # noqa: F401
+    AppendInput,
+    AppendShape,
+    append_kv,
+    append_shape_error,
     BatchInput,
     BatchShape,
     DeviceInput,

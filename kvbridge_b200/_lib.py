@@ -72,6 +72,14 @@ class KvbBatchInput(ctypes.Structure):
     ]
 
 
+class KvbAppendShape(ctypes.Structure):
+    _fields_ = [(n, c_uint32) for n in ("tokens", "kv_heads", "dim", "page_tokens", "pages")]
+
+
+class KvbAppendInput(ctypes.Structure):
+    _fields_ = [(n, c_void_p) for n in ("k_new", "v_new", "slots", "k", "v", "k_scales", "v_scales")]
+
+
 # name -> (restype, argtypes); mirrors include/kvbridge_c.h
 SIGNATURES = {
     "kvb_last_error": (c_char_p, []),
@@ -138,6 +146,8 @@ SIGNATURES = {
             c_void_p,
         ],
     ),
+    "kvb_append_shape_error": (c_char_p, [POINTER(KvbAppendShape)]),
+    "kvb_append_kv": (c_int, [POINTER(KvbAppendShape), POINTER(KvbAppendInput), c_void_p]),
     "kvb_merge_attention_shards": (
         c_int,
         [

@@ -15,7 +15,7 @@ from dataclasses import dataclass
 from typing import Any, Optional
 
 from . import _lib
-from ._lib import KvbBatchInput, KvbBatchShape, KvbDeviceInput, KvbShape, check
+from ._lib import KvbAppendInput, KvbAppendShape, KvbBatchInput, KvbBatchShape, KvbDeviceInput, KvbShape, check
 
 kSplitTokens = 256
 
@@ -324,6 +324,45 @@ def merge_attention_shards(
             _stream(stream),
         )
     )
+
+
+# ---- paged KV append (quantise + write; include/kvbridge/attention_b200.h) ----
+
+
+@dataclass
+class AppendShape:
+    tokens: int
+    kv_heads: int
+    dim: int
+    page_tokens: int
+    pages: int
+
+    def c(self) -> KvbAppendShape:
+        return KvbAppendShape(self.tokens, self.kv_heads, self.dim, self.page_tokens, self.pages)
+
+
+@dataclass
+class AppendInput:
+    k_new: Any  # f32 [tokens, kv_heads, dim]
+    v_new: Any
+    slots: Any  # i64 [tokens]: page * page_tokens + position in page; < 0 skips
+    k: Any
+    v: Any
+    k_scales: Any
+    v_scales: Any
+
+    def c(self) -> KvbAppendInput:
+        return KvbAppendInput(*(_ptr(getattr(self, f)) for f, _ in KvbAppendInput._fields_))
+
+
+def append_shape_error(s: AppendShape) -> Optional[str]:
+    msg = _lib.load().kvb_append_shape_error(ctypes.byref(s.c()))
+    return msg.decode() if msg else None
+
+
+def append_kv(s: AppendShape, inp: AppendInput, stream=None) -> None:
+    """Quantise rows (absmax int8 per token and KV head) into the paged pool."""
+    check(_lib.load().kvb_append_kv(ctypes.byref(s.c()), ctypes.byref(inp.c()), _stream(stream)))
 
 
 def read_device_status() -> int:

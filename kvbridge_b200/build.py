@@ -29,6 +29,7 @@ HEADERS = [
     "decode_tma.cuh",
     "decode_simt.cuh",
     "merge.cuh",
+    "append_kv.cuh",
     "launch_checks.h",
 ]
 

@@ -19,6 +19,7 @@
 #include "decode_simt.cuh"
 #include "decode_tma.cuh"
 #include "merge.cuh"
+#include "append_kv.cuh"
 
 namespace kvbridge {
 namespace {
@@ -515,6 +516,49 @@ void merge_attention_shards(unsigned shards, unsigned row_heads, unsigned dim,
   mp.dim = dim;
   mp.np = shards;
   launch_merge(kvb::kMergeShards, mp, stream);
+}
+
+// ---------------------------------------------------------------------------
+// Paged KV append.
+
+const char* append_shape_error(const AppendShape& s) noexcept {
+  if (s.kv_heads == 0) return "kv_heads must be positive";
+  if (s.dim == 0 || s.dim > 256) return "dim must be in [1, 256]";
+  if (s.page_tokens == 0) return "page_tokens must be positive";
+  if (s.pages == 0) return "pages must be positive";
+  // Pool extent pages * kv_heads * page_tokens * dim must stay below 2^48.
+  const uint64_t per_page = uint64_t(s.kv_heads) * s.page_tokens * s.dim;
+  if (uint64_t(s.pages) > ((uint64_t(1) << 48) - 1) / per_page) return "pool extent exceeds 2^48";
+  return nullptr;
+}
+
+void append_kv(const AppendShape& s, const AppendInput& in, cudaStream_t stream) {
+  if (const char* e = append_shape_error(s)) throw std::invalid_argument(e);
+  if (s.tokens == 0) return;
+  if (in.k_new == nullptr || in.v_new == nullptr || in.slots == nullptr || in.k == nullptr ||
+      in.v == nullptr || in.k_scales == nullptr || in.v_scales == nullptr)
+    throw std::invalid_argument("append rows, slots and the pool must be non-null device buffers");
+  if (!aligned_to(in.k_new, 4) || !aligned_to(in.v_new, 4) || !aligned_to(in.k_scales, 4) ||
+      !aligned_to(in.v_scales, 4) || !aligned_to(in.slots, 8))
+    throw std::invalid_argument("append float buffers must be 4-byte and slots 8-byte aligned");
+  const uint64_t rows = uint64_t(s.tokens) * s.kv_heads * 2;
+  const uint64_t blocks = (rows + kvb::kAppendWarps - 1) / kvb::kAppendWarps;
+  if (blocks > 0x7fffffffull) throw std::invalid_argument("append call too large for one grid");
+  kvb::AppendParams prm{};
+  prm.k_new = in.k_new;
+  prm.v_new = in.v_new;
+  prm.slots = in.slots;
+  prm.k = in.k;
+  prm.v = in.v;
+  prm.k_scales = in.k_scales;
+  prm.v_scales = in.v_scales;
+  prm.tokens = s.tokens;
+  prm.kv_heads = s.kv_heads;
+  prm.dim = s.dim;
+  prm.page_tokens = s.page_tokens;
+  prm.slots_total = uint64_t(s.pages) * s.page_tokens;
+  kvb::append_kv_kernel<<<dim3(uint32_t(blocks)), dim3(32 * kvb::kAppendWarps), 0, stream>>>(prm);
+  cuda_ok(cudaGetLastError(), "append launch");
 }
 
 cudaError_t read_device_status(int* status) {

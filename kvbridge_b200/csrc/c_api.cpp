@@ -231,6 +231,24 @@ int kvb_launch_attention_batched(const kvb_batch_shape* s, const kvb_batch_input
   });
 }
 
+const char* kvb_append_shape_error(const kvb_append_shape* s) {
+  if (s == nullptr) return "shape pointer is null";
+  return kvbridge::append_shape_error(
+      kvbridge::AppendShape{s->tokens, s->kv_heads, s->dim, s->page_tokens, s->pages});
+}
+
+int kvb_append_kv(const kvb_append_shape* s, const kvb_append_input* in, void* stream) {
+  return guarded([&] {
+    if (s == nullptr) throw std::invalid_argument("shape pointer is null");
+    if (in == nullptr) throw std::invalid_argument("input pointer is null");
+    kvbridge::append_kv(
+        kvbridge::AppendShape{s->tokens, s->kv_heads, s->dim, s->page_tokens, s->pages},
+        kvbridge::AppendInput{in->k_new, in->v_new, in->slots, in->k, in->v, in->k_scales,
+                              in->v_scales},
+        as_stream(stream));
+  });
+}
+
 int kvb_merge_attention_shards(unsigned shards, unsigned row_heads, unsigned dim,
                                const float* m_parts, const float* l_parts, const float* n_parts,
                                float* m, float* l, float* n, void* out_f16, void* stream) {

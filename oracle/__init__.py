@@ -12,6 +12,10 @@ import this package, and only as the checker; the product path never calls it.
 * ``RefCuda``      - the reference's own CUDA launchers compiled for sm_100a.
 * ``make_reference_fixture()`` - the reference's deterministic fixture
   generator (examples/attention_reference.h:19-48) restated in numpy.
+* ``append_kv()``  - the paged KV append (absmax int8 quantisation into the
+  pool layout) restated in C; the reference ships no quantiser, so this
+  follows the benchmark configurations' stated rule and is cross-checked
+  against the independent torch restatement in kvbridge_b200.synth.
 """
 from __future__ import annotations
 
@@ -72,6 +76,8 @@ def _load_oracle():
         lib.kvbo_reference.argtypes = [POINTER(_Shape), POINTER(_Inputs), POINTER(_Outputs), c_int]
         lib.kvbo_merge.restype = None
         lib.kvbo_merge.argtypes = [c_uint32, c_uint32, c_uint32] + [c_void_p] * 6
+        lib.kvbo_append_kv.restype = c_int
+        lib.kvbo_append_kv.argtypes = [c_uint32] * 5 + [c_void_p] * 7
         _oracle = lib
     return _oracle
 
@@ -291,3 +297,24 @@ class RefCuda:
         p = (c_void_p * 8)(*ptrs)
         fn = self.lib.kvbref_cuda_launch_attention_mma if mma else self.lib.kvbref_cuda_launch_attention
         return fn(dims, float(f["scale"]), int(bool(f["int8"])), p, scratch, m, l, n, stream)
+
+
+def append_kv(k_new, v_new, slots, k, v, k_scales, v_scales, pages: int, page_tokens: int) -> int:
+    """Quantise and write rows into numpy pools in place (oracle/kvb_oracle.c
+    kvbo_append_kv). k_new/v_new float32 [tokens, kv_heads, dim]; slots int64
+    [tokens]; k int8 [pages, kv, P, D]; v int8 [pages, kv, D, P]; scales float32
+    [pages, kv, P]. Returns the number of out-of-range slots skipped."""
+    kn = np.ascontiguousarray(_np(k_new, np.float32))
+    vn = np.ascontiguousarray(_np(v_new, np.float32))
+    sl = np.ascontiguousarray(_np(slots, np.int64))
+    for a in (k, v, k_scales, v_scales):
+        assert isinstance(a, np.ndarray) and a.flags["C_CONTIGUOUS"]
+    assert k.dtype == np.int8 and v.dtype == np.int8
+    assert k_scales.dtype == np.float32 and v_scales.dtype == np.float32
+    tokens, kv_heads, dim = kn.shape
+    assert vn.shape == kn.shape and sl.shape == (tokens,)
+    assert k.shape == (pages, kv_heads, page_tokens, dim) and v.shape == (pages, kv_heads, dim, page_tokens)
+    assert k_scales.shape == (pages, kv_heads, page_tokens) and v_scales.shape == k_scales.shape
+    ptr = lambda a: a.ctypes.data_as(c_void_p)  # noqa: E731
+    return _load_oracle().kvbo_append_kv(tokens, kv_heads, dim, page_tokens, pages, ptr(kn), ptr(vn),
+                                         ptr(sl), ptr(k), ptr(v), ptr(k_scales), ptr(v_scales))

@@ -187,3 +187,53 @@ void kvbo_merge(uint32_t parts, uint32_t row_heads, uint32_t dim, const double* 
     l_out[rh] = L;
   }
 }
+
+/* Paged KV append (no counterpart in the reference, which ships no
+ * quantiser; the rule is the benchmark configurations' symmetric
+ * per-(token, kv-head) absmax quantisation): for each of `tokens` rows and
+ * kv head h, K row x = k_new[(t*kv_heads + h)*dim ..], likewise V,
+ *   scale = max|x| / 127 (float), div = scale > 0 ? scale : 1,
+ *   code  = clamp(rint(x / div), -127, 127)   (float division, ties to even)
+ * written to physical slot slots[t] = page*page_tokens + s of the pool in the
+ * reference layout (attention_common.h:11-46): K codes at
+ * ((page*kv_heads + h)*P + s)*dim + d, V codes at ((page*kv_heads + h)*dim +
+ * d)*P + s, scales at (page*kv_heads + h)*P + s. Negative slots are skipped;
+ * slots >= pages*P are skipped and counted (the return value). */
+int kvbo_append_kv(uint32_t tokens, uint32_t kv_heads, uint32_t dim, uint32_t page_tokens,
+                   uint32_t pages, const float* k_new, const float* v_new, const int64_t* slots,
+                   int8_t* k, int8_t* v, float* k_scales, float* v_scales) {
+  int bad = 0;
+  const uint64_t P = page_tokens, total = (uint64_t)pages * page_tokens;
+  for (uint32_t t = 0; t < tokens; ++t) {
+    if (slots[t] < 0) continue;
+    if ((uint64_t)slots[t] >= total) {
+      ++bad;
+      continue;
+    }
+    const uint64_t page = (uint64_t)slots[t] / P, s = (uint64_t)slots[t] % P;
+    for (uint32_t h = 0; h < kv_heads; ++h) {
+      const uint64_t unit = page * kv_heads + h;
+      for (int kind = 0; kind < 2; ++kind) {
+        const float* x = (kind == 0 ? k_new : v_new) + ((uint64_t)t * kv_heads + h) * dim;
+        float amax = 0.0f;
+        for (uint32_t d = 0; d < dim; ++d) {
+          const float a = fabsf(x[d]);
+          if (a > amax) amax = a;
+        }
+        const float scale = amax / 127.0f;
+        const float div = scale > 0.0f ? scale : 1.0f;
+        for (uint32_t d = 0; d < dim; ++d) {
+          float c = rintf(x[d] / div);
+          if (c > 127.0f) c = 127.0f;
+          if (c < -127.0f) c = -127.0f;
+          if (kind == 0)
+            k[(unit * P + s) * dim + d] = (int8_t)(int)c;
+          else
+            v[(unit * dim + d) * P + s] = (int8_t)(int)c;
+        }
+        (kind == 0 ? k_scales : v_scales)[unit * P + s] = scale;
+      }
+    }
+  }
+  return bad;
+}
