@@ -132,10 +132,26 @@ int resident_ctas(const FastVariant& v) {
 
 uint32_t query_rows(const Shape& s) { return s.rows * (s.q_heads / s.kv_heads); }
 
-bool fast_geometry(uint32_t dim, uint32_t page_tokens, uint32_t qrows) {
+// Query columns per KV head a CTA takes: 8 * nt, nt <= 2 (1 at dim 256,
+// where the PV accumulators of 16 columns would not fit in registers).
+// Single sequences with more columns (e.g. the reference's native 8 rows x
+// group 6) are cut into column groups, one CTA per group and KV range.
+struct ColumnPlan {
+  uint32_t nt, groups;
+};
+constexpr uint32_t kMaxQueryColumns = 64;
+
+ColumnPlan column_plan(uint32_t dim, uint32_t qrows) {
+  const uint32_t nt_max = dim == 256 ? 1u : 2u;
+  const uint32_t nt = std::min(nt_max, (qrows + 7) / 8);
+  return ColumnPlan{nt, (qrows + 8 * nt - 1) / (8 * nt)};
+}
+
+// Tensor-core geometry. `max_rows`: query columns per KV head the caller can
+// cut into column groups (single sequence), or one group's worth (batched).
+bool fast_geometry(uint32_t dim, uint32_t page_tokens, uint32_t qrows, uint32_t max_rows) {
   const bool dim_ok = dim == 64 || dim == 128 || dim == 256;
   const bool page_ok = page_tokens == 16 || page_tokens == 32 || page_tokens == 64;
-  const uint32_t max_rows = dim == 256 ? 8u : 16u;
   return dim_ok && page_ok && qrows >= 1 && qrows <= max_rows;
 }
 
@@ -228,7 +244,7 @@ uint32_t batched_ctas(const FastVariant& v) {
 
 bool attention_b200_supported(const Shape& s, const DeviceInput& in) noexcept {
   if (!attention_shape_valid(s) || !s.int8) return false;
-  if (!fast_geometry(s.dim, s.page_tokens, query_rows(s))) return false;
+  if (!fast_geometry(s.dim, s.page_tokens, query_rows(s), kMaxQueryColumns)) return false;
   return aligned_to(in.q, 16) && aligned_to(in.k, 16) && aligned_to(in.v, 16) &&
          aligned_to(in.k_scales, 16) && aligned_to(in.v_scales, 16);
 }
@@ -239,11 +255,11 @@ unsigned attention_partitions(const Shape& s, unsigned requested) {
   if (stages == 0) return 0;
   uint32_t parts = requested;
   if (parts == 0) {
-    const uint32_t nt = (query_rows(s) + 7) / 8;
-    const FastVariant v = fast_variant(s.dim, nt);
+    const ColumnPlan plan = column_plan(s.dim, query_rows(s));
+    const FastVariant v = fast_variant(s.dim, plan.nt);
     const uint32_t wave =
         v.fn ? uint32_t(current_device_facts().sms) * uint32_t(resident_ctas(v)) : 1u;
-    parts = std::max(1u, wave / s.kv_heads);
+    parts = std::max(1u, wave / (s.kv_heads * plan.groups));
   }
   parts = std::min(parts, stages);
   parts = std::min(parts, split_count(s));
@@ -330,7 +346,10 @@ kvb::DecodeParams single_params(const Shape& s, const DeviceInput& in, uint32_t 
   prm.seg_stages = kvb::stages_of_range(s.begin, s.end);
   prm.split_stride = split_stride;
   prm.max_tokens = s.tokens;
-  prm.ctas = parts * s.kv_heads;
+  const ColumnPlan plan = column_plan(s.dim, query_rows(s));
+  prm.col_groups = plan.groups;
+  prm.group_cols = 8 * plan.nt;
+  prm.ctas = parts * s.kv_heads * plan.groups;
   prm.total_stages = uint64_t(prm.seg_stages) * s.kv_heads;
   prm.score_scale = s.scale;
   return prm;
@@ -348,10 +367,9 @@ unsigned launch_attention_partials(const Shape& s, const DeviceInput& in, unsign
   const uint32_t splits = split_count(s);
   const uint32_t parts = attention_partitions(s, partitions);
   if (parts == 0) return 0;
-  const uint32_t nt = (query_rows(s) + 7) / 8;
   kvb::DecodeParams prm = single_params(s, in, parts, scratch, splits);
   prm.prefetch_stages = kPrefetchStages;
-  fast_variant(s.dim, nt).launch(prm, stream);
+  fast_variant(s.dim, prm.group_cols / 8).launch(prm, stream);
   return parts;
 }
 
@@ -416,7 +434,7 @@ const char* batch_shape_error(const BatchShape& s) noexcept {
   if (s.batch == 0 || s.q_heads == 0 || s.kv_heads == 0)
     return "batch and head counts must be positive";
   if (s.q_heads % s.kv_heads) return "q_heads must be divisible by kv_heads";
-  if (!fast_geometry(s.dim, s.page_tokens, s.q_heads / s.kv_heads))
+  if (!fast_geometry(s.dim, s.page_tokens, s.q_heads / s.kv_heads, s.dim == 256 ? 8u : 16u))
     return "batched decode needs dim 64/128/256, page_tokens 16/32/64 and a query group of at "
            "most 16 (8 at dim 256)";
   if (s.pages == 0 || s.table_stride == 0) return "pages and table_stride must be positive";
@@ -476,6 +494,8 @@ void launch_attention_batched(const BatchShape& s, const BatchInput& in, void* w
   prm.table_stride = s.table_stride;
   prm.max_tokens = s.max_tokens;
   prm.ctas = batched_ctas(v);
+  prm.col_groups = 1;
+  prm.group_cols = 8 * ((group + 7) / 8);
   prm.score_scale = s.scale;
   v.launch(prm, stream);
 
@@ -640,38 +660,9 @@ void launch_attention_noalloc(const Shape& s, const DeviceInput& in, unsigned pa
   parts = uint32_t(std::min<size_t>(parts, fit));
   float* scratch = noalloc_scratch_on_current_device();
   if (parts > 0) {
-    const uint32_t nt = (query_rows(s) + 7) / 8;
-    const FastVariant v = fast_variant(s.dim, nt);
-    kvb::DecodeParams prm{};
-    prm.q = in.q;
-    prm.q_positions = in.q_positions;
-    prm.k_positions = in.k_positions;
-    prm.table = in.page_table;
-    prm.k = static_cast<const int8_t*>(in.k);
-    prm.v = static_cast<const int8_t*>(in.v);
-    prm.k_scales = in.k_scales;
-    prm.v_scales = in.v_scales;
-    prm.seq_lens = nullptr;
-    prm.part = scratch;
-    prm.batch = 1;
-    prm.rows = s.rows;
-    prm.q_heads = s.q_heads;
-    prm.kv_heads = s.kv_heads;
-    prm.group = s.q_heads / s.kv_heads;
-    prm.qr = query_rows(s);
-    prm.page_tokens = s.page_tokens;
-    prm.log2_page = log2_exact(s.page_tokens);
-    prm.pages = s.pages;
-    prm.table_stride = 0;
-    prm.begin = s.begin;
-    prm.end = s.end;
-    prm.seg_stages = kvb::stages_of_range(s.begin, s.end);
-    prm.split_stride = parts;  // partials packed [row-head][partition]
-    prm.max_tokens = s.tokens;
-    prm.ctas = parts * s.kv_heads;
-    prm.total_stages = uint64_t(prm.seg_stages) * s.kv_heads;
-    prm.score_scale = s.scale;
-    v.launch(prm, stream);
+    // Partials packed [row-head][partition]: split stride = parts.
+    const kvb::DecodeParams prm = single_params(s, in, parts, scratch, parts);
+    fast_variant(s.dim, prm.group_cols / 8).launch(prm, stream);
   }
   launch_merge(kvb::kMergeScratch,
                scratch_merge_params(s, scratch, parts, parts, false, m, l, n, out_f16), stream);

@@ -67,6 +67,11 @@ struct DecodeParams {
   // Single sequence: L2 prefetch of the CTA's first `prefetch_stages` stages
   // before the dependency wait on the preceding grid (0 = none).
   uint32_t prefetch_stages;
+  // Single sequence: the query columns (rows * group per KV head) are cut
+  // into col_groups groups of group_cols (= 8 * NT) columns; CTA c works on
+  // group c % col_groups, so the CTAs of one KV range and different groups
+  // run side by side and share its pages in L2. Batched: 1 and 8 * NT.
+  uint32_t col_groups, group_cols;
 };
 
 constexpr int kConsumerWarps = 4;
@@ -115,6 +120,7 @@ struct Piece {
   uint32_t j0, j1;     // stage range within the segment
   uint32_t lo, hi;     // attended token interval of the sequence
   uint32_t slot;       // partial slot (see write_partial)
+  uint32_t col0;       // first query column of the CTA's column group
 };
 
 __device__ __forceinline__ uint32_t clamped_len(const DecodeParams& p, uint32_t b) {
@@ -173,11 +179,15 @@ __device__ __forceinline__ void batched_locate(const DecodeParams& p, uint64_t x
 // segment, in 32-bit arithmetic: floor(j*T/parts) = j*(T/parts) +
 // floor(j*(T%parts)/parts).
 __device__ __forceinline__ Piece single_piece(const DecodeParams& p, uint32_t c) {
-  const uint32_t parts = p.ctas / p.kv_heads;
+  const uint32_t groups = p.col_groups;
+  const uint32_t parts = p.ctas / (p.kv_heads * groups);
+  const uint32_t col_group = c % groups;
+  c /= groups;
   const uint32_t h = c / parts, j = c - h * parts;
   const uint32_t T = p.seg_stages, q = T / parts, r = T - q * parts;
   Piece pc;
   pc.b = 0;
+  pc.col0 = col_group * p.group_cols;
   pc.h = h;
   pc.j0 = j * q + (j * r) / parts;
   pc.j1 = (j + 1) * q + ((j + 1) * r) / parts;
@@ -192,6 +202,7 @@ __device__ __forceinline__ Piece locate_piece(const DecodeParams& p, uint64_t x,
                                               uint64_t total, uint32_t c) {
   if (p.seq_lens == nullptr) return single_piece(p, c);
   Piece pc;
+  pc.col0 = 0;
   uint64_t seg_base;
   uint32_t seg_len;
   if (p.seq_lens == nullptr) {
@@ -409,7 +420,7 @@ __device__ __forceinline__ void load_query(const DecodeParams& p, const Piece& p
   const uint32_t lane = threadIdx.x & 31, grp = lane >> 2, tig = lane & 3;
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) {
-    const uint32_t col = 8 * nt + grp;
+    const uint32_t col = pc.col0 + 8 * nt + grp;
     const bool valid = col < p.qr;
     const uint32_t r = valid ? col / p.group : 0, g = valid ? col % p.group : 0;
     const uint32_t row = p.seq_lens == nullptr ? r : pc.b;
@@ -460,7 +471,7 @@ __device__ __forceinline__ void load_query(const DecodeParams& p, const Piece& p
 #pragma unroll
     for (int ee = 0; ee < 2; ++ee) {
       qf.cf[nt][ee] = __shfl_sync(0xffffffffu, cf_b, 4 * (2 * tig + ee));
-      const uint32_t ccol = 8 * nt + 2 * tig + ee;
+      const uint32_t ccol = pc.col0 + 8 * nt + 2 * tig + ee;
       int64_t qp = INT64_MAX;
       if (p.seq_lens == nullptr && ccol < p.qr) qp = __ldg(p.q_positions + ccol / p.group);
       qf.qpos[nt][ee] = qp;
@@ -838,7 +849,8 @@ __global__ void __launch_bounds__(kDecodeThreads, 2) decode_partial_kernel(Decod
     constexpr uint32_t kTpc = 32 * kConsumerWarps / L::kCols;  // threads per column
     constexpr uint32_t kDpt = D / kTpc;                          // dims per thread
     const uint32_t col = threadIdx.x / kTpc, part = threadIdx.x % kTpc;
-    if (col < p.qr) {
+    const uint32_t gcol = pc.col0 + col;  // the column among all p.qr
+    if (gcol < p.qr) {
       float mw[kConsumerWarps], M = -INFINITY;
 #pragma unroll
       for (int w = 0; w < kConsumerWarps; ++w) {
@@ -853,11 +865,11 @@ __global__ void __launch_bounds__(kDecodeThreads, 2) decode_partial_kernel(Decod
       }
       size_t base;
       if (p.seq_lens == nullptr) {
-        const uint32_t r = col / p.group, gq = col % p.group;
+        const uint32_t r = gcol / p.group, gq = gcol % p.group;
         const size_t rh = size_t(r) * p.q_heads + size_t(pc.h) * p.group + gq;
         base = (rh * p.split_stride + pc.slot) * (D + 2);
       } else {
-        base = (size_t(pc.slot) * p.qr + col) * (D + 2);
+        base = (size_t(pc.slot) * p.qr + gcol) * (D + 2);
       }
       float* out = p.part + base;
       if (part == 0) {

@@ -115,7 +115,11 @@ def test_b200_predicate(kvb_lib):
     assert not kvb.attention_b200_supported(_shape(int8=False), aligned)
     assert not kvb.attention_b200_supported(_shape(dim=96), aligned)
     assert not kvb.attention_b200_supported(_shape(page_tokens=128, pages=32), aligned)
-    assert not kvb.attention_b200_supported(_shape(rows=8, q_heads=24, kv_heads=4, dim=256, page_tokens=32,
+    # the reference's native shape: 48 query columns per KV head, in 6 column groups
+    assert kvb.attention_b200_supported(_shape(rows=8, q_heads=24, kv_heads=4, dim=256, page_tokens=32,
+                                               pages=128), aligned)
+    # more than 64 query columns per KV head: general kernel
+    assert not kvb.attention_b200_supported(_shape(rows=16, q_heads=24, kv_heads=4, dim=256, page_tokens=32,
                                                    pages=128), aligned)
     shifted = kvb.DeviceInput(FAKE, FAKE, FAKE, FAKE, FAKE + 4, FAKE, FAKE, FAKE)
     assert not kvb.attention_b200_supported(_shape(), shifted)

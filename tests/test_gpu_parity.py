@@ -172,7 +172,7 @@ def test_general_geometry_kernel(cuda_device):
     """Shapes outside the tensor-core kernel run the general kernel."""
     cases = [
         dict(rows=1, q_heads=12, kv_heads=1, dim=96, page_tokens=8, tokens=700),  # group 12, dim 96, P8
-        dict(rows=8, q_heads=24, kv_heads=4, dim=256, page_tokens=32, tokens=1100),  # reference native shape
+        dict(rows=16, q_heads=24, kv_heads=4, dim=256, page_tokens=32, tokens=1100),  # 96 query columns
         dict(rows=1, q_heads=4, kv_heads=2, dim=33, page_tokens=5, tokens=123),  # odd everything
     ]
     for i, kw in enumerate(cases):
@@ -183,6 +183,31 @@ def test_general_geometry_kernel(cuda_device):
         assert not kvb.attention_b200_supported(case.shape, case.device_input())
         res = run_single(case)
         check_against_oracle(res, case.shape, oracle.reference_case(case, threads=8), f"general{i}")
+
+
+@pytest.mark.parametrize(
+    "rows,q_heads,kv_heads,dim,page_tokens",
+    [
+        (8, 24, 4, 256, 32),  # the reference's native shape: 48 columns, 6 groups of 8
+        (3, 24, 4, 256, 32),  # 18 columns: 3 groups, the last one 2 columns wide
+        (6, 32, 8, 128, 64),  # 24 columns: 2 groups of 16, the last one half used
+        (8, 64, 8, 128, 16),  # 64 columns: 4 groups of 16
+        (5, 64, 8, 64, 32),   # 40 columns at dim 64: 3 groups
+    ],
+)
+def test_query_column_groups(cuda_device, rows, q_heads, kv_heads, dim, page_tokens):
+    """More query columns per KV head than one CTA holds (rows x group > 16,
+    > 8 at dim 256): the tensor-core kernel runs one CTA per column group and
+    KV range, with the rows' causal positions, against the FP64 oracle."""
+    tokens = 1500
+    qpos = [tokens - rows + r for r in range(rows)]
+    case = make(cuda_device, rows=rows, q_heads=q_heads, kv_heads=kv_heads, dim=dim, page_tokens=page_tokens,
+                tokens=tokens, seed=rows * 7 + dim, q_positions=qpos)
+    assert kvb.attention_b200_supported(case.shape, case.device_input())
+    ref = oracle.reference_case(case, threads=8)
+    for partitions in (0, 3):
+        res = run_single(case, partitions=partitions)
+        check_against_oracle(res, case.shape, ref, f"groups {rows}x{q_heads // kv_heads} d{dim} P{partitions}")
 
 
 def test_mma_launcher_contract(cuda_device):
