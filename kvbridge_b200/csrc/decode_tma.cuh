@@ -273,6 +273,128 @@ __device__ void prefetch_first_stages(const DecodeParams& p, uint32_t count) {
   }
 }
 
+// Drain: every copy the producer issued (stages 0..g-1) must land before the
+// CTA can exit; only the last STAGES of them can still be in flight.
+template <int STAGES>
+__device__ __forceinline__ void drain_copies(uint64_t* full, uint32_t g) {
+  const uint32_t first = g > STAGES ? g - STAGES : 0u;
+  for (uint32_t s = first; s < g; ++s) {
+    // Copies land whatever the consumers do, so this wait ignores an abort.
+    volatile int no_abort = 0;
+    if (mbar_wait_bounded(&full[s % STAGES], (s / STAGES) & 1u, &no_abort, kStatusDrainTimeout,
+                          int(s)) != kWaitOk)
+      break;
+  }
+}
+
+// Producer for pages shorter than a stage (16 or 32 tokens). Each bulk copy
+// costs the SM's copy engine about as much time as a small one, and with
+// 16-token pages the four copies per page (K, V and two 64-byte scale runs)
+// made that the streaming limit. Here only K and V are bulk-copied; per
+// stage, lane l loads the 16 bytes of scales of tokens 4*(l%16) .. +3 (K
+// scales for l < 16, V scales above) with a plain load and stores them to the
+// stage before the barrier is armed, and the lane holding a page's first
+// four tokens starts the bulk copy of that page's K (l < 16) or V (l >= 16).
+// A lane's table entries and scales are fetched 8 and 3 stages ahead in
+// registers that take turns (no register copies, which would wait for the
+// loads). With 64-token pages the extra per-stage work costs more than the
+// two copies it saves, so produce() keeps those.
+template <int D, int STAGES>
+__device__ void produce_small_pages(const DecodeParams& p, uint8_t* ring, uint64_t* full,
+                                    uint64_t* empty, volatile uint32_t* tags,
+                                    volatile int* abort_flag, uint64_t x0, uint64_t x1,
+                                    uint64_t total) {
+  const uint32_t lane = threadIdx.x & 31;
+  const uint64_t policy = l2_evict_first_policy();
+  const uint32_t P = p.page_tokens;
+  const uint32_t kv_bytes = 2u * P * D;  // bulk-copied bytes per page
+  const uint32_t vpitch = v_page_pitch(D, P);
+  const uint32_t pps = kStageTokens >> p.log2_page;  // pages per stage: 2 or 4
+  const uint32_t tok4 = 4u * (lane & 15u);
+  const uint32_t q = tok4 >> p.log2_page;  // the lane's page within a stage
+  const bool is_v = lane >= 16;
+  const bool copier = (tok4 & (P - 1u)) == 0u;
+  const float* scale_base = is_v ? p.v_scales : p.k_scales;
+  const uint32_t scale_off = is_v ? StageLayout<D>::kVs : StageLayout<D>::kKs;
+  uint32_t g = 0;  // stages issued so far (CTA stage sequence number)
+  bool failed = false;
+  for (uint64_t x = x0; x < x1 && !failed;) {
+    const Piece pc = locate_piece(p, x, x1, total, blockIdx.x);
+    const uint32_t first_stage = pc.lo / kStageTokens;
+    const uint32_t page_lo = max(pc.lo, (first_stage + pc.j0) * kStageTokens) >> p.log2_page;
+    const uint32_t page_hi = (min(pc.hi, (first_stage + pc.j1) * kStageTokens) - 1) >> p.log2_page;
+    const uint32_t* trow =
+        p.seq_lens == nullptr ? p.table : p.table + size_t(pc.b) * p.table_stride;
+    // Table entry of this lane's page of stage j (in flight after return).
+    auto table_load = [&](uint32_t j, uint32_t& t, bool& mine) {
+      const uint32_t pg = (first_stage + j) * pps + q;
+      mine = j < pc.j1 && pg >= page_lo && pg <= page_hi;
+      t = mine ? __ldg(trow + pg) : 0u;
+    };
+    // This lane's 16 bytes of scales of the stage whose table entry is t.
+    auto scale_load = [&](uint32_t t, bool mine, float4& sc) {
+      const bool ok = mine && t < p.pages;
+      const size_t unit = size_t(ok ? t : 0u) * p.kv_heads + pc.h;  // (page, kv head)
+      sc = ok ? __ldcs(reinterpret_cast<const float4*>(scale_base + unit * P + (tok4 & (P - 1u))))
+              : make_float4(0.f, 0.f, 0.f, 0.f);
+    };
+    // One stage: wait for its slot, store the scales, arm the barrier,
+    // start the bulk copies. False if the slot wait gave up.
+    auto issue_stage = [&](uint32_t t, bool mine, const float4& sc) -> bool {
+      const bool ok = mine && t < p.pages;
+      if (__ballot_sync(0xffffffffu, mine && !ok) && lane == 0)
+        atomicMax(&g_kvb_status, kStatusBadPage);
+      const uint32_t okpages = __popc(__ballot_sync(0xffffffffu, ok && copier && !is_v));
+      const uint32_t slot = g % STAGES;
+      if (mbar_wait_bounded(&empty[slot], ((g / STAGES) & 1u) ^ 1u, abort_flag,
+                            kStatusEmptyWaitTimeout, int(g)) != kWaitOk)
+        return false;
+      uint8_t* st = ring + size_t(slot) * StageLayout<D>::kBytes;
+      *reinterpret_cast<float4*>(st + scale_off + tok4 * 4u) = sc;
+      // The warp's scale stores come before lane 0's arrive (release).
+      __syncwarp();
+      if (lane == 0) {
+        // Tag protocol as in produce().
+        tags[slot] = g;
+        mbar_arrive_expect_tx(&full[slot], okpages * kv_bytes);
+      }
+      __syncwarp();
+      if (ok && copier) {
+        const size_t unit = size_t(t) * p.kv_heads + pc.h;
+        if (is_v)
+          bulk_copy_g2s(st + StageLayout<D>::kV + q * vpitch, p.v + unit * D * P, D * P,
+                        &full[slot], policy);
+        else
+          bulk_copy_g2s(st + StageLayout<D>::kK + q * P * D, p.k + unit * P * D, P * D,
+                        &full[slot], policy);
+      }
+      ++g;
+      return true;
+    };
+    uint32_t t[8];
+    bool mine[8];
+    float4 sc[4];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) table_load(pc.j0 + u, t[u], mine[u]);
+#pragma unroll
+    for (int u = 0; u < 3; ++u) scale_load(t[u], mine[u], sc[u]);
+    for (uint32_t jb = pc.j0; jb < pc.j1 && !failed; jb += 8) {
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        if (jb + u >= pc.j1) break;
+        scale_load(t[(u + 3) & 7], mine[(u + 3) & 7], sc[(u + 3) & 3]);
+        if (!issue_stage(t[u], mine[u], sc[u & 3])) {
+          failed = true;
+          break;
+        }
+        table_load(jb + u + 8, t[u], mine[u]);
+      }
+    }
+    x = piece_end_stage(p, pc, x);
+  }
+  drain_copies<STAGES>(full, g);
+}
+
 template <int D, int STAGES>
 __device__ void produce(const DecodeParams& p, uint8_t* ring, uint64_t* full, uint64_t* empty,
                         volatile uint32_t* tags, volatile int* abort_flag, uint64_t x0, uint64_t x1,
@@ -368,16 +490,7 @@ __device__ void produce(const DecodeParams& p, uint8_t* ring, uint64_t* full, ui
     }
     x = piece_end_stage(p, pc, x);
   }
-  // Drain: every copy this warp issued (stages 0..g-1) must land before the
-  // CTA can exit; only the last STAGES of them can still be in flight.
-  const uint32_t first = g > STAGES ? g - STAGES : 0u;
-  for (uint32_t s = first; s < g; ++s) {
-    // Copies land whatever the consumers do, so this wait ignores an abort.
-    volatile int no_abort = 0;
-    if (mbar_wait_bounded(&full[s % STAGES], (s / STAGES) & 1u, &no_abort, kStatusDrainTimeout,
-                          int(s)) != kWaitOk)
-      break;
-  }
+  drain_copies<STAGES>(full, g);
 }
 
 // ---------------------------------------------------------------------------
@@ -766,7 +879,10 @@ __global__ void __launch_bounds__(kDecodeThreads, 2) decode_partial_kernel(Decod
   }
 
   if (warp == kProducerWarp) {
-    produce<D, STAGES>(p, ring, full, empty, tags, abort_flag, x0, x1, total);
+    if (p.page_tokens < kStageTokens)
+      produce_small_pages<D, STAGES>(p, ring, full, empty, tags, abort_flag, x0, x1, total);
+    else
+      produce<D, STAGES>(p, ring, full, empty, tags, abort_flag, x0, x1, total);
     return;
   }
 
