@@ -27,8 +27,8 @@ struct LaunchOptions {
 };
 
 // True when launch_attention(_ex) will use the TMA/tensor-core kernel for this
-// shape and these buffers (int8 KV, dim in {64,128,256}, page_tokens dividing
-// 64, rows*group <= 16, 16-byte aligned K/V/scale buffers). Host-only.
+// shape and these buffers (int8 KV, dim in {64,128,256}, page_tokens 16, 32
+// or 64, rows*group <= 64, 16-byte aligned K/V/scale buffers). Host-only.
 bool attention_b200_supported(const Shape&, const DeviceInput&) noexcept;
 
 // Partition count launch_attention_ex will use (host-only; needs the SM count
