@@ -132,20 +132,19 @@ int resident_ctas(const FastVariant& v) {
 
 uint32_t query_rows(const Shape& s) { return s.rows * (s.q_heads / s.kv_heads); }
 
-// Query columns per KV head a CTA takes: 8 * nt, nt <= 2 (1 at dim 256,
-// where the PV accumulators of 16 columns would not fit in registers).
-// Single sequences with more columns (e.g. the reference's native 8 rows x
-// group 6) are cut into column groups, one CTA per group and KV range.
+// Single sequence: a CTA takes 8 query columns of one KV head (nt = 1);
+// more columns (rows x group up to 64, e.g. the reference's native 8 rows x
+// group 6) are cut into column groups, one CTA per group and KV range, whose
+// repeated page reads hit L2. Measured at 64K tokens with 16 columns, two
+// 8-column groups (51.8 us) beat one 16-column CTA (69.3 us), whose PV
+// accumulators spill. (The batched path, without column groups, still takes
+// up to 16 columns in one CTA.)
 struct ColumnPlan {
   uint32_t nt, groups;
 };
 constexpr uint32_t kMaxQueryColumns = 64;
 
-ColumnPlan column_plan(uint32_t dim, uint32_t qrows) {
-  const uint32_t nt_max = dim == 256 ? 1u : 2u;
-  const uint32_t nt = std::min(nt_max, (qrows + 7) / 8);
-  return ColumnPlan{nt, (qrows + 8 * nt - 1) / (8 * nt)};
-}
+ColumnPlan column_plan(uint32_t /*dim*/, uint32_t qrows) { return ColumnPlan{1, (qrows + 7) / 8}; }
 
 // Tensor-core geometry. `max_rows`: query columns per KV head the caller can
 // cut into column groups (single sequence), or one group's worth (batched).
