@@ -529,7 +529,7 @@ def main():
         ),
         "roofline": {
             "bound": "hbm",
-            "kernel": "decode_partial_kernel<128,1,5>",
+            "kernel": "decode_partial_kernel<128,1,5,false>",
             "achieved": round(achieved, 2),
             "peak": peak,
             "unit": "GB/s",

@@ -839,7 +839,10 @@ __device__ __forceinline__ void consume_stage(const DecodeParams& p, const uint8
   }
 }
 
-template <int D, int NT, int STAGES>
+// SMALL_PAGES: pages shorter than a stage (produce_small_pages); a separate
+// instantiation, so that the 64-token-page kernel does not carry that code
+// (which cost it ~0.6 us a call at cfg2 when both producers were compiled in).
+template <int D, int NT, int STAGES, bool SMALL_PAGES>
 __global__ void __launch_bounds__(kDecodeThreads, 2) decode_partial_kernel(DecodeParams p) {
   using L = DecodeSmem<D, NT, STAGES>;
   extern __shared__ __align__(128) uint8_t smem[];
@@ -879,7 +882,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 2) decode_partial_kernel(Decod
   }
 
   if (warp == kProducerWarp) {
-    if (p.page_tokens < kStageTokens)
+    if constexpr (SMALL_PAGES)
       produce_small_pages<D, STAGES>(p, ring, full, empty, tags, abort_flag, x0, x1, total);
     else
       produce<D, STAGES>(p, ring, full, empty, tags, abort_flag, x0, x1, total);
