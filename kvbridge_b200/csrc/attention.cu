@@ -75,9 +75,10 @@ void launch_pdl(const void* fn, dim3 grid, dim3 block, uint32_t smem, cudaStream
   cuda_ok(cudaLaunchKernelExC(&cfg, fn, args), what);
 }
 
-template <int D, int NT, int STAGES, bool SMALL>
+template <int D, int NT, int STAGES, bool SMALL, bool BATCHED>
 void launch_fast_variant(const kvb::DecodeParams& prm, cudaStream_t stream) {
-  const void* fn = reinterpret_cast<const void*>(&kvb::decode_partial_kernel<D, NT, STAGES, SMALL>);
+  const void* fn =
+      reinterpret_cast<const void*>(&kvb::decode_partial_kernel<D, NT, STAGES, SMALL, BATCHED>);
   constexpr uint32_t smem = kvb::DecodeSmem<D, NT, STAGES>::kBytes;
   cuda_ok(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)),
           "decode kernel shared-memory opt-in");
@@ -87,27 +88,35 @@ void launch_fast_variant(const kvb::DecodeParams& prm, cudaStream_t stream) {
              "decode partial launch");
 }
 
-template <int D, int NT, int STAGES>
-FastVariant make_variant(bool small_pages) {
+template <int D, int NT, int STAGES, bool SMALL, bool BATCHED>
+FastVariant make_variant() {
   FastVariant v;
-  v.fn = small_pages
-             ? reinterpret_cast<const void*>(&kvb::decode_partial_kernel<D, NT, STAGES, true>)
-             : reinterpret_cast<const void*>(&kvb::decode_partial_kernel<D, NT, STAGES, false>);
+  v.fn = reinterpret_cast<const void*>(&kvb::decode_partial_kernel<D, NT, STAGES, SMALL, BATCHED>);
   v.smem = kvb::DecodeSmem<D, NT, STAGES>::kBytes;
-  v.launch = small_pages ? &launch_fast_variant<D, NT, STAGES, true>
-                         : &launch_fast_variant<D, NT, STAGES, false>;
+  v.launch = &launch_fast_variant<D, NT, STAGES, SMALL, BATCHED>;
   return v;
+}
+
+// Page size (small pages have their own producer) and mode (single
+// sequence or batched) are template parameters, so that each kernel carries
+// only the code it runs; compiling the other paths in cost the 64-token
+// single-sequence call ~1.6 us at cfg2.
+template <int D, int NT, int STAGES>
+FastVariant make_variant(bool small_pages, bool batched) {
+  if (small_pages)
+    return batched ? make_variant<D, NT, STAGES, true, true>() : make_variant<D, NT, STAGES, true, false>();
+  return batched ? make_variant<D, NT, STAGES, false, true>() : make_variant<D, NT, STAGES, false, false>();
 }
 
 // Stage counts keep two CTAs per SM resident (<= ~110 KB each) except at
 // dim 256, where one CTA per SM holds four 33 KB stages.
-FastVariant fast_variant(uint32_t dim, uint32_t nt, uint32_t page_tokens) {
+FastVariant fast_variant(uint32_t dim, uint32_t nt, uint32_t page_tokens, bool batched) {
   const bool small = page_tokens < kvb::kStageTokens;
-  if (dim == 128 && nt == 1) return make_variant<128, 1, 5>(small);
-  if (dim == 128 && nt == 2) return make_variant<128, 2, 4>(small);
-  if (dim == 64 && nt == 1) return make_variant<64, 1, 8>(small);
-  if (dim == 64 && nt == 2) return make_variant<64, 2, 7>(small);
-  if (dim == 256 && nt == 1) return make_variant<256, 1, 4>(small);
+  if (dim == 128 && nt == 1) return make_variant<128, 1, 5>(small, batched);
+  if (dim == 128 && nt == 2 && batched) return make_variant<128, 2, 4>(small, batched);
+  if (dim == 64 && nt == 1) return make_variant<64, 1, 8>(small, batched);
+  if (dim == 64 && nt == 2 && batched) return make_variant<64, 2, 7>(small, batched);
+  if (dim == 256 && nt == 1) return make_variant<256, 1, 4>(small, batched);
   return FastVariant{};
 }
 
@@ -259,7 +268,7 @@ unsigned attention_partitions(const Shape& s, unsigned requested) {
   uint32_t parts = requested;
   if (parts == 0) {
     const ColumnPlan plan = column_plan(s.dim, query_rows(s));
-    const FastVariant v = fast_variant(s.dim, plan.nt, s.page_tokens);
+    const FastVariant v = fast_variant(s.dim, plan.nt, s.page_tokens, false);
     const uint32_t wave =
         v.fn ? uint32_t(current_device_facts().sms) * uint32_t(resident_ctas(v)) : 1u;
     parts = std::max(1u, wave / (s.kv_heads * plan.groups));
@@ -298,9 +307,10 @@ cudaError_t preload_attention_mma_kernels() {
   if (code != cudaSuccess) return code;
   if (major != 10) return cudaErrorNotSupported;
   const std::pair<uint32_t, uint32_t> variants[] = {{128, 1}, {128, 2}, {64, 1}, {64, 2}, {256, 1}};
-  for (int small = 0; small < 2; ++small) {
+  for (int mode = 0; mode < 4; ++mode) {
     for (const auto& dv : variants) {
-      const FastVariant v = fast_variant(dv.first, dv.second, small ? 16u : 64u);
+      const FastVariant v = fast_variant(dv.first, dv.second, mode & 1 ? 16u : 64u, mode >= 2);
+      if (v.fn == nullptr) continue;
       cudaFuncAttributes a{};
       code = cudaFuncGetAttributes(&a, v.fn);
       if (code != cudaSuccess) return code;
@@ -374,7 +384,7 @@ unsigned launch_attention_partials(const Shape& s, const DeviceInput& in, unsign
   if (parts == 0) return 0;
   kvb::DecodeParams prm = single_params(s, in, parts, scratch, splits);
   prm.prefetch_stages = kPrefetchStages;
-  fast_variant(s.dim, prm.group_cols / 8, s.page_tokens).launch(prm, stream);
+  fast_variant(s.dim, prm.group_cols / 8, s.page_tokens, false).launch(prm, stream);
   return parts;
 }
 
@@ -459,7 +469,7 @@ const char* batch_shape_error(const BatchShape& s) noexcept {
 size_t batch_workspace_bytes(const BatchShape& s) {
   if (const char* e = batch_shape_error(s)) throw std::invalid_argument(e);
   const uint32_t group = s.q_heads / s.kv_heads;
-  const FastVariant v = fast_variant(s.dim, (group + 7) / 8, s.page_tokens);
+  const FastVariant v = fast_variant(s.dim, (group + 7) / 8, s.page_tokens, true);
   const uint64_t slots = uint64_t(batched_ctas(v)) + uint64_t(s.batch) * s.kv_heads;
   return size_t(slots * group * (s.dim + 2) * sizeof(float));
 }
@@ -477,7 +487,7 @@ void launch_attention_batched(const BatchShape& s, const BatchInput& in, void* w
   if (workspace_bytes < batch_workspace_bytes(s))
     throw std::invalid_argument("workspace smaller than batch_workspace_bytes(shape)");
   const uint32_t group = s.q_heads / s.kv_heads;
-  const FastVariant v = fast_variant(s.dim, (group + 7) / 8, s.page_tokens);
+  const FastVariant v = fast_variant(s.dim, (group + 7) / 8, s.page_tokens, true);
   kvb::DecodeParams prm{};
   prm.q = in.q;
   prm.table = in.block_table;
@@ -667,7 +677,7 @@ void launch_attention_noalloc(const Shape& s, const DeviceInput& in, unsigned pa
   if (parts > 0) {
     // Partials packed [row-head][partition]: split stride = parts.
     const kvb::DecodeParams prm = single_params(s, in, parts, scratch, parts);
-    fast_variant(s.dim, prm.group_cols / 8, s.page_tokens).launch(prm, stream);
+    fast_variant(s.dim, prm.group_cols / 8, s.page_tokens, false).launch(prm, stream);
   }
   launch_merge(kvb::kMergeScratch,
                scratch_merge_params(s, scratch, parts, parts, false, m, l, n, out_f16), stream);

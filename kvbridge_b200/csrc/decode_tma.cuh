@@ -198,14 +198,15 @@ __device__ __forceinline__ Piece single_piece(const DecodeParams& p, uint32_t c)
 }
 
 // The piece starting at global stage x of CTA c whose range ends at x_end.
+template <bool BATCHED>
 __device__ __forceinline__ Piece locate_piece(const DecodeParams& p, uint64_t x, uint64_t x_end,
                                               uint64_t total, uint32_t c) {
-  if (p.seq_lens == nullptr) return single_piece(p, c);
+  if (!BATCHED) return single_piece(p, c);
   Piece pc;
   pc.col0 = 0;
   uint64_t seg_base;
   uint32_t seg_len;
-  if (p.seq_lens == nullptr) {
+  if (!BATCHED) {
     pc.b = 0;
     pc.lo = p.begin;
     pc.hi = p.end;
@@ -224,7 +225,7 @@ __device__ __forceinline__ Piece locate_piece(const DecodeParams& p, uint64_t x,
   pc.j0 = static_cast<uint32_t>(x - seg_off);
   const uint64_t rem = x_end - seg_off;
   pc.j1 = rem < seg_len ? static_cast<uint32_t>(rem) : seg_len;
-  if (p.seq_lens == nullptr)
+  if (!BATCHED)
     pc.slot = c - cta_of_stage(seg_off, total, p.ctas);
   else
     pc.slot = c + pc.b * p.kv_heads + pc.h;
@@ -299,7 +300,7 @@ __device__ __forceinline__ void drain_copies(uint64_t* full, uint32_t g) {
 // registers that take turns (no register copies, which would wait for the
 // loads). With 64-token pages the extra per-stage work costs more than the
 // two copies it saves, so produce() keeps those.
-template <int D, int STAGES>
+template <int D, int STAGES, bool BATCHED>
 __device__ void produce_small_pages(const DecodeParams& p, uint8_t* ring, uint64_t* full,
                                     uint64_t* empty, volatile uint32_t* tags,
                                     volatile int* abort_flag, uint64_t x0, uint64_t x1,
@@ -319,12 +320,12 @@ __device__ void produce_small_pages(const DecodeParams& p, uint8_t* ring, uint64
   uint32_t g = 0;  // stages issued so far (CTA stage sequence number)
   bool failed = false;
   for (uint64_t x = x0; x < x1 && !failed;) {
-    const Piece pc = locate_piece(p, x, x1, total, blockIdx.x);
+    const Piece pc = locate_piece<BATCHED>(p, x, x1, total, blockIdx.x);
     const uint32_t first_stage = pc.lo / kStageTokens;
     const uint32_t page_lo = max(pc.lo, (first_stage + pc.j0) * kStageTokens) >> p.log2_page;
     const uint32_t page_hi = (min(pc.hi, (first_stage + pc.j1) * kStageTokens) - 1) >> p.log2_page;
     const uint32_t* trow =
-        p.seq_lens == nullptr ? p.table : p.table + size_t(pc.b) * p.table_stride;
+        !BATCHED ? p.table : p.table + size_t(pc.b) * p.table_stride;
     // Table entry of this lane's page of stage j (in flight after return).
     auto table_load = [&](uint32_t j, uint32_t& t, bool& mine) {
       const uint32_t pg = (first_stage + j) * pps + q;
@@ -395,7 +396,7 @@ __device__ void produce_small_pages(const DecodeParams& p, uint8_t* ring, uint64
   drain_copies<STAGES>(full, g);
 }
 
-template <int D, int STAGES>
+template <int D, int STAGES, bool BATCHED>
 __device__ void produce(const DecodeParams& p, uint8_t* ring, uint64_t* full, uint64_t* empty,
                         volatile uint32_t* tags, volatile int* abort_flag, uint64_t x0, uint64_t x1,
                         uint64_t total) {
@@ -429,12 +430,12 @@ __device__ void produce(const DecodeParams& p, uint8_t* ring, uint64_t* full, ui
   uint32_t g = 0;  // stages issued so far (CTA stage sequence number)
   bool failed = false;
   for (uint64_t x = x0; x < x1 && !failed;) {
-    const Piece pc = locate_piece(p, x, x1, total, blockIdx.x);
+    const Piece pc = locate_piece<BATCHED>(p, x, x1, total, blockIdx.x);
     const uint32_t first_stage = pc.lo / kStageTokens;
     const uint32_t page_lo = max(pc.lo, (first_stage + pc.j0) * kStageTokens) >> p.log2_page;
     const uint32_t page_hi = (min(pc.hi, (first_stage + pc.j1) * kStageTokens) - 1) >> p.log2_page;
     const uint32_t* trow =
-        p.seq_lens == nullptr ? p.table : p.table + size_t(pc.b) * p.table_stride;
+        !BATCHED ? p.table : p.table + size_t(pc.b) * p.table_stride;
     // This lane's page of the batch starting at stage j, if the piece reads it.
     auto batch_page = [&](uint32_t j, uint32_t& pg) {
       pg = (first_stage + j) * pps + lane_page;
@@ -527,7 +528,7 @@ __device__ __forceinline__ uint32_t pack_s8x4(int a, int b, int c, int d) {
          (uint32_t(d) << 24);
 }
 
-template <int D, int NT>
+template <int D, int NT, bool BATCHED>
 __device__ __forceinline__ void load_query(const DecodeParams& p, const Piece& pc,
                                            QueryFrags<D, NT>& qf) {
   const uint32_t lane = threadIdx.x & 31, grp = lane >> 2, tig = lane & 3;
@@ -536,7 +537,7 @@ __device__ __forceinline__ void load_query(const DecodeParams& p, const Piece& p
     const uint32_t col = pc.col0 + 8 * nt + grp;
     const bool valid = col < p.qr;
     const uint32_t r = valid ? col / p.group : 0, g = valid ? col % p.group : 0;
-    const uint32_t row = p.seq_lens == nullptr ? r : pc.b;
+    const uint32_t row = !BATCHED ? r : pc.b;
     const float* qrow = p.q + (size_t(row) * p.q_heads + size_t(pc.h) * p.group + g) * D;
     float vals[D / 64][16];
     float amax = 0.f;
@@ -586,7 +587,7 @@ __device__ __forceinline__ void load_query(const DecodeParams& p, const Piece& p
       qf.cf[nt][ee] = __shfl_sync(0xffffffffu, cf_b, 4 * (2 * tig + ee));
       const uint32_t ccol = pc.col0 + 8 * nt + 2 * tig + ee;
       int64_t qp = INT64_MAX;
-      if (p.seq_lens == nullptr && ccol < p.qr) qp = __ldg(p.q_positions + ccol / p.group);
+      if (!BATCHED && ccol < p.qr) qp = __ldg(p.q_positions + ccol / p.group);
       qf.qpos[nt][ee] = qp;
     }
   }
@@ -842,7 +843,7 @@ __device__ __forceinline__ void consume_stage(const DecodeParams& p, const uint8
 // SMALL_PAGES: pages shorter than a stage (produce_small_pages); a separate
 // instantiation, so that the 64-token-page kernel does not carry that code
 // (which cost it ~0.6 us a call at cfg2 when both producers were compiled in).
-template <int D, int NT, int STAGES, bool SMALL_PAGES>
+template <int D, int NT, int STAGES, bool SMALL_PAGES, bool BATCHED>
 __global__ void __launch_bounds__(kDecodeThreads, 2) decode_partial_kernel(DecodeParams p) {
   using L = DecodeSmem<D, NT, STAGES>;
   extern __shared__ __align__(128) uint8_t smem[];
@@ -865,14 +866,14 @@ __global__ void __launch_bounds__(kDecodeThreads, 2) decode_partial_kernel(Decod
     fence_barrier_init();
   }
   __syncthreads();
-  if (warp == kProducerWarp && p.prefetch_stages != 0 && p.seq_lens == nullptr)
+  if (warp == kProducerWarp && p.prefetch_stages != 0 && !BATCHED)
     prefetch_first_stages<D>(p, p.prefetch_stages);
   // Inputs may be produced by the preceding kernel on the stream.
   grid_dependency_wait();
 
-  const uint64_t total = p.seq_lens == nullptr ? p.total_stages : batched_total(p);
+  const uint64_t total = !BATCHED ? p.total_stages : batched_total(p);
   uint64_t x0, x1;
-  if (p.seq_lens == nullptr) {
+  if (!BATCHED) {
     const Piece only = single_piece(p, blockIdx.x);
     x0 = uint64_t(only.h) * p.seg_stages + only.j0;
     x1 = x0 + (only.j1 - only.j0);
@@ -883,23 +884,23 @@ __global__ void __launch_bounds__(kDecodeThreads, 2) decode_partial_kernel(Decod
 
   if (warp == kProducerWarp) {
     if constexpr (SMALL_PAGES)
-      produce_small_pages<D, STAGES>(p, ring, full, empty, tags, abort_flag, x0, x1, total);
+      produce_small_pages<D, STAGES, BATCHED>(p, ring, full, empty, tags, abort_flag, x0, x1, total);
     else
-      produce<D, STAGES>(p, ring, full, empty, tags, abort_flag, x0, x1, total);
+      produce<D, STAGES, BATCHED>(p, ring, full, empty, tags, abort_flag, x0, x1, total);
     return;
   }
 
   const uint32_t grp = lane >> 2, tig = lane & 3;
   uint32_t g_base = 0;  // CTA stage sequence number of the piece's first stage
   for (uint64_t x = x0; x < x1;) {
-    const Piece pc = locate_piece(p, x, x1, total, blockIdx.x);
+    const Piece pc = locate_piece<BATCHED>(p, x, x1, total, blockIdx.x);
     const uint32_t first_stage = pc.lo / kStageTokens;
     QueryFrags<D, NT> qf;
-    load_query<D, NT>(p, pc, qf);
+    load_query<D, NT, BATCHED>(p, pc, qf);
     // Causality: k_positions is nondecreasing, so the piece is fully visible
     // when its last token is visible to every query row.
     bool all_visible = true;
-    if (p.seq_lens == nullptr) {
+    if (!BATCHED) {
       const uint32_t last = min(pc.hi, (first_stage + pc.j1) * kStageTokens) - 1;
       const int64_t kp = __ldg(p.k_positions + last);
       const bool row_ok = lane >= p.rows || kp <= __ldg(p.q_positions + lane);
@@ -983,7 +984,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 2) decode_partial_kernel(Decod
         Lsum += ew[w] * stats[(w * L::kCols + col) * 2 + 1];
       }
       size_t base;
-      if (p.seq_lens == nullptr) {
+      if (!BATCHED) {
         const uint32_t r = gcol / p.group, gq = gcol % p.group;
         const size_t rh = size_t(r) * p.q_heads + size_t(pc.h) * p.group + gq;
         base = (rh * p.split_stride + pc.slot) * (D + 2);
