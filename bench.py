@@ -265,7 +265,9 @@ def run_reference_arm(args):
             "cores": threads,
             "kind": kind,
             "sample": f"each step: the last {tokens} of 65,536 tokens for all 32 q-heads "
-                      f"({threads} threads, FP64 oracle)",
+                      f"({threads} threads, "
+                      + ("the reference's FP64 CPU oracle built from its sources)" if kind == "reference"
+                         else "the C restatement of the reference's FP64 oracle)"),
         },
         "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -529,7 +531,7 @@ def main():
         ),
         "roofline": {
             "bound": "hbm",
-            "kernel": "decode_partial_kernel<128,1,5,false>",
+            "kernel": "decode_partial_kernel<128,1,5,false,false>",
             "achieved": round(achieved, 2),
             "peak": peak,
             "unit": "GB/s",
