@@ -75,6 +75,17 @@ void launch_pdl(const void* fn, dim3 grid, dim3 block, uint32_t smem, cudaStream
   cuda_ok(cudaLaunchKernelExC(&cfg, fn, args), what);
 }
 
+// The merge kernels use 4 KB of shared memory, and left to itself the driver
+// gives an SM running one a small shared-memory carveout. A partial-kernel CTA
+// (two per SM at ~100 KB each) cannot start on that SM until the merge CTA
+// has left and the SM has been reconfigured, which held back the next call's
+// CTAs on every SM that ran a merge CTA (~3.5 us late at 64K tokens). Asking
+// for the largest carveout keeps both kernels on one configuration.
+cudaError_t prefer_max_shared(const void* fn) {
+  return cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout,
+                              int(cudaSharedmemCarveoutMaxShared));
+}
+
 template <int D, int NT, int STAGES, bool SMALL, bool BATCHED>
 void launch_fast_variant(const kvb::DecodeParams& prm, cudaStream_t stream) {
   const void* fn =
@@ -82,6 +93,7 @@ void launch_fast_variant(const kvb::DecodeParams& prm, cudaStream_t stream) {
   constexpr uint32_t smem = kvb::DecodeSmem<D, NT, STAGES>::kBytes;
   cuda_ok(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)),
           "decode kernel shared-memory opt-in");
+  cuda_ok(prefer_max_shared(fn), "decode kernel carveout");
   kvb::DecodeParams copy = prm;
   void* args[] = {&copy};
   launch_pdl(fn, dim3(prm.ctas), dim3(kvb::kDecodeThreads), smem, stream, args,
@@ -196,6 +208,7 @@ void launch_merge(int mode, const kvb::MergeParams& prm, cudaStream_t stream) {
   kvb::MergeParams copy = prm;
   void* args[] = {&copy};
   const void* fn = merge_fn(mode, prm.dim);
+  cuda_ok(prefer_max_shared(fn), "merge kernel carveout");
   launch_pdl(fn, dim3(blocks), dim3(32 * kvb::kMergeWarps), 0, stream, args,
              "attention merge launch");
 }
@@ -293,7 +306,10 @@ cudaError_t preload_attention_reference_kernels() {
       merge_fn(kvb::kMergeShards, 256),
   };
   for (const void* fn : fns) {
-    const cudaError_t code = cudaFuncGetAttributes(&a, fn);
+    cudaError_t code = cudaFuncGetAttributes(&a, fn);
+    // The merges (every entry after the two SIMT kernels) share the partial
+    // kernels' shared-memory configuration.
+    if (code == cudaSuccess && fn != fns[0] && fn != fns[1]) code = prefer_max_shared(fn);
     if (code != cudaSuccess) return code;
   }
   return cudaSuccess;

@@ -199,9 +199,9 @@ __device__ __forceinline__ Piece single_piece(const DecodeParams& p, uint32_t c)
 
 // The piece starting at global stage x of CTA c whose range ends at x_end.
 template <bool BATCHED>
-__device__ __forceinline__ Piece locate_piece(const DecodeParams& p, uint64_t x, uint64_t x_end,
-                                              uint64_t total, uint32_t c) {
-  if (!BATCHED) return single_piece(p, c);
+__device__ __forceinline__ Piece locate_piece(const DecodeParams& p, const Piece& only, uint64_t x,
+                                              uint64_t x_end, uint64_t total, uint32_t c) {
+  if (!BATCHED) return only;
   Piece pc;
   pc.col0 = 0;
   uint64_t seg_base;
@@ -237,6 +237,22 @@ __device__ __forceinline__ uint64_t piece_end_stage(const DecodeParams& p, const
   return x + (pc.j1 - pc.j0);
 }
 
+// The CTA's global stage range [x0, x1) and the call's stage count. A batched
+// call reads the sequence lengths, so this runs after the dependency wait.
+template <bool BATCHED>
+__device__ __forceinline__ void cta_stage_range(const DecodeParams& p, const Piece& only,
+                                                uint64_t& total, uint64_t& x0, uint64_t& x1) {
+  if (!BATCHED) {
+    total = p.total_stages;
+    x0 = uint64_t(only.h) * p.seg_stages + only.j0;
+    x1 = x0 + (only.j1 - only.j0);
+  } else {
+    total = batched_total(p);
+    x0 = cta_stage_begin(blockIdx.x, total, p.ctas);
+    x1 = cta_stage_begin(blockIdx.x + 1, total, p.ctas);
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Producer: one warp, bulk copies of whole pages.
 
@@ -247,9 +263,8 @@ __device__ __forceinline__ uint64_t piece_end_stage(const DecodeParams& p, const
 // (read through L2, so that no stale copy stays in L1), out-of-range entries
 // are skipped, and the copies proper re-read everything after the wait.
 template <int D>
-__device__ void prefetch_first_stages(const DecodeParams& p, uint32_t count) {
+__device__ void prefetch_first_stages(const DecodeParams& p, const Piece& pc, uint32_t count) {
   const uint32_t lane = threadIdx.x & 31;
-  const Piece pc = single_piece(p, blockIdx.x);
   const uint32_t first_stage = pc.lo / kStageTokens;
   const uint32_t j_end = min(pc.j1, pc.j0 + count);
   const uint32_t tok_lo = max(pc.lo, (first_stage + pc.j0) * kStageTokens);
@@ -271,6 +286,29 @@ __device__ void prefetch_first_stages(const DecodeParams& p, uint32_t count) {
     prefetch_l2(p.v + unit * D * P, D * P);
     prefetch_l2(p.k_scales + unit * P, 4 * P);
     prefetch_l2(p.v_scales + unit * P, 4 * P);
+  }
+}
+
+// Single sequence, before the dependency wait: L2 prefetch of the query rows
+// of the CTA's columns and of the two position words the piece setup reads.
+// A hint only: the setup loads them again after the wait. (Under a streaming
+// call those lines are often no longer in L2, and a miss behind the first
+// copies of every CTA took ~1.5 us.)
+template <int D, int NT>
+__device__ void prefetch_query_lines(const DecodeParams& p, const Piece& pc) {
+  const uint32_t lane = threadIdx.x & 31;
+  if (pc.j1 <= pc.j0) return;
+  constexpr uint32_t kLines = D * 4 / 128;  // 128-byte lines of one fp32 query row
+  for (uint32_t i = lane; i < 8u * NT * kLines; i += 32) {
+    const uint32_t col = pc.col0 + i / kLines;
+    if (col >= p.qr) break;
+    const uint32_t r = col / p.group, g = col % p.group;
+    prefetch_line_l2(p.q + (size_t(r) * p.q_heads + size_t(pc.h) * p.group + g) * D + (i % kLines) * 32);
+  }
+  if (lane == 0) {
+    const uint32_t first_stage = pc.lo / kStageTokens;
+    prefetch_line_l2(p.k_positions + (min(pc.hi, (first_stage + pc.j1) * kStageTokens) - 1));
+    prefetch_line_l2(p.q_positions + pc.col0 / p.group);
   }
 }
 
@@ -301,10 +339,9 @@ __device__ __forceinline__ void drain_copies(uint64_t* full, uint32_t g) {
 // loads). With 64-token pages the extra per-stage work costs more than the
 // two copies it saves, so produce() keeps those.
 template <int D, int STAGES, bool BATCHED>
-__device__ void produce_small_pages(const DecodeParams& p, uint8_t* ring, uint64_t* full,
-                                    uint64_t* empty, volatile uint32_t* tags,
-                                    volatile int* abort_flag, uint64_t x0, uint64_t x1,
-                                    uint64_t total) {
+__device__ void produce_small_pages(const DecodeParams& p, const Piece& only, uint8_t* ring,
+                                    uint64_t* full, uint64_t* empty, volatile uint32_t* tags,
+                                    volatile int* abort_flag) {
   const uint32_t lane = threadIdx.x & 31;
   const uint64_t policy = l2_evict_first_policy();
   const uint32_t P = p.page_tokens;
@@ -317,10 +354,13 @@ __device__ void produce_small_pages(const DecodeParams& p, uint8_t* ring, uint64
   const bool copier = (tok4 & (P - 1u)) == 0u;
   const float* scale_base = is_v ? p.v_scales : p.k_scales;
   const uint32_t scale_off = is_v ? StageLayout<D>::kVs : StageLayout<D>::kKs;
+  grid_dependency_wait();
+  uint64_t total, x0, x1;
+  cta_stage_range<BATCHED>(p, only, total, x0, x1);
   uint32_t g = 0;  // stages issued so far (CTA stage sequence number)
   bool failed = false;
   for (uint64_t x = x0; x < x1 && !failed;) {
-    const Piece pc = locate_piece<BATCHED>(p, x, x1, total, blockIdx.x);
+    const Piece pc = locate_piece<BATCHED>(p, only, x, x1, total, blockIdx.x);
     const uint32_t first_stage = pc.lo / kStageTokens;
     const uint32_t page_lo = max(pc.lo, (first_stage + pc.j0) * kStageTokens) >> p.log2_page;
     const uint32_t page_hi = (min(pc.hi, (first_stage + pc.j1) * kStageTokens) - 1) >> p.log2_page;
@@ -397,9 +437,8 @@ __device__ void produce_small_pages(const DecodeParams& p, uint8_t* ring, uint64
 }
 
 template <int D, int STAGES, bool BATCHED>
-__device__ void produce(const DecodeParams& p, uint8_t* ring, uint64_t* full, uint64_t* empty,
-                        volatile uint32_t* tags, volatile int* abort_flag, uint64_t x0, uint64_t x1,
-                        uint64_t total) {
+__device__ void produce(const DecodeParams& p, const Piece& only, uint8_t* ring, uint64_t* full,
+                        uint64_t* empty, volatile uint32_t* tags, volatile int* abort_flag) {
   const uint32_t lane = threadIdx.x & 31;
   const uint64_t policy = l2_evict_first_policy();
   const uint32_t P = p.page_tokens;
@@ -427,10 +466,13 @@ __device__ void produce(const DecodeParams& p, uint8_t* ring, uint64_t* full, ui
     part_bytes = 4 * P;
     dst_off = (part == 2 ? StageLayout<D>::kKs : StageLayout<D>::kVs) + page_in_stage * P * 4;
   }
+  grid_dependency_wait();
+  uint64_t total, x0, x1;
+  cta_stage_range<BATCHED>(p, only, total, x0, x1);
   uint32_t g = 0;  // stages issued so far (CTA stage sequence number)
   bool failed = false;
   for (uint64_t x = x0; x < x1 && !failed;) {
-    const Piece pc = locate_piece<BATCHED>(p, x, x1, total, blockIdx.x);
+    const Piece pc = locate_piece<BATCHED>(p, only, x, x1, total, blockIdx.x);
     const uint32_t first_stage = pc.lo / kStageTokens;
     const uint32_t page_lo = max(pc.lo, (first_stage + pc.j0) * kStageTokens) >> p.log2_page;
     const uint32_t page_hi = (min(pc.hi, (first_stage + pc.j1) * kStageTokens) - 1) >> p.log2_page;
@@ -528,10 +570,25 @@ __device__ __forceinline__ uint32_t pack_s8x4(int a, int b, int c, int d) {
          (uint32_t(d) << 24);
 }
 
+// Loads the piece's query operands and, for a single sequence, returns
+// whether every token of the piece is visible to every query row of the
+// CTA's columns (k_positions is nondecreasing, so it is enough that the
+// piece's last token `last_token` is). Every global load of this setup (Q
+// rows, their positions, the last key position) is issued before any is
+// used, so the setup costs one memory round trip.
 template <int D, int NT, bool BATCHED>
-__device__ __forceinline__ void load_query(const DecodeParams& p, const Piece& pc,
-                                           QueryFrags<D, NT>& qf) {
+__device__ __forceinline__ bool load_query(const DecodeParams& p, const Piece& pc,
+                                           uint32_t last_token, QueryFrags<D, NT>& qf) {
   const uint32_t lane = threadIdx.x & 31, grp = lane >> 2, tig = lane & 3;
+  // Visibility: lane j < 8 * NT checks the row of column col0 + j.
+  int64_t kp_last = 0, qp_own = INT64_MAX;
+  if (!BATCHED) {
+    kp_last = __ldg(p.k_positions + last_token);
+    const uint32_t ocol = pc.col0 + lane;
+    if (lane < 8u * NT && ocol < p.qr) qp_own = __ldg(p.q_positions + ocol / p.group);
+  }
+  float vals[NT][D / 64][16];
+  int64_t qp[NT][2];
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) {
     const uint32_t col = pc.col0 + 8 * nt + grp;
@@ -539,21 +596,32 @@ __device__ __forceinline__ void load_query(const DecodeParams& p, const Piece& p
     const uint32_t r = valid ? col / p.group : 0, g = valid ? col % p.group : 0;
     const uint32_t row = !BATCHED ? r : pc.b;
     const float* qrow = p.q + (size_t(row) * p.q_heads + size_t(pc.h) * p.group + g) * D;
-    float vals[D / 64][16];
-    float amax = 0.f;
 #pragma unroll
     for (int c = 0; c < D / 64; ++c) {
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        float4 f = valid ? __ldg(reinterpret_cast<const float4*>(qrow + 64 * c + 16 * tig) + i)
-                         : make_float4(0.f, 0.f, 0.f, 0.f);
-        vals[c][4 * i + 0] = f.x;
-        vals[c][4 * i + 1] = f.y;
-        vals[c][4 * i + 2] = f.z;
-        vals[c][4 * i + 3] = f.w;
-        amax = fmaxf(amax, fmaxf(fmaxf(fabsf(f.x), fabsf(f.y)), fmaxf(fabsf(f.z), fabsf(f.w))));
+        const float4 f = valid ? __ldg(reinterpret_cast<const float4*>(qrow + 64 * c + 16 * tig) + i)
+                               : make_float4(0.f, 0.f, 0.f, 0.f);
+        vals[nt][c][4 * i + 0] = f.x;
+        vals[nt][c][4 * i + 1] = f.y;
+        vals[nt][c][4 * i + 2] = f.z;
+        vals[nt][c][4 * i + 3] = f.w;
       }
     }
+    // C layout: this thread's columns are 2*tig and 2*tig+1 of the n-tile.
+#pragma unroll
+    for (int ee = 0; ee < 2; ++ee) {
+      const uint32_t ccol = pc.col0 + 8 * nt + 2 * tig + ee;
+      qp[nt][ee] = (!BATCHED && ccol < p.qr) ? __ldg(p.q_positions + ccol / p.group) : INT64_MAX;
+    }
+  }
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    float amax = 0.f;
+#pragma unroll
+    for (int c = 0; c < D / 64; ++c)
+#pragma unroll
+      for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(vals[nt][c][i]));
     amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
     amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
     // 2^e > max|q|; q * 2^(22-e) rounds to an integer of magnitude <= 2^22.
@@ -570,7 +638,7 @@ __device__ __forceinline__ void load_query(const DecodeParams& p, const Piece& p
           int l[3][4];
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
-            const int qi = __float2int_rn(vals[c][8 * jj + 4 * half + i] * up);
+            const int qi = __float2int_rn(vals[nt][c][8 * jj + 4 * half + i] * up);
             split_limbs(qi, l[0][i], l[1][i], l[2][i]);
           }
 #pragma unroll
@@ -580,17 +648,15 @@ __device__ __forceinline__ void load_query(const DecodeParams& p, const Piece& p
       }
     }
     const float cf_b = p.score_scale * kLog2e * __uint_as_float(uint32_t(127 + e - 22) << 23);
-    // C layout: this thread's columns are 2*tig and 2*tig+1 of the n-tile;
-    // their factor lives in lane 4*column.
+    // The factor of column 2*tig+ee lives in lane 4*(2*tig+ee).
 #pragma unroll
     for (int ee = 0; ee < 2; ++ee) {
       qf.cf[nt][ee] = __shfl_sync(0xffffffffu, cf_b, 4 * (2 * tig + ee));
-      const uint32_t ccol = pc.col0 + 8 * nt + 2 * tig + ee;
-      int64_t qp = INT64_MAX;
-      if (!BATCHED && ccol < p.qr) qp = __ldg(p.q_positions + ccol / p.group);
-      qf.qpos[nt][ee] = qp;
+      qf.qpos[nt][ee] = qp[nt][ee];
     }
   }
+  if (BATCHED) return true;
+  return __all_sync(0xffffffffu, kp_last <= qp_own);
 }
 
 // One 64-token stage for one warp.
@@ -866,46 +932,32 @@ __global__ void __launch_bounds__(kDecodeThreads, 2) decode_partial_kernel(Decod
     fence_barrier_init();
   }
   __syncthreads();
-  if (warp == kProducerWarp && p.prefetch_stages != 0 && !BATCHED)
-    prefetch_first_stages<D>(p, p.prefetch_stages);
-  // Inputs may be produced by the preceding kernel on the stream.
-  grid_dependency_wait();
-
-  const uint64_t total = !BATCHED ? p.total_stages : batched_total(p);
-  uint64_t x0, x1;
-  if (!BATCHED) {
-    const Piece only = single_piece(p, blockIdx.x);
-    x0 = uint64_t(only.h) * p.seg_stages + only.j0;
-    x1 = x0 + (only.j1 - only.j0);
-  } else {
-    x0 = cta_stage_begin(blockIdx.x, total, p.ctas);
-    x1 = cta_stage_begin(blockIdx.x + 1, total, p.ctas);
-  }
-
+  // A single sequence's piece depends on the launch parameters only, so it
+  // is worked out before the dependency wait on the preceding grid (which
+  // may still be writing the inputs); each role waits just before its first
+  // read of an input.
+  const Piece only = !BATCHED ? single_piece(p, blockIdx.x) : Piece{};
   if (warp == kProducerWarp) {
+    if (!BATCHED && p.prefetch_stages != 0) prefetch_first_stages<D>(p, only, p.prefetch_stages);
     if constexpr (SMALL_PAGES)
-      produce_small_pages<D, STAGES, BATCHED>(p, ring, full, empty, tags, abort_flag, x0, x1, total);
+      produce_small_pages<D, STAGES, BATCHED>(p, only, ring, full, empty, tags, abort_flag);
     else
-      produce<D, STAGES, BATCHED>(p, ring, full, empty, tags, abort_flag, x0, x1, total);
+      produce<D, STAGES, BATCHED>(p, only, ring, full, empty, tags, abort_flag);
     return;
   }
+  if (warp == 0 && !BATCHED && p.prefetch_stages != 0) prefetch_query_lines<D, NT>(p, only);
+  grid_dependency_wait();
+  uint64_t total, x0, x1;
+  cta_stage_range<BATCHED>(p, only, total, x0, x1);
 
   const uint32_t grp = lane >> 2, tig = lane & 3;
   uint32_t g_base = 0;  // CTA stage sequence number of the piece's first stage
   for (uint64_t x = x0; x < x1;) {
-    const Piece pc = locate_piece<BATCHED>(p, x, x1, total, blockIdx.x);
+    const Piece pc = locate_piece<BATCHED>(p, only, x, x1, total, blockIdx.x);
     const uint32_t first_stage = pc.lo / kStageTokens;
     QueryFrags<D, NT> qf;
-    load_query<D, NT, BATCHED>(p, pc, qf);
-    // Causality: k_positions is nondecreasing, so the piece is fully visible
-    // when its last token is visible to every query row.
-    bool all_visible = true;
-    if (!BATCHED) {
-      const uint32_t last = min(pc.hi, (first_stage + pc.j1) * kStageTokens) - 1;
-      const int64_t kp = __ldg(p.k_positions + last);
-      const bool row_ok = lane >= p.rows || kp <= __ldg(p.q_positions + lane);
-      all_visible = __all_sync(0xffffffffu, row_ok);
-    }
+    const uint32_t last = min(pc.hi, (first_stage + pc.j1) * kStageTokens) - 1;
+    const bool all_visible = load_query<D, NT, BATCHED>(p, pc, last, qf);
     WarpState<D, NT> ws;
 #pragma unroll
     for (int md = 0; md < D / 16; ++md)

@@ -210,6 +210,22 @@ def test_query_column_groups(cuda_device, rows, q_heads, kv_heads, dim, page_tok
         check_against_oracle(res, case.shape, ref, f"groups {rows}x{q_heads // kv_heads} d{dim} P{partitions}")
 
 
+def test_causal_visibility_of_every_row(cuda_device):
+    """40 query rows with group 1 (five column groups) whose positions fall
+    with the row index, so that the rows past the first 32 are the ones that
+    see the fewest tokens: each CTA's whole-piece visibility test must cover
+    the rows of its own columns."""
+    tokens, rows = 3000, 40
+    qpos = [tokens - 1 - 9 * r for r in range(rows)]
+    case = make(cuda_device, rows=rows, q_heads=4, kv_heads=4, dim=128, page_tokens=64, tokens=tokens, seed=77,
+                q_positions=qpos)
+    assert kvb.attention_b200_supported(case.shape, case.device_input())
+    ref = oracle.reference_case(case, threads=8)
+    for partitions in (0, 7):
+        res = run_single(case, partitions=partitions)
+        check_against_oracle(res, case.shape, ref, f"falling positions P{partitions}")
+
+
 def test_mma_launcher_contract(cuda_device):
     """launch_attention_mma keeps the reference predicate: its native shape
     runs, BASELINE shapes are rejected with ValueError before launch."""
