@@ -531,7 +531,7 @@ def main():
         ),
         "roofline": {
             "bound": "hbm",
-            "kernel": "decode_partial_kernel<128,1,5,false,false>",
+            "kernel": "decode_partial_kernel<128,1,6,false,false>",
             "achieved": round(achieved, 2),
             "peak": peak,
             "unit": "GB/s",

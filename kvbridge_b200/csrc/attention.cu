@@ -90,7 +90,7 @@ template <int D, int NT, int STAGES, bool SMALL, bool BATCHED>
 void launch_fast_variant(const kvb::DecodeParams& prm, cudaStream_t stream) {
   const void* fn =
       reinterpret_cast<const void*>(&kvb::decode_partial_kernel<D, NT, STAGES, SMALL, BATCHED>);
-  constexpr uint32_t smem = kvb::DecodeSmem<D, NT, STAGES>::kBytes;
+  constexpr uint32_t smem = kvb::DecodeSmem<D, NT, STAGES, !BATCHED>::kBytes;
   cuda_ok(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)),
           "decode kernel shared-memory opt-in");
   cuda_ok(prefer_max_shared(fn), "decode kernel carveout");
@@ -104,7 +104,7 @@ template <int D, int NT, int STAGES, bool SMALL, bool BATCHED>
 FastVariant make_variant() {
   FastVariant v;
   v.fn = reinterpret_cast<const void*>(&kvb::decode_partial_kernel<D, NT, STAGES, SMALL, BATCHED>);
-  v.smem = kvb::DecodeSmem<D, NT, STAGES>::kBytes;
+  v.smem = kvb::DecodeSmem<D, NT, STAGES, !BATCHED>::kBytes;
   v.launch = &launch_fast_variant<D, NT, STAGES, SMALL, BATCHED>;
   return v;
 }
@@ -113,22 +113,29 @@ FastVariant make_variant() {
 // sequence or batched) are template parameters, so that each kernel carries
 // only the code it runs; compiling the other paths in cost the 64-token
 // single-sequence call ~1.6 us at cfg2.
-template <int D, int NT, int STAGES>
-FastVariant make_variant(bool small_pages, bool batched) {
-  if (small_pages)
-    return batched ? make_variant<D, NT, STAGES, true, true>() : make_variant<D, NT, STAGES, true, false>();
-  return batched ? make_variant<D, NT, STAGES, false, true>() : make_variant<D, NT, STAGES, false, false>();
+template <int D, int NT, int STAGES, bool BATCHED>
+FastVariant make_variant(bool small_pages) {
+  return small_pages ? make_variant<D, NT, STAGES, true, BATCHED>()
+                     : make_variant<D, NT, STAGES, false, BATCHED>();
 }
 
 // Stage counts keep two CTAs per SM resident (<= ~110 KB each) except at
-// dim 256, where one CTA per SM holds four 33 KB stages.
+// dim 256, where one CTA per SM holds 33 KB stages. Single-sequence kernels
+// keep their combine buffer in the ring, which makes room for a sixth stage
+// at dim 128 (and at dim 256 leaves six stages room beside a merge CTA).
 FastVariant fast_variant(uint32_t dim, uint32_t nt, uint32_t page_tokens, bool batched) {
   const bool small = page_tokens < kvb::kStageTokens;
-  if (dim == 128 && nt == 1) return make_variant<128, 1, 5>(small, batched);
-  if (dim == 128 && nt == 2 && batched) return make_variant<128, 2, 4>(small, batched);
-  if (dim == 64 && nt == 1) return make_variant<64, 1, 8>(small, batched);
-  if (dim == 64 && nt == 2 && batched) return make_variant<64, 2, 7>(small, batched);
-  if (dim == 256 && nt == 1) return make_variant<256, 1, 4>(small, batched);
+  if (batched) {
+    if (dim == 128 && nt == 1) return make_variant<128, 1, 5, true>(small);
+    if (dim == 128 && nt == 2) return make_variant<128, 2, 4, true>(small);
+    if (dim == 64 && nt == 1) return make_variant<64, 1, 8, true>(small);
+    if (dim == 64 && nt == 2) return make_variant<64, 2, 7, true>(small);
+    if (dim == 256 && nt == 1) return make_variant<256, 1, 4, true>(small);
+    return FastVariant{};
+  }
+  if (dim == 128 && nt == 1) return make_variant<128, 1, 6, false>(small);
+  if (dim == 64 && nt == 1) return make_variant<64, 1, 8, false>(small);
+  if (dim == 256 && nt == 1) return make_variant<256, 1, 6, false>(small);
   return FastVariant{};
 }
 

@@ -95,16 +95,22 @@ __device__ __forceinline__ uint32_t v_page_pitch(uint32_t dim, uint32_t page_tok
   return dim * page_tokens + (page_tokens < 64 ? 2u * page_tokens : 0u);
 }
 
-template <int D, int NT, int STAGES>
+// RING_COMBINE: the warps' combine buffer reuses the start of the ring. A
+// single-sequence CTA has one piece, so when it combines, every copy has
+// landed and every stage has been read (the consumers meet at a barrier
+// first); the freed shared memory holds one more stage. A batched CTA may
+// already be loading its next piece and keeps a buffer of its own.
+template <int D, int NT, int STAGES, bool RING_COMBINE>
 struct DecodeSmem {
   static constexpr uint32_t kRing = STAGES * StageLayout<D>::kBytes;
   static constexpr uint32_t kCols = 8 * NT;
   static constexpr uint32_t kPitch = D + 4;  // floats; breaks bank aliasing of columns
   static constexpr uint32_t kCombine = kConsumerWarps * kCols * kPitch * 4;
+  static_assert(!RING_COMBINE || kCombine <= kRing, "combine buffer larger than the ring");
   static constexpr uint32_t kStats = kConsumerWarps * kCols * 2 * 4;
   static constexpr uint32_t kBarriers = 2 * STAGES * 8;
-  static constexpr uint32_t kOffCombine = kRing;
-  static constexpr uint32_t kOffStats = kOffCombine + kCombine;
+  static constexpr uint32_t kOffCombine = RING_COMBINE ? 0 : kRing;
+  static constexpr uint32_t kOffStats = RING_COMBINE ? kRing : kOffCombine + kCombine;
   static constexpr uint32_t kOffBar = kOffStats + kStats;
   static constexpr uint32_t kOffAbort = kOffBar + kBarriers;
   // Stage tags: the CTA stage sequence number each ring slot is armed for.
@@ -557,19 +563,6 @@ struct QueryFrags {
   int64_t qpos[NT][2];   // query position of the thread's C columns
 };
 
-// Signed int8 limbs of a fixed-point value |q| <= 2^22: q = l0 + 256 l1 + 65536 l2.
-__device__ __forceinline__ void split_limbs(int q, int& l0, int& l1, int& l2) {
-  l0 = static_cast<int8_t>(q & 0xff);
-  const int r = (q - l0) >> 8;
-  l1 = static_cast<int8_t>(r & 0xff);
-  l2 = (r - l1) >> 8;
-}
-
-__device__ __forceinline__ uint32_t pack_s8x4(int a, int b, int c, int d) {
-  return (uint32_t(a) & 0xffu) | ((uint32_t(b) & 0xffu) << 8) | ((uint32_t(c) & 0xffu) << 16) |
-         (uint32_t(d) << 24);
-}
-
 // Loads the piece's query operands and, for a single sequence, returns
 // whether every token of the piece is visible to every query row of the
 // CTA's columns (k_positions is nondecreasing, so it is enough that the
@@ -629,21 +622,30 @@ __device__ __forceinline__ bool load_query(const DecodeParams& p, const Piece& p
     if (amax > 0.f) e = int((__float_as_uint(amax) >> 23) & 0xffu) - 126;
     e = max(-100, min(100, e));
     const float up = __uint_as_float(uint32_t(127 + 22 - e) << 23);
+    // q = rint(v * up), |q| <= 2^22, is split into signed base-256 digits
+    // q = l0 + 256 l1 + 65536 l2 with l0, l1 in [-128, 127] (unique, so the
+    // same limbs as a sequential split). v * up is exact (a power-of-two
+    // scale), so fma(v, up, 1.5 * 2^23) rounds it to the nearest integer
+    // (ties to even) in the low mantissa bits; subtracting the sum's bias and
+    // adding 0x808080 leaves q + 0x808080, whose bytes 0..2 are l0..l2 + 128.
+    // Byte permutes gather digit k of four values and xor 0x80 removes the 128.
+    constexpr float kRoundInt = 12582912.0f;  // 1.5 * 2^23
+    constexpr uint32_t kBias = 0x808080u - 0x4B400000u;
 #pragma unroll
     for (int c = 0; c < D / 64; ++c) {
 #pragma unroll
       for (int jj = 0; jj < 2; ++jj) {
 #pragma unroll
         for (int half = 0; half < 2; ++half) {
-          int l[3][4];
+          uint32_t w[4];
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const int qi = __float2int_rn(vals[nt][c][8 * jj + 4 * half + i] * up);
-            split_limbs(qi, l[0][i], l[1][i], l[2][i]);
-          }
-#pragma unroll
-          for (int k = 0; k < 3; ++k)
-            qf.limb[nt][2 * c + jj][k][half] = pack_s8x4(l[k][0], l[k][1], l[k][2], l[k][3]);
+          for (int i = 0; i < 4; ++i)
+            w[i] = __float_as_uint(fmaf(vals[nt][c][8 * jj + 4 * half + i], up, kRoundInt)) + kBias;
+          const uint32_t a = __byte_perm(w[0], w[1], 0x5140), b = __byte_perm(w[2], w[3], 0x5140);
+          const uint32_t c2 = __byte_perm(w[0], w[1], 0x0062), d2 = __byte_perm(w[2], w[3], 0x0062);
+          qf.limb[nt][2 * c + jj][0][half] = __byte_perm(a, b, 0x5410) ^ 0x80808080u;
+          qf.limb[nt][2 * c + jj][1][half] = __byte_perm(a, b, 0x7632) ^ 0x80808080u;
+          qf.limb[nt][2 * c + jj][2][half] = __byte_perm(c2, d2, 0x5410) ^ 0x80808080u;
         }
       }
     }
@@ -909,9 +911,24 @@ __device__ __forceinline__ void consume_stage(const DecodeParams& p, const uint8
 // SMALL_PAGES: pages shorter than a stage (produce_small_pages); a separate
 // instantiation, so that the 64-token-page kernel does not carry that code
 // (which cost it ~0.6 us a call at cfg2 when both producers were compiled in).
+// Register cap per variant. Registers are split between an SM's four
+// sub-partitions (16K each, allocated per warp in 256-register units), and a
+// CTA's five warps are spread over them, so one sub-partition holds three
+// warps of two resident CTAs: <= 168 registers (3 x 21 units) keeps two
+// CTAs per SM at dims 64 and 128. The merge kernel that follows a call needs
+// room for one of its warps (10 units) in every sub-partition: at 168 an SM
+// still holding a merge CTA admitted one partial CTA instead of two, and at
+// 64K tokens the call's last 32 CTAs started ~3 us late. The dim-128,
+// 8-column kernels are therefore held to 144 (3 x 18 + 10 units; no
+// spills). At dim 256 one CTA has the SM to itself: 216 (2 x 27 + 10).
+template <int D, int NT, bool BATCHED>
+constexpr int decode_max_regs() {
+  return D == 256 ? 216 : (D == 128 && NT == 1) ? 144 : 168;
+}
+
 template <int D, int NT, int STAGES, bool SMALL_PAGES, bool BATCHED>
-__global__ void __launch_bounds__(kDecodeThreads, 2) decode_partial_kernel(DecodeParams p) {
-  using L = DecodeSmem<D, NT, STAGES>;
+__global__ void __maxnreg__((decode_max_regs<D, NT, BATCHED>())) decode_partial_kernel(DecodeParams p) {
+  using L = DecodeSmem<D, NT, STAGES, !BATCHED>;
   extern __shared__ __align__(128) uint8_t smem[];
   uint8_t* ring = smem;
   float* combine = reinterpret_cast<float*>(smem + L::kOffCombine);
@@ -995,6 +1012,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 2) decode_partial_kernel(Decod
 
     // ---- flush this warp's state.
     float* cw = combine + size_t(warp) * L::kCols * L::kPitch;
+    float lsums[NT][2];
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
@@ -1003,10 +1021,18 @@ __global__ void __launch_bounds__(kDecodeThreads, 2) decode_partial_kernel(Decod
         lsum += __shfl_xor_sync(0xffffffffu, lsum, 4);
         lsum += __shfl_xor_sync(0xffffffffu, lsum, 8);
         lsum += __shfl_xor_sync(0xffffffffu, lsum, 16);
+        lsums[nt][e] = lsum;
+      }
+    // The combine buffer overlays ring slots that other warps may still read.
+    if (!BATCHED) named_barrier(1, 32 * kConsumerWarps);
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
         const uint32_t col = 8 * nt + 2 * tig + e;
         if (grp == 0) {
           stats[(warp * L::kCols + col) * 2 + 0] = ws.m[nt][e];
-          stats[(warp * L::kCols + col) * 2 + 1] = lsum;
+          stats[(warp * L::kCols + col) * 2 + 1] = lsums[nt][e];
         }
 #pragma unroll
         for (int md = 0; md < D / 16; ++md) {
