@@ -41,7 +41,8 @@ void launch_attention_ex(const Shape&, const DeviceInput&, const LaunchOptions&,
 // The two halves of launch_attention_ex on the tensor-core path, for callers
 // that merge partials themselves (e.g. across GPUs). launch_attention_partials
 // writes one (m, l, n) partial per partition into the leading splits of the
-// scratch layout of attention_common.h and returns the partition count used
+// scratch layout of attention_common.h, marks the remaining splits as empty
+// partials, and returns the partition count used
 // (0 for an empty range, where nothing is launched); it throws
 // std::invalid_argument unless attention_b200_supported(shape, input).
 // merge_attention_ex merges the leading `partitions` splits of every

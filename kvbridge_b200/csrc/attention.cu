@@ -435,7 +435,9 @@ void launch_attention_ex(const Shape& s, const DeviceInput& in, const LaunchOpti
     return;
   }
   const uint32_t parts = launch_attention_partials(s, in, opt.partitions, scratch, stream);
-  merge_attention_ex(s, scratch, parts, m, l, n, opt.out_f16, stream);
+  // The partial kernel has already marked splits [parts, splits) empty.
+  launch_merge(kvb::kMergeScratch,
+               scratch_merge_params(s, scratch, parts, splits, false, m, l, n, opt.out_f16), stream);
 }
 
 void launch_attention(const Shape& s, const DeviceInput& in, float* scratch, float* m, float* l,

@@ -332,6 +332,30 @@ __device__ __forceinline__ void drain_copies(uint64_t* full, uint32_t g) {
   }
 }
 
+// Single sequence: splits [parts, split_stride) of the CTA's row-heads are
+// written as empty partials (m = -inf, l = 0; n is left as it is), so that
+// the scratch holds a complete reference layout for a merge over all splits.
+// They are spread over the CTAs by slot (split parts + slot + k * parts) and
+// written by the producer warp once its copies are issued, off the path of
+// the call's last stage and of the merge that follows.
+template <int D>
+__device__ void mark_empty_splits(const DecodeParams& p, const Piece& pc) {
+  const uint32_t lane = threadIdx.x & 31;
+  const uint32_t parts = p.ctas / (p.kv_heads * p.col_groups);
+  if (p.split_stride <= parts + pc.slot) return;
+  const uint32_t count = (p.split_stride - parts - pc.slot - 1) / parts + 1;
+  const uint32_t cols = min(p.group_cols, p.qr - pc.col0);
+  for (uint32_t w = lane; w < cols * count; w += 32) {
+    const uint32_t col = pc.col0 + w % cols;
+    const uint32_t split = parts + pc.slot + (w / cols) * parts;
+    const uint32_t r = col / p.group, gq = col % p.group;
+    const size_t rh = size_t(r) * p.q_heads + size_t(pc.h) * p.group + gq;
+    float* e = p.part + (rh * p.split_stride + split) * (D + 2);
+    e[0] = -INFINITY;
+    e[1] = 0.f;
+  }
+}
+
 // Producer for pages shorter than a stage (16 or 32 tokens). Each bulk copy
 // costs the SM's copy engine about as much time as a small one, and with
 // 16-token pages the four copies per page (K, V and two 64-byte scale runs)
@@ -439,6 +463,7 @@ __device__ void produce_small_pages(const DecodeParams& p, const Piece& only, ui
     }
     x = piece_end_stage(p, pc, x);
   }
+  if (!BATCHED && !failed) mark_empty_splits<D>(p, only);
   drain_copies<STAGES>(full, g);
 }
 
@@ -539,6 +564,7 @@ __device__ void produce(const DecodeParams& p, const Piece& only, uint8_t* ring,
     }
     x = piece_end_stage(p, pc, x);
   }
+  if (!BATCHED && !failed) mark_empty_splits<D>(p, only);
   drain_copies<STAGES>(full, g);
 }
 

@@ -477,6 +477,35 @@ def test_uninitialised_scratch_repeats_and_full_remerge(cuda_device):
         assert torch.equal(v.cpu(), results[0][k]), k
 
 
+@pytest.mark.parametrize("rows,q_heads,kv_heads,dim,page_tokens,tokens",
+                         [(1, 32, 8, 128, 64, 16384), (3, 24, 4, 256, 32, 9000), (5, 64, 8, 64, 16, 5000)])
+def test_partials_mark_every_other_split_empty(cuda_device, rows, q_heads, kv_heads, dim, page_tokens, tokens):
+    """launch_attention_partials alone (no merge_attention_ex) leaves a
+    complete reference scratch: every split past the partitions used reads as
+    an empty partial (m = -inf, l = 0), so a merge over all split_count splits
+    of a garbage-initialised scratch reproduces launch_attention_ex."""
+    qpos = [tokens - rows + r for r in range(rows)] if rows > 1 else None
+    case = make(cuda_device, rows=rows, q_heads=q_heads, kv_heads=kv_heads, dim=dim, page_tokens=page_tokens,
+                tokens=tokens, seed=tokens + dim, q_positions=qpos)
+    shape = case.shape
+    splits = kvb.split_count(shape)
+    inp = case.device_input()
+    scratch = _scratch_garbage(shape, cuda_device, 9)
+    parts = kvb.launch_attention_partials(shape, inp, scratch)
+    assert 0 < parts < splits
+    rows_view = scratch.view(kvb.output_scalar_elements(shape), splits, dim + 2)
+    torch.cuda.synchronize()
+    assert torch.all(rows_view[:, parts:, 0].cpu() == float("-inf"))
+    assert torch.all(rows_view[:, parts:, 1].cpu() == 0)
+    _, m, l, n = outputs_for(shape, cuda_device)
+    kvb.merge_attention(shape, scratch, splits, m, l, n)
+    _, m2, l2, n2 = outputs_for(shape, cuda_device)
+    kvb.launch_attention_ex(shape, inp, _scratch_garbage(shape, cuda_device, 10), m2, l2, n2)
+    torch.cuda.synchronize()
+    assert torch.equal(m.cpu(), m2.cpu())
+    assert _close(l.cpu(), l2.cpu()) and _close(n.cpu(), n2.cpu())
+
+
 def test_independent_streams(cuda_device):
     """Calls on two streams with their own scratch buffers run concurrently
     without sharing state: interleaved launches reproduce each case's own
