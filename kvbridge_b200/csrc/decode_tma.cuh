@@ -15,24 +15,25 @@
 //    mbarriers. K and V are consumed exactly as stored (int8); nothing is
 //    converted before it reaches shared memory.
 //  * Math: each consumer warp owns whole stages (stage g goes to warp g % 4)
-//    and keeps its own online-softmax state. QK and PV both run "swap-AB" on
-//    warp-level tensor-core MMAs so that the query rows of the KV head
-//    (rows * group <= 8 * NT) sit in the narrow N dimension:
-//        S^T[token][qrow] = K[token][d] . Q^T[d][qrow]   (M = 16 tokens)
-//        O^T[d][qrow]     = V[d][token] . P[token][qrow]  (M = 16 dims)
-//    Both run on the int8 MMA (m16n8k32, exact s32 accumulation) with K and
-//    V used exactly as stored. QK: each query row is a 22-bit fixed-point
-//    value split into three signed int8 limbs (q = L0 + 2^8 L1 + 2^16 L2,
-//    scaled by a power of two per row). PV: P = w * vscale is a 15-bit
-//    signed fixed-point value per (stage, column) split into a u8 low and an
-//    s8 high limb; the
-//    exact sums are folded into fp32 accumulators with the power-of-two
+//    and keeps its own online-softmax state. QK and PV run on the int8
+//    warp-level MMA (m16n8k32, exact s32 accumulation) with the query side
+//    as the A operand, whose 16 rows are (query column, int8 limb) pairs, and
+//    K / V as the B operand, used exactly as stored:
+//        S[(col, limb)][token] = Q_limb[col][d] . K^T[d][token]
+//        O[(col, limb)][d]     = P_limb[col][token] . V^T[token][d]
+//    A thread's B fragment is then 8 contiguous bytes of one K row (dims) or
+//    one V row (tokens), so every 16-byte shared load lands as two aligned B
+//    register pairs, and both limbs of a column come back in the same
+//    thread's C fragment. QK: each query row is a 22-bit fixed-point value
+//    split into three signed int8 limbs (q = L0 + 2^8 L1 + 2^16 L2, scaled by
+//    a power of two per row). PV: P = w * vscale is a 15-bit signed
+//    fixed-point value per (stage, column) split into two signed int8 limbs;
+//    the exact sums are folded into fp32 accumulators with the power-of-two
 //    scale. Per-token kscale multiplies the fp32 scores and per-token vscale
-//    rides on P, as in the reference MMA kernel. The QK accumulator
-//    fragments become the PV B operand through movmatrix (8x8 transposes of
-//    16-bit P pairs) and byte permutes, never touching shared memory, because
-//    the token order of the QK rows is chosen so that each thread's PV A
-//    operand is its own 16-byte word of each V row.
+//    rides on P, as in the reference MMA kernel. The QK n-tiles take their
+//    tokens in the order that leaves each thread the scores of 16 contiguous
+//    tokens of its column, which are exactly the tokens of its PV A operand,
+//    so P never leaves the thread's registers.
 //  * Precision: QK is exact up to the 2^-22 (relative to the row's largest
 //    |q|) rounding of Q; P is exact up to 2^-15 of the stage's largest |P|
 //    of the column (its power-of-two scale adapts per stage and column, so
@@ -573,20 +574,27 @@ __device__ void produce(const DecodeParams& p, const Piece& only, uint8_t* ring,
 
 template <int D, int NT>
 struct WarpState {
-  float acc[D / 16][NT][4];  // O^T fragments: rows d, columns = query rows
-  float m[NT][2];            // running max (log2 units) of columns 2*tig+e
-  float l[NT][2];            // thread-partial denominators
+  float acc[D / 8][NT][2];  // O fragments: column grp + 8 nt, dims 8 dn + 2 tig + e
+  float m[NT];              // running max (log2 units) of column grp + 8 nt
+  float l[NT];              // thread-partial denominator of that column
 };
 
-// Per-piece query operands of one warp: the three int8 limbs of every query
-// row in the B-fragment layout of m16n8k32 (k-step j covers dims
-// 64*(j/2) + 16*tig + 8*(j%2) + [0,8) for lane tig), and the fp32 factor
-// turning combined limb dots into log2-unit scores.
+// QK m-tiles: rows (column c, limb k) are numbered 3 c + k (c < 8 NT taken
+// as 8 nt + row-in-group), eight to a half-tile: m-tile mt holds row sets
+// 2 mt (rows 0-7) and 2 mt + 1 (rows 8-15). With NT = 1 the last half-tile
+// is zero.
+template <int NT>
+constexpr int qk_tiles() { return (3 * NT + 1) / 2; }
+
+// Per-piece query operands of one warp: the A fragments of the QK MMA for
+// every k-step (k-step j covers dims 64*(j/2) + 16*tig + 8*(j%2) + [0,8) for
+// lane tig; a thread holds the limbs of its own column grp + 8 nt), and the
+// fp32 factor turning combined limb dots into log2-unit scores.
 template <int D, int NT>
 struct QueryFrags {
-  uint32_t limb[NT][D / 32][3][2];
-  float cf[NT][2];       // score factor of the thread's C columns (log2 units)
-  int64_t qpos[NT][2];   // query position of the thread's C columns
+  uint32_t a[qk_tiles<NT>()][D / 32][4];
+  float cf[NT];      // score factor of column grp + 8 nt (log2 units)
+  int64_t qpos[NT];  // query position of that column
 };
 
 // Loads the piece's query operands and, for a single sequence, returns
@@ -607,7 +615,7 @@ __device__ __forceinline__ bool load_query(const DecodeParams& p, const Piece& p
     if (lane < 8u * NT && ocol < p.qr) qp_own = __ldg(p.q_positions + ocol / p.group);
   }
   float vals[NT][D / 64][16];
-  int64_t qp[NT][2];
+  int64_t qp[NT];
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) {
     const uint32_t col = pc.col0 + 8 * nt + grp;
@@ -627,12 +635,7 @@ __device__ __forceinline__ bool load_query(const DecodeParams& p, const Piece& p
         vals[nt][c][4 * i + 3] = f.w;
       }
     }
-    // C layout: this thread's columns are 2*tig and 2*tig+1 of the n-tile.
-#pragma unroll
-    for (int ee = 0; ee < 2; ++ee) {
-      const uint32_t ccol = pc.col0 + 8 * nt + 2 * tig + ee;
-      qp[nt][ee] = (!BATCHED && ccol < p.qr) ? __ldg(p.q_positions + ccol / p.group) : INT64_MAX;
-    }
+    qp[nt] = (!BATCHED && valid) ? __ldg(p.q_positions + r) : INT64_MAX;
   }
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) {
@@ -669,268 +672,242 @@ __device__ __forceinline__ bool load_query(const DecodeParams& p, const Piece& p
             w[i] = __float_as_uint(fmaf(vals[nt][c][8 * jj + 4 * half + i], up, kRoundInt)) + kBias;
           const uint32_t a = __byte_perm(w[0], w[1], 0x5140), b = __byte_perm(w[2], w[3], 0x5140);
           const uint32_t c2 = __byte_perm(w[0], w[1], 0x0062), d2 = __byte_perm(w[2], w[3], 0x0062);
-          qf.limb[nt][2 * c + jj][0][half] = __byte_perm(a, b, 0x5410) ^ 0x80808080u;
-          qf.limb[nt][2 * c + jj][1][half] = __byte_perm(a, b, 0x7632) ^ 0x80808080u;
-          qf.limb[nt][2 * c + jj][2][half] = __byte_perm(c2, d2, 0x5410) ^ 0x80808080u;
+          const uint32_t limb[3] = {__byte_perm(a, b, 0x5410) ^ 0x80808080u,
+                                    __byte_perm(a, b, 0x7632) ^ 0x80808080u,
+                                    __byte_perm(c2, d2, 0x5410) ^ 0x80808080u};
+          // Row set 3 nt + k of the A fragment: a0/a2 (rows 0-7, k-lo/hi),
+          // a1/a3 (rows 8-15).
+#pragma unroll
+          for (int k = 0; k < 3; ++k) {
+            const int rs = 3 * nt + k;
+            qf.a[rs / 2][2 * c + jj][(rs % 2) + 2 * half] = limb[k];
+          }
         }
       }
     }
-    const float cf_b = p.score_scale * kLog2e * __uint_as_float(uint32_t(127 + e - 22) << 23);
-    // The factor of column 2*tig+ee lives in lane 4*(2*tig+ee).
+    qf.cf[nt] = p.score_scale * kLog2e * __uint_as_float(uint32_t(127 + e - 22) << 23);
+    qf.qpos[nt] = qp[nt];
+  }
+  if (3 * NT % 2 == 1) {
 #pragma unroll
-    for (int ee = 0; ee < 2; ++ee) {
-      qf.cf[nt][ee] = __shfl_sync(0xffffffffu, cf_b, 4 * (2 * tig + ee));
-      qf.qpos[nt][ee] = qp[nt][ee];
+    for (int j = 0; j < D / 32; ++j) {
+      qf.a[qk_tiles<NT>() - 1][j][1] = 0u;
+      qf.a[qk_tiles<NT>() - 1][j][3] = 0u;
     }
   }
   if (BATCHED) return true;
   return __all_sync(0xffffffffu, kp_last <= qp_own);
 }
 
-// One 64-token stage for one warp.
+// One 64-token stage for one warp. The thread (grp, tig) works on columns
+// grp + 8 nt and on the stage's tokens 16 tig + [0, 16) (local index t).
 template <int D, int NT>
 __device__ __forceinline__ void consume_stage(const DecodeParams& p, const uint8_t* st,
                                               uint32_t tb, uint32_t lo, uint32_t hi,
                                               bool all_visible, const QueryFrags<D, NT>& qf,
                                               WarpState<D, NT>& ws) {
+  constexpr int kQk = qk_tiles<NT>();
   const uint32_t lane = threadIdx.x & 31, grp = lane >> 2, tig = lane & 3;
   const uint8_t* sk = st + StageLayout<D>::kK;
   const uint8_t* sv = st + StageLayout<D>::kV;
   const float* sks = reinterpret_cast<const float*>(st + StageLayout<D>::kKs);
   const float* svs = reinterpret_cast<const float*>(st + StageLayout<D>::kVs);
 
-  // ---- S^T = K Q^T. QK row r of m-tile s holds token
-  //      16*((r&7)>>1) + 4*s + 2*(r>>3) + (r&1), so a thread's rows grp and
-  //      grp+8 are tokens t0 and t0+2.
-  float sc[4][NT][4];
+  // ---- S = Q K^T. N-tile j holds tokens 16*(n/2) + 2j + n%2 (n = 0..7): the
+  //      thread supplies the K row of token n = grp and gets back columns
+  //      n = 2 tig + e, i.e. tokens 16 tig + 2 j + e (t = 2 j + e).
+  float sc[NT][16];
 #pragma unroll
-  for (int s = 0; s < 4; ++s) {
-    const uint32_t t0 = 16 * (grp >> 1) + 4 * s + (grp & 1), t1 = t0 + 2;
-    int acc[NT][3][4];
+  for (int j = 0; j < 8; ++j) {
+    const uint32_t tk = 16 * (grp >> 1) + 2 * j + (grp & 1);
+    int acc[kQk][4];
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt)
+    for (int mt = 0; mt < kQk; ++mt)
 #pragma unroll
-      for (int k = 0; k < 3; ++k)
-#pragma unroll
-        for (int i = 0; i < 4; ++i) acc[nt][k][i] = 0;
+      for (int i = 0; i < 4; ++i) acc[mt][i] = 0;
 #pragma unroll
     for (int c = 0; c < D / 64; ++c) {
-      const uint4 ra = *reinterpret_cast<const uint4*>(sk + t0 * D + 64 * c + 16 * tig);
-      const uint4 rb = *reinterpret_cast<const uint4*>(sk + t1 * D + 64 * c + 16 * tig);
-      const uint32_t wa[4] = {ra.x, ra.y, ra.z, ra.w};
-      const uint32_t wb[4] = {rb.x, rb.y, rb.z, rb.w};
+      const uint4 kw = *reinterpret_cast<const uint4*>(sk + tk * D + 64 * c + 16 * tig);
 #pragma unroll
-      for (int jj = 0; jj < 2; ++jj) {
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-          for (int k = 0; k < 3; ++k)
-            imma_16832(acc[nt][k], wa[2 * jj], wb[2 * jj], wa[2 * jj + 1], wb[2 * jj + 1],
-                       qf.limb[nt][2 * c + jj][k][0], qf.limb[nt][2 * c + jj][k][1]);
+      for (int mt = 0; mt < kQk; ++mt) {
+        const uint32_t* a0 = qf.a[mt][2 * c];
+        const uint32_t* a1 = qf.a[mt][2 * c + 1];
+        imma_16832(acc[mt], a0[0], a0[1], a0[2], a0[3], kw.x, kw.y);
+        imma_16832(acc[mt], a1[0], a1[1], a1[2], a1[3], kw.z, kw.w);
       }
     }
-    // Limb dots are exact integers (|acc| < 2^21); combine in fp32.
+    // Limb k of column grp + 8 nt is row set 3 nt + k: C rows 0-7 (c0, c1) or
+    // 8-15 (c2, c3) of m-tile (3 nt + k) / 2. Limb dots are exact integers
+    // (|dot| < 2^21); combine in fp32.
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-      for (int i = 0; i < 4; ++i)
-        sc[s][nt][i] = fmaf(float(acc[nt][2][i]), 65536.f,
-                            fmaf(float(acc[nt][1][i]), 256.f, float(acc[nt][0][i])));
+      for (int e = 0; e < 2; ++e) {
+        const int r0 = 3 * nt, r1 = 3 * nt + 1, r2 = 3 * nt + 2;
+        const int d0 = acc[r0 / 2][2 * (r0 % 2) + e], d1 = acc[r1 / 2][2 * (r1 % 2) + e];
+        const int d2 = acc[r2 / 2][2 * (r2 % 2) + e];
+        sc[nt][2 * j + e] = fmaf(float(d2), 65536.f, fmaf(float(d1), 256.f, float(d0)));
+      }
+    // Keep the K loads of later n-tiles from being hoisted over this pair
+    // (register pressure; the other warps cover the load latency).
+    if (j % 2 == 1) asm volatile("" ::: "memory");
   }
 
   // ---- scores in log2 units, masking.
   const bool full = all_visible && tb >= lo && tb + kStageTokens <= hi;
+  const uint32_t t0 = tb + 16 * tig;  // sequence index of local token 0
+  {
+    float ks[16];
 #pragma unroll
-  for (int s = 0; s < 4; ++s) {
-    const uint32_t t0 = 16 * (grp >> 1) + 4 * s + (grp & 1), t1 = t0 + 2;
-    const float k0 = sks[t0], k1 = sks[t1];
-    bool in0 = true, in1 = true;
-    int64_t kp0 = 0, kp1 = 0;
-    if (!full) {
-      in0 = tb + t0 >= lo && tb + t0 < hi;
-      in1 = tb + t1 >= lo && tb + t1 < hi;
-      if (!all_visible) {
-        kp0 = in0 ? __ldg(p.k_positions + tb + t0) : 0;
-        kp1 = in1 ? __ldg(p.k_positions + tb + t1) : 0;
-      }
+    for (int i = 0; i < 4; ++i) {
+      const float4 f = reinterpret_cast<const float4*>(sks + 16 * tig)[i];
+      ks[4 * i + 0] = f.x;
+      ks[4 * i + 1] = f.y;
+      ks[4 * i + 2] = f.z;
+      ks[4 * i + 3] = f.w;
     }
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        float x0 = sc[s][nt][e] * k0 * qf.cf[nt][e];
-        float x1 = sc[s][nt][2 + e] * k1 * qf.cf[nt][e];
-        if (!full) {
-          const bool v0 = in0 && (all_visible || kp0 <= qf.qpos[nt][e]);
-          const bool v1 = in1 && (all_visible || kp1 <= qf.qpos[nt][e]);
-          x0 = v0 ? x0 : -INFINITY;
-          x1 = v1 ? x1 : -INFINITY;
-        }
-        sc[s][nt][e] = x0;
-        sc[s][nt][2 + e] = x1;
-      }
+      for (int t = 0; t < 16; ++t) sc[nt][t] *= ks[t] * qf.cf[nt];
+  }
+  if (!full) {
+#pragma unroll
+    for (int t = 0; t < 16; ++t) {
+      const bool in = t0 + t >= lo && t0 + t < hi;
+      const int64_t kp = (in && !all_visible) ? __ldg(p.k_positions + t0 + t) : 0;
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+        if (!in || (!all_visible && kp > qf.qpos[nt])) sc[nt][t] = -INFINITY;
+    }
   }
 
-  // ---- vscale of the stage's tokens (token t sits in lane t % 32, register
-  //      t / 32); tokens outside [lo, hi) read as 0 (their slots may hold
-  //      anything).
-  float vs_lane[2];
-#pragma unroll
-  for (int i = 0; i < 2; ++i) {
-    const uint32_t t = lane + 32 * i;
-    const bool in = full || (tb + t >= lo && tb + t < hi);
-    vs_lane[i] = in ? svs[t] : 0.f;
-  }
+  // ---- online softmax update per column (its 64 tokens sit in the four
+  //      lanes of the thread's quad).
   {
-    // ---- online softmax update per column.
     bool rescale = false;
-    float fac[NT][2];
+    float fac[NT];
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt)
+    for (int nt = 0; nt < NT; ++nt) {
+      float cm = sc[nt][0];
 #pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        float cm = -INFINITY;
+      for (int t = 1; t < 16; ++t) cm = fmaxf(cm, sc[nt][t]);
+      cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 1));
+      cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 2));
+      const float mold = ws.m[nt];
+      const float mnew = fmaxf(mold, cm);
+      const float alpha = mnew == -INFINITY ? 1.f : fast_exp2(mold - mnew);
+      ws.m[nt] = mnew;
+      const float msub = mnew == -INFINITY ? 0.f : mnew;
+      float lsum = 0.f;
 #pragma unroll
-        for (int s = 0; s < 4; ++s) cm = fmaxf(cm, fmaxf(sc[s][nt][e], sc[s][nt][2 + e]));
-        cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 4));
-        cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 8));
-        cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 16));
-        const float mold = ws.m[nt][e];
-        const float mnew = fmaxf(mold, cm);
-        const float alpha = mnew == -INFINITY ? 1.f : fast_exp2(mold - mnew);
-        ws.m[nt][e] = mnew;
-        const float msub = mnew == -INFINITY ? 0.f : mnew;
-        float lsum = 0.f;
-#pragma unroll
-        for (int s = 0; s < 4; ++s) {
-          const float w0 = fast_exp2(sc[s][nt][e] - msub);
-          const float w1 = fast_exp2(sc[s][nt][2 + e] - msub);
-          sc[s][nt][e] = w0;
-          sc[s][nt][2 + e] = w1;
-          lsum += w0 + w1;
-        }
-        ws.l[nt][e] = ws.l[nt][e] * alpha + lsum;
-        fac[nt][e] = alpha;
-        rescale |= alpha != 1.f;
+      for (int t = 0; t < 16; ++t) {
+        sc[nt][t] = fast_exp2(sc[nt][t] - msub);
+        lsum += sc[nt][t];
       }
+      ws.l[nt] = ws.l[nt] * alpha + lsum;
+      fac[nt] = alpha;
+      rescale |= alpha != 1.f;
+    }
     if (__any_sync(0xffffffffu, rescale)) {
 #pragma unroll
-      for (int md = 0; md < D / 16; ++md)
+      for (int dn = 0; dn < D / 8; ++dn)
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
-          ws.acc[md][nt][0] *= fac[nt][0];
-          ws.acc[md][nt][1] *= fac[nt][1];
-          ws.acc[md][nt][2] *= fac[nt][0];
-          ws.acc[md][nt][3] *= fac[nt][1];
+          ws.acc[dn][nt][0] *= fac[nt];
+          ws.acc[dn][nt][1] *= fac[nt];
         }
     }
   }
 
-  // ---- P = w * vscale in fp32, and per column the power of two that puts
+  // ---- P = w * vscale in fp32 (tokens outside [lo, hi) take vscale 0: their
+  //      slots may hold anything), and per column the power of two that puts
   //      the stage's largest |P| in [2^13, 2^14): pscale scales P into the
   //      fixed point below, inv_pscale scales the exact sums back.
-  float pscale[NT][2], inv_pscale[NT][2];
+  float pscale[NT], inv_pscale[NT];
   {
-    float pmax[NT][2];
+    float vs[16];
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt) pmax[nt][0] = pmax[nt][1] = 0.f;
+    for (int i = 0; i < 4; ++i) {
+      const float4 f = reinterpret_cast<const float4*>(svs + 16 * tig)[i];
+      vs[4 * i + 0] = f.x;
+      vs[4 * i + 1] = f.y;
+      vs[4 * i + 2] = f.z;
+      vs[4 * i + 3] = f.w;
+    }
+    if (!full) {
 #pragma unroll
-    for (int s = 0; s < 4; ++s) {
-      const uint32_t t0 = 16 * (grp >> 1) + 4 * s + (grp & 1), t1 = t0 + 2;
-      const float v0a = __shfl_sync(0xffffffffu, vs_lane[0], t0 & 31);
-      const float v0b = __shfl_sync(0xffffffffu, vs_lane[1], t0 & 31);
-      const float v1a = __shfl_sync(0xffffffffu, vs_lane[0], t1 & 31);
-      const float v1b = __shfl_sync(0xffffffffu, vs_lane[1], t1 & 31);
-      const float vm0 = t0 < 32 ? v0a : v0b;
-      const float vm1 = t1 < 32 ? v1a : v1b;
-#pragma unroll
-      for (int nt = 0; nt < NT; ++nt) {
-        sc[s][nt][0] *= vm0;
-        sc[s][nt][1] *= vm0;
-        sc[s][nt][2] *= vm1;
-        sc[s][nt][3] *= vm1;
-        pmax[nt][0] = fmaxf(pmax[nt][0], fmaxf(fabsf(sc[s][nt][0]), fabsf(sc[s][nt][2])));
-        pmax[nt][1] = fmaxf(pmax[nt][1], fmaxf(fabsf(sc[s][nt][1]), fabsf(sc[s][nt][3])));
-      }
+      for (int t = 0; t < 16; ++t)
+        if (!(t0 + t >= lo && t0 + t < hi)) vs[t] = 0.f;
     }
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt)
+    for (int nt = 0; nt < NT; ++nt) {
+      float pm = 0.f;
 #pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        float pm = pmax[nt][e];
-        pm = fmaxf(pm, __shfl_xor_sync(0xffffffffu, pm, 4));
-        pm = fmaxf(pm, __shfl_xor_sync(0xffffffffu, pm, 8));
-        pm = fmaxf(pm, __shfl_xor_sync(0xffffffffu, pm, 16));
-        // pm < 2^(x - 126) for biased exponent x; pscale = 2^(140 - x), kept
-        // a normal float (stages with |P| below ~2^-113 lose precision).
-        const int x = int((__float_as_uint(pm) >> 23) & 0xffu);
-        const int sh = max(-126, min(126, 140 - x));
-        pscale[nt][e] = pm > 0.f ? __uint_as_float(uint32_t(127 + sh) << 23) : 1.f;
-        inv_pscale[nt][e] = pm > 0.f ? __uint_as_float(uint32_t(127 - sh) << 23) : 1.f;
+      for (int t = 0; t < 16; ++t) {
+        sc[nt][t] *= vs[t];
+        pm = fmaxf(pm, fabsf(sc[nt][t]));
       }
+      pm = fmaxf(pm, __shfl_xor_sync(0xffffffffu, pm, 1));
+      pm = fmaxf(pm, __shfl_xor_sync(0xffffffffu, pm, 2));
+      // pm < 2^(x - 126) for biased exponent x; pscale = 2^(140 - x), kept
+      // a normal float (stages with |P| below ~2^-113 lose precision).
+      const int x = int((__float_as_uint(pm) >> 23) & 0xffu);
+      const int sh = max(-126, min(126, 140 - x));
+      pscale[nt] = pm > 0.f ? __uint_as_float(uint32_t(127 + sh) << 23) : 1.f;
+      inv_pscale[nt] = pm > 0.f ? __uint_as_float(uint32_t(127 - sh) << 23) : 1.f;
+    }
   }
 
   // ---- P as signed fixed point per (stage, column): u = rint(P * pscale),
-  //      |u| < 2^14, split into a u8 low limb and an s8 high limb
-  //      (u = 256 * hi + lo, two's complement). Rows grp/grp+8 of QK m-tile s
-  //      are packed as 16-bit pairs (columns 2*tig, 2*tig+1) and transposed
-  //      with movmatrix, so the thread then holds column grp of tokens
-  //      16*tig+4*s+{0,1} (t01) and 16*tig+4*s+{2,3} (t23).
-  uint32_t t01[4][NT], t23[4][NT];
+  //      |u| < 2^14, split into signed base-256 digits u = lo + 256 hi
+  //      (lo in [-128, 127], |hi| <= 64) as for the query limbs: the fma
+  //      with 1.5 * 2^23 rounds the exact product to an integer (ties to
+  //      even), and after the bias u + 0x8080 holds lo + 128 and hi + 128
+  //      in its two low bytes. The PV A fragment of k-step kb is rows
+  //      (column, lo) and (column, hi) over tokens 8 kb + [0, 8) of the
+  //      thread: a0 / a2 = lo of tokens +0..3 / +4..7, a1 / a3 = hi.
+  constexpr float kRoundInt = 12582912.0f;  // 1.5 * 2^23
+  constexpr uint32_t kBias = 0x8080u - 0x4B400000u;
+  uint32_t pa[NT][2][4];
 #pragma unroll
-  for (int s = 0; s < 4; ++s) {
+  for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
-      const uint32_t u00 = uint32_t(__float2int_rn(sc[s][nt][0] * pscale[nt][0]));
-      const uint32_t u01 = uint32_t(__float2int_rn(sc[s][nt][1] * pscale[nt][1]));
-      const uint32_t u10 = uint32_t(__float2int_rn(sc[s][nt][2] * pscale[nt][0]));
-      const uint32_t u11 = uint32_t(__float2int_rn(sc[s][nt][3] * pscale[nt][1]));
-      t01[s][nt] = transpose_8x8_b16(__byte_perm(u00, u01, 0x5410));
-      t23[s][nt] = transpose_8x8_b16(__byte_perm(u10, u11, 0x5410));
-    }
-  }
-
-  // ---- O^T += V P on the int8 MMA (m16n8k32: s8 V x u8 low / s8 high P
-  //      limbs, exact s32).
-  //      k-step ks covers QK m-tiles 2ks (k = 4*tig + j) and 2ks+1
-  //      (k = 16 + 4*tig + j), i.e. tokens 16*tig + 8*ks + [0,8): words 2ks
-  //      and 2ks+1 of the thread's 16-byte slice of each V row, used as stored.
-  uint32_t blo[2][NT][2], bhi[2][NT][2];
+    for (int kb = 0; kb < 2; ++kb)
 #pragma unroll
-  for (int ks = 0; ks < 2; ++ks)
+      for (int half = 0; half < 2; ++half) {
+        uint32_t w[4];
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        blo[ks][nt][h] = __byte_perm(t01[2 * ks + h][nt], t23[2 * ks + h][nt], 0x6420);
-        bhi[ks][nt][h] = __byte_perm(t01[2 * ks + h][nt], t23[2 * ks + h][nt], 0x7531);
+        for (int i = 0; i < 4; ++i)
+          w[i] = __float_as_uint(fmaf(sc[nt][8 * kb + 4 * half + i], pscale[nt], kRoundInt)) + kBias;
+        const uint32_t t01 = __byte_perm(w[0], w[1], 0x5140), t23 = __byte_perm(w[2], w[3], 0x5140);
+        pa[nt][kb][2 * half + 0] = __byte_perm(t01, t23, 0x5410) ^ 0x80808080u;
+        pa[nt][kb][2 * half + 1] = __byte_perm(t01, t23, 0x7632) ^ 0x80808080u;
       }
+
+  // ---- O += P V on the int8 MMA (exact s32). k-step kb covers the thread's
+  //      tokens 16 tig + 8 kb + [0, 8): k = 4 tig + i is token +i, k = 16 +
+  //      4 tig + i is token +4+i, so the B fragment is bytes 8 kb .. 8 kb + 7
+  //      of the thread's 16-byte slice of V row d = 8 dn + grp, used as stored.
   const uint32_t P = p.page_tokens;
   const uint32_t vpitch = v_page_pitch(D, P);
   const uint8_t* vslice = sv + ((16 * tig) >> p.log2_page) * vpitch + ((16 * tig) & (P - 1));
 #pragma unroll
-  for (int md = 0; md < D / 16; ++md) {
-    const uint32_t d0 = 16 * md + grp, d1 = d0 + 8;
-    const uint4 va = *reinterpret_cast<const uint4*>(vslice + d0 * P);
-    const uint4 vb = *reinterpret_cast<const uint4*>(vslice + d1 * P);
-    const uint32_t wa[4] = {va.x, va.y, va.z, va.w};
-    const uint32_t wb[4] = {vb.x, vb.y, vb.z, vb.w};
+  for (int dn = 0; dn < D / 8; ++dn) {
+    const uint4 vw = *reinterpret_cast<const uint4*>(vslice + (8 * dn + grp) * P);
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
-      int lo[4] = {0, 0, 0, 0}, hi[4] = {0, 0, 0, 0};
+      int c4[4] = {0, 0, 0, 0};
+      imma_16832(c4, pa[nt][0][0], pa[nt][0][1], pa[nt][0][2], pa[nt][0][3], vw.x, vw.y);
+      imma_16832(c4, pa[nt][1][0], pa[nt][1][1], pa[nt][1][2], pa[nt][1][3], vw.z, vw.w);
+      // c0, c1: lo-limb sums of dims 8 dn + 2 tig + e; c2, c3: hi-limb sums.
+      // |lo sum| <= 64 * 128 * 128 and |hi sum| <= 64 * 128 * 64, so
+      // hi * 256 + lo (< 2^28) is exact in s32.
 #pragma unroll
-      for (int ks = 0; ks < 2; ++ks) {
-        imma_16832_s8u8(lo, wa[2 * ks], wb[2 * ks], wa[2 * ks + 1], wb[2 * ks + 1], blo[ks][nt][0],
-                        blo[ks][nt][1]);
-        imma_16832(hi, wa[2 * ks], wb[2 * ks], wa[2 * ks + 1], wb[2 * ks + 1], bhi[ks][nt][0],
-                   bhi[ks][nt][1]);
-      }
-      // |lo| <= 64 * 128 * 255 and |hi| <= 64 * 128 * 64, so hi * 256 + lo
-      // (< 2^28) is exact in s32.
-#pragma unroll
-      for (int i = 0; i < 4; ++i)
-        ws.acc[md][nt][i] = fmaf(float(hi[i] * 256 + lo[i]), inv_pscale[nt][i & 1], ws.acc[md][nt][i]);
+      for (int e = 0; e < 2; ++e)
+        ws.acc[dn][nt][e] = fmaf(float(c4[2 + e] * 256 + c4[e]), inv_pscale[nt], ws.acc[dn][nt][e]);
     }
+    if (dn % 4 == 3) asm volatile("" ::: "memory");
   }
 }
 
@@ -1003,15 +980,13 @@ __global__ void __maxnreg__((decode_max_regs<D, NT, BATCHED>())) decode_partial_
     const bool all_visible = load_query<D, NT, BATCHED>(p, pc, last, qf);
     WarpState<D, NT> ws;
 #pragma unroll
-    for (int md = 0; md < D / 16; ++md)
+    for (int dn = 0; dn < D / 8; ++dn)
 #pragma unroll
-      for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-        for (int i = 0; i < 4; ++i) ws.acc[md][nt][i] = 0.f;
+      for (int nt = 0; nt < NT; ++nt) ws.acc[dn][nt][0] = ws.acc[dn][nt][1] = 0.f;
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
-      ws.m[nt][0] = ws.m[nt][1] = -INFINITY;
-      ws.l[nt][0] = ws.l[nt][1] = 0.f;
+      ws.m[nt] = -INFINITY;
+      ws.l[nt] = 0.f;
     }
 
     const uint32_t n = pc.j1 - pc.j0;
@@ -1038,34 +1013,28 @@ __global__ void __maxnreg__((decode_max_regs<D, NT, BATCHED>())) decode_partial_
 
     // ---- flush this warp's state.
     float* cw = combine + size_t(warp) * L::kCols * L::kPitch;
-    float lsums[NT][2];
+    float lsums[NT];
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        float lsum = ws.l[nt][e];
-        lsum += __shfl_xor_sync(0xffffffffu, lsum, 4);
-        lsum += __shfl_xor_sync(0xffffffffu, lsum, 8);
-        lsum += __shfl_xor_sync(0xffffffffu, lsum, 16);
-        lsums[nt][e] = lsum;
-      }
+    for (int nt = 0; nt < NT; ++nt) {
+      float lsum = ws.l[nt];
+      lsum += __shfl_xor_sync(0xffffffffu, lsum, 1);
+      lsum += __shfl_xor_sync(0xffffffffu, lsum, 2);
+      lsums[nt] = lsum;
+    }
     // The combine buffer overlays ring slots that other warps may still read.
     if (!BATCHED) named_barrier(1, 32 * kConsumerWarps);
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const uint32_t col = 8 * nt + 2 * tig + e;
-        if (grp == 0) {
-          stats[(warp * L::kCols + col) * 2 + 0] = ws.m[nt][e];
-          stats[(warp * L::kCols + col) * 2 + 1] = lsums[nt][e];
-        }
-#pragma unroll
-        for (int md = 0; md < D / 16; ++md) {
-          cw[col * L::kPitch + 16 * md + grp] = ws.acc[md][nt][e];
-          cw[col * L::kPitch + 16 * md + grp + 8] = ws.acc[md][nt][2 + e];
-        }
+    for (int nt = 0; nt < NT; ++nt) {
+      const uint32_t col = 8 * nt + grp;
+      if (tig == 0) {
+        stats[(warp * L::kCols + col) * 2 + 0] = ws.m[nt];
+        stats[(warp * L::kCols + col) * 2 + 1] = lsums[nt];
       }
+#pragma unroll
+      for (int dn = 0; dn < D / 8; ++dn)
+        *reinterpret_cast<float2*>(cw + col * L::kPitch + 8 * dn + 2 * tig) =
+            make_float2(ws.acc[dn][nt][0], ws.acc[dn][nt][1]);
+    }
     if (x + n >= x1) grid_launch_dependents();
     named_barrier(1, 32 * kConsumerWarps);
 
