@@ -720,9 +720,21 @@ __device__ __forceinline__ void consume_stage(const DecodeParams& p, const uint8
   //      thread supplies the K row of token n = grp and gets back columns
   //      n = 2 tig + e, i.e. tokens 16 tig + 2 j + e (t = 2 j + e).
   float sc[NT][16];
+  // K rows are read one n-tile ahead of the MMAs that use them; the compiler
+  // fence after each read keeps it from hoisting further (register pressure).
+  uint4 kw[2][D / 64];
+#pragma unroll
+  for (int c = 0; c < D / 64; ++c)
+    kw[0][c] = *reinterpret_cast<const uint4*>(sk + (16 * (grp >> 1) + (grp & 1)) * D + 64 * c + 16 * tig);
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
-    const uint32_t tk = 16 * (grp >> 1) + 2 * j + (grp & 1);
+    if (j + 1 < 8) {
+      const uint32_t tk = 16 * (grp >> 1) + 2 * (j + 1) + (grp & 1);
+#pragma unroll
+      for (int c = 0; c < D / 64; ++c)
+        kw[(j + 1) & 1][c] = *reinterpret_cast<const uint4*>(sk + tk * D + 64 * c + 16 * tig);
+    }
+    asm volatile("" ::: "memory");
     int acc[kQk][4];
 #pragma unroll
     for (int mt = 0; mt < kQk; ++mt)
@@ -730,13 +742,13 @@ __device__ __forceinline__ void consume_stage(const DecodeParams& p, const uint8
       for (int i = 0; i < 4; ++i) acc[mt][i] = 0;
 #pragma unroll
     for (int c = 0; c < D / 64; ++c) {
-      const uint4 kw = *reinterpret_cast<const uint4*>(sk + tk * D + 64 * c + 16 * tig);
+      const uint4 k4 = kw[j & 1][c];
 #pragma unroll
       for (int mt = 0; mt < kQk; ++mt) {
         const uint32_t* a0 = qf.a[mt][2 * c];
         const uint32_t* a1 = qf.a[mt][2 * c + 1];
-        imma_16832(acc[mt], a0[0], a0[1], a0[2], a0[3], kw.x, kw.y);
-        imma_16832(acc[mt], a1[0], a1[1], a1[2], a1[3], kw.z, kw.w);
+        imma_16832(acc[mt], a0[0], a0[1], a0[2], a0[3], k4.x, k4.y);
+        imma_16832(acc[mt], a1[0], a1[1], a1[2], a1[3], k4.z, k4.w);
       }
     }
     // Limb k of column grp + 8 nt is row set 3 nt + k: C rows 0-7 (c0, c1) or
@@ -751,9 +763,6 @@ __device__ __forceinline__ void consume_stage(const DecodeParams& p, const uint8
         const int d2 = acc[r2 / 2][2 * (r2 % 2) + e];
         sc[nt][2 * j + e] = fmaf(float(d2), 65536.f, fmaf(float(d1), 256.f, float(d0)));
       }
-    // Keep the K loads of later n-tiles from being hoisted over this pair
-    // (register pressure; the other warps cover the load latency).
-    if (j % 2 == 1) asm volatile("" ::: "memory");
   }
 
   // ---- scores in log2 units, masking.
@@ -895,14 +904,19 @@ __device__ __forceinline__ void consume_stage(const DecodeParams& p, const uint8
   const uint32_t P = p.page_tokens;
   const uint32_t vpitch = v_page_pitch(D, P);
   const uint8_t* vslice = sv + ((16 * tig) >> p.log2_page) * vpitch + ((16 * tig) & (P - 1));
+  // V rows are read two n-tiles ahead of their MMAs, fenced like K.
+  uint4 vw[2];
+  vw[0] = *reinterpret_cast<const uint4*>(vslice + grp * P);
 #pragma unroll
   for (int dn = 0; dn < D / 8; ++dn) {
-    const uint4 vw = *reinterpret_cast<const uint4*>(vslice + (8 * dn + grp) * P);
+    if (dn + 1 < D / 8) vw[(dn + 1) & 1] = *reinterpret_cast<const uint4*>(vslice + (8 * (dn + 1) + grp) * P);
+    if (dn % 2 == 0) asm volatile("" ::: "memory");
+    const uint4 v4 = vw[dn & 1];
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
       int c4[4] = {0, 0, 0, 0};
-      imma_16832(c4, pa[nt][0][0], pa[nt][0][1], pa[nt][0][2], pa[nt][0][3], vw.x, vw.y);
-      imma_16832(c4, pa[nt][1][0], pa[nt][1][1], pa[nt][1][2], pa[nt][1][3], vw.z, vw.w);
+      imma_16832(c4, pa[nt][0][0], pa[nt][0][1], pa[nt][0][2], pa[nt][0][3], v4.x, v4.y);
+      imma_16832(c4, pa[nt][1][0], pa[nt][1][1], pa[nt][1][2], pa[nt][1][3], v4.z, v4.w);
       // c0, c1: lo-limb sums of dims 8 dn + 2 tig + e; c2, c3: hi-limb sums.
       // |lo sum| <= 64 * 128 * 128 and |hi sum| <= 64 * 128 * 64, so
       // hi * 256 + lo (< 2^28) is exact in s32.
@@ -910,7 +924,6 @@ __device__ __forceinline__ void consume_stage(const DecodeParams& p, const uint8
       for (int e = 0; e < 2; ++e)
         ws.acc[dn][nt][e] = fmaf(float(c4[2 + e] * 256 + c4[e]), inv_pscale[nt], ws.acc[dn][nt][e]);
     }
-    if (dn % 4 == 3) asm volatile("" ::: "memory");
   }
 }
 
