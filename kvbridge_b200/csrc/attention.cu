@@ -13,6 +13,9 @@
 #include <stdexcept>
 #include <utility>
 
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include "kvbridge/attention_b200.h"
 #include "kvbridge/attention_common.h"
 #include "launch_checks.h"
@@ -354,6 +357,50 @@ namespace {
 // Stages per CTA prefetched into L2 while the preceding grid finishes.
 constexpr uint32_t kPrefetchStages = 4;
 
+// cuTensorMapEncodeTiled through the runtime's driver entry point (the
+// library does not link libcuda); null when the driver does not offer it.
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static const PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult found{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &found) !=
+            cudaSuccess ||
+        found != cudaDriverEntryPointSuccess)
+      f = nullptr;
+    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+  }();
+  return fn;
+}
+
+// 16-token pages at dim <= 128: tensor maps of the K and V pools with one
+// row of page_tokens * dim bytes (read as 8-byte elements, <= 256 a row) per
+// (page, KV head), for the producer's four-row gathers. Anything that does
+// not fit a map (or a missing encoder) leaves gather_kv = 0: per-page copies.
+void set_gather_maps(kvb::DecodeParams& prm, uint32_t dim, uint64_t pages) {
+  prm.gather_kv = 0;
+  if (prm.page_tokens != 16) return;
+  const uint64_t row_bytes = uint64_t(prm.page_tokens) * dim;
+  const uint64_t row_elems = row_bytes / 8;
+  const uint64_t rows = pages * prm.kv_heads;
+  if (row_bytes % 16 != 0 || row_elems == 0 || row_elems > 256 || rows == 0 ||
+      rows > 0x7fffffffull)
+    return;
+  if (!aligned_to(prm.k, 16) || !aligned_to(prm.v, 16)) return;
+  const PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
+  if (encode == nullptr) return;
+  auto make = [&](CUtensorMap* map, const void* base) {
+    const cuuint64_t dims[2] = {row_elems, rows};
+    const cuuint64_t strides[1] = {row_bytes};
+    const cuuint32_t box[2] = {cuuint32_t(row_elems), 1};
+    const cuuint32_t elem_strides[2] = {1, 1};
+    return encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<void*>(base), dims, strides,
+                  box, elem_strides, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
+           CUDA_SUCCESS;
+  };
+  if (make(&prm.tm_k, prm.k) && make(&prm.tm_v, prm.v)) prm.gather_kv = 1;
+}
+
 // Kernel parameters of the single-sequence tensor-core path; partials go to
 // `scratch` with `split_stride` slots per row-head.
 kvb::DecodeParams single_params(const Shape& s, const DeviceInput& in, uint32_t parts,
@@ -390,6 +437,7 @@ kvb::DecodeParams single_params(const Shape& s, const DeviceInput& in, uint32_t 
   prm.ctas = parts * s.kv_heads * plan.groups;
   prm.total_stages = uint64_t(prm.seg_stages) * s.kv_heads;
   prm.score_scale = s.scale;
+  set_gather_maps(prm, s.dim, s.pages);
   return prm;
 }
 
@@ -537,6 +585,7 @@ void launch_attention_batched(const BatchShape& s, const BatchInput& in, void* w
   prm.col_groups = 1;
   prm.group_cols = 8 * ((group + 7) / 8);
   prm.score_scale = s.scale;
+  set_gather_maps(prm, s.dim, s.pages);
   v.launch(prm, stream);
 
   kvb::MergeParams mp{};

@@ -40,12 +40,19 @@
 //    any finite vscale works).
 //  * Pieces end with an in-CTA log-sum-exp combine of the four warps'
 //    states and one (m, l, n) write per query row.
+#include <cuda.h>
+
 #include "kvb_device.cuh"
 #include "kvb_schedule.h"
 
 namespace kvb {
 
 struct DecodeParams {
+  // 16-token pages at dim <= 128 (gather_kv = 1): the K and V pools as 2-D
+  // tensor maps of one row of page_tokens * dim bytes per (page, KV head),
+  // so that one gather load brings a stage's four pages.
+  CUtensorMap tm_k, tm_v;
+  uint32_t gather_kv;
   const float* q;
   const int64_t* q_positions;  // single sequence: [rows]; batched: unused
   const int64_t* k_positions;  // single sequence: [tokens]; batched: unused
@@ -90,10 +97,11 @@ struct StageLayout {
   static constexpr uint32_t kBytes = kVs + 256u;
 };
 
-// V page pitch inside a stage: pages of page_tokens < 64 get a 2*page_tokens
-// byte gap so the four 16-token groups of a warp land on distinct banks.
+// V page pitch inside a stage: the pages of a stage sit back to back (as a
+// gather load writes them). A warp's 16-byte V reads (row 8 dn + grp, tokens
+// 16 tig..) then take the minimum four wavefronts whatever the page size.
 __device__ __forceinline__ uint32_t v_page_pitch(uint32_t dim, uint32_t page_tokens) {
-  return dim * page_tokens + (page_tokens < 64 ? 2u * page_tokens : 0u);
+  return dim * page_tokens;
 }
 
 // RING_COMBINE: the warps' combine buffer reuses the start of the ring. A
@@ -420,6 +428,9 @@ __device__ void produce_small_pages(const DecodeParams& p, const Piece& only, ui
       if (__ballot_sync(0xffffffffu, mine && !ok) && lane == 0)
         atomicMax(&g_kvb_status, kStatusBadPage);
       const uint32_t okpages = __popc(__ballot_sync(0xffffffffu, ok && copier && !is_v));
+      // Lanes 0..15 and 16..31 each cover the stage's pages (four lanes a page).
+      const bool gather = pps == 4 && p.gather_kv != 0 && __all_sync(0xffffffffu, ok);
+      const int32_t unit32 = int32_t(uint32_t(ok ? t : 0u) * p.kv_heads + pc.h);
       const uint32_t slot = g % STAGES;
       if (mbar_wait_bounded(&empty[slot], ((g / STAGES) & 1u) ^ 1u, abort_flag,
                             kStatusEmptyWaitTimeout, int(g)) != kWaitOk)
@@ -434,7 +445,17 @@ __device__ void produce_small_pages(const DecodeParams& p, const Piece& only, ui
         mbar_arrive_expect_tx(&full[slot], okpages * kv_bytes);
       }
       __syncwarp();
-      if (ok && copier) {
+      if (gather) {
+        // All four pages of the stage are valid: two four-row gathers (K, V)
+        // instead of eight page copies (the bulk-copy request rate, not HBM,
+        // bounds 16-token pages).
+        const int32_t u0 = __shfl_sync(0xffffffffu, unit32, 0), u1 = __shfl_sync(0xffffffffu, unit32, 4);
+        const int32_t u2 = __shfl_sync(0xffffffffu, unit32, 8), u3 = __shfl_sync(0xffffffffu, unit32, 12);
+        if (lane == 0) {
+          tma_gather4(st + StageLayout<D>::kK, &p.tm_k, u0, u1, u2, u3, &full[slot], policy);
+          tma_gather4(st + StageLayout<D>::kV, &p.tm_v, u0, u1, u2, u3, &full[slot], policy);
+        }
+      } else if (ok && copier) {
         const size_t unit = size_t(t) * p.kv_heads + pc.h;
         if (is_v)
           bulk_copy_g2s(st + StageLayout<D>::kV + q * vpitch, p.v + unit * D * P, D * P,
@@ -946,7 +967,7 @@ constexpr int decode_max_regs() {
 }
 
 template <int D, int NT, int STAGES, bool SMALL_PAGES, bool BATCHED>
-__global__ void __maxnreg__((decode_max_regs<D, NT, BATCHED>())) decode_partial_kernel(DecodeParams p) {
+__global__ void __maxnreg__((decode_max_regs<D, NT, BATCHED>())) decode_partial_kernel(const __grid_constant__ DecodeParams p) {
   using L = DecodeSmem<D, NT, STAGES, !BATCHED>;
   extern __shared__ __align__(128) uint8_t smem[];
   uint8_t* ring = smem;

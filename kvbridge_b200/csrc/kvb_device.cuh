@@ -143,6 +143,21 @@ __device__ __forceinline__ void bulk_copy_g2s(void* dst, const void* src, uint32
       : "memory");
 }
 
+// Four-row gather (TMA tile::gather4) from a 2-D tensor map whose box is one
+// row high: rows r0..r3 of the map, from column 0, land back to back at
+// `dst` (128-byte aligned), completing their bytes on `bar`. The map lives
+// in kernel parameter space (a __grid_constant__ parameter).
+__device__ __forceinline__ void tma_gather4(void* dst, const void* tmap, int32_t r0, int32_t r1,
+                                            int32_t r2, int32_t r3, uint64_t* bar,
+                                            uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
+      ".L2::cache_hint [%0], [%1, {%2, %3, %4, %5, %6}], [%7], %8;" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(0), "r"(r0), "r"(r1), "r"(r2), "r"(r3),
+      "r"(smem_addr(bar)), "l"(policy)
+      : "memory");
+}
+
 // Prefetch the cache line holding `p` into L2.
 __device__ __forceinline__ void prefetch_line_l2(const void* p) {
   asm volatile("prefetch.global.L2 [%0];" ::"l"(p) : "memory");
