@@ -60,7 +60,7 @@ DeviceFacts current_device_facts() {
 struct FastVariant {
   const void* fn = nullptr;
   uint32_t smem = 0;
-  void (*launch)(const kvb::DecodeParams&, cudaStream_t) = nullptr;
+  void (*launch)(const kvb::DecodeParamsGather&, cudaStream_t) = nullptr;
 };
 
 void launch_pdl(const void* fn, dim3 grid, dim3 block, uint32_t smem, cudaStream_t stream,
@@ -90,14 +90,23 @@ cudaError_t prefer_max_shared(const void* fn) {
 }
 
 template <int D, int NT, int STAGES, bool SMALL, bool BATCHED>
-void launch_fast_variant(const kvb::DecodeParams& prm, cudaStream_t stream) {
+const void* kernel_fn() {
+  if constexpr (SMALL)
+    return reinterpret_cast<const void*>(&kvb::decode_partial_kernel_gather<D, NT, STAGES, BATCHED>);
+  else
+    return reinterpret_cast<const void*>(&kvb::decode_partial_kernel<D, NT, STAGES, false, BATCHED>);
+}
+
+template <int D, int NT, int STAGES, bool SMALL, bool BATCHED>
+void launch_fast_variant(const kvb::DecodeParamsGather& prm, cudaStream_t stream) {
   const void* fn =
-      reinterpret_cast<const void*>(&kvb::decode_partial_kernel<D, NT, STAGES, SMALL, BATCHED>);
+      kernel_fn<D, NT, STAGES, SMALL, BATCHED>();
   constexpr uint32_t smem = kvb::DecodeSmem<D, NT, STAGES, !BATCHED>::kBytes;
   cuda_ok(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)),
           "decode kernel shared-memory opt-in");
   cuda_ok(prefer_max_shared(fn), "decode kernel carveout");
-  kvb::DecodeParams copy = prm;
+  // 64-token-page kernels take the parameters without the gather maps.
+  kvb::KernelParams<SMALL> copy = prm;
   void* args[] = {&copy};
   launch_pdl(fn, dim3(prm.ctas), dim3(kvb::kDecodeThreads), smem, stream, args,
              "decode partial launch");
@@ -106,7 +115,7 @@ void launch_fast_variant(const kvb::DecodeParams& prm, cudaStream_t stream) {
 template <int D, int NT, int STAGES, bool SMALL, bool BATCHED>
 FastVariant make_variant() {
   FastVariant v;
-  v.fn = reinterpret_cast<const void*>(&kvb::decode_partial_kernel<D, NT, STAGES, SMALL, BATCHED>);
+  v.fn = kernel_fn<D, NT, STAGES, SMALL, BATCHED>();
   v.smem = kvb::DecodeSmem<D, NT, STAGES, !BATCHED>::kBytes;
   v.launch = &launch_fast_variant<D, NT, STAGES, SMALL, BATCHED>;
   return v;
@@ -376,7 +385,7 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
 // row of page_tokens * dim bytes (read as 8-byte elements, <= 256 a row) per
 // (page, KV head), for the producer's four-row gathers. Anything that does
 // not fit a map (or a missing encoder) leaves gather_kv = 0: per-page copies.
-void set_gather_maps(kvb::DecodeParams& prm, uint32_t dim, uint64_t pages) {
+void set_gather_maps(kvb::DecodeParamsGather& prm, uint32_t dim, uint64_t pages) {
   prm.gather_kv = 0;
   if (prm.page_tokens != 16) return;
   const uint64_t row_bytes = uint64_t(prm.page_tokens) * dim;
@@ -403,9 +412,9 @@ void set_gather_maps(kvb::DecodeParams& prm, uint32_t dim, uint64_t pages) {
 
 // Kernel parameters of the single-sequence tensor-core path; partials go to
 // `scratch` with `split_stride` slots per row-head.
-kvb::DecodeParams single_params(const Shape& s, const DeviceInput& in, uint32_t parts,
+kvb::DecodeParamsGather single_params(const Shape& s, const DeviceInput& in, uint32_t parts,
                                 float* scratch, uint32_t split_stride) {
-  kvb::DecodeParams prm{};
+  kvb::DecodeParamsGather prm{};
   prm.q = in.q;
   prm.q_positions = in.q_positions;
   prm.k_positions = in.k_positions;
@@ -453,7 +462,7 @@ unsigned launch_attention_partials(const Shape& s, const DeviceInput& in, unsign
   const uint32_t splits = split_count(s);
   const uint32_t parts = attention_partitions(s, partitions);
   if (parts == 0) return 0;
-  kvb::DecodeParams prm = single_params(s, in, parts, scratch, splits);
+  kvb::DecodeParamsGather prm = single_params(s, in, parts, scratch, splits);
   prm.prefetch_stages = kPrefetchStages;
   fast_variant(s.dim, prm.group_cols / 8, s.page_tokens, false).launch(prm, stream);
   return parts;
@@ -561,7 +570,7 @@ void launch_attention_batched(const BatchShape& s, const BatchInput& in, void* w
     throw std::invalid_argument("workspace smaller than batch_workspace_bytes(shape)");
   const uint32_t group = s.q_heads / s.kv_heads;
   const FastVariant v = fast_variant(s.dim, (group + 7) / 8, s.page_tokens, true);
-  kvb::DecodeParams prm{};
+  kvb::DecodeParamsGather prm{};
   prm.q = in.q;
   prm.table = in.block_table;
   prm.k = in.k;
@@ -750,7 +759,7 @@ void launch_attention_noalloc(const Shape& s, const DeviceInput& in, unsigned pa
   float* scratch = noalloc_scratch_on_current_device();
   if (parts > 0) {
     // Partials packed [row-head][partition]: split stride = parts.
-    const kvb::DecodeParams prm = single_params(s, in, parts, scratch, parts);
+    const kvb::DecodeParamsGather prm = single_params(s, in, parts, scratch, parts);
     fast_variant(s.dim, prm.group_cols / 8, s.page_tokens, false).launch(prm, stream);
   }
   launch_merge(kvb::kMergeScratch,

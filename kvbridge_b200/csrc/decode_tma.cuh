@@ -42,17 +42,14 @@
 //    states and one (m, l, n) write per query row.
 #include <cuda.h>
 
+#include <type_traits>
+
 #include "kvb_device.cuh"
 #include "kvb_schedule.h"
 
 namespace kvb {
 
 struct DecodeParams {
-  // 16-token pages at dim <= 128 (gather_kv = 1): the K and V pools as 2-D
-  // tensor maps of one row of page_tokens * dim bytes per (page, KV head),
-  // so that one gather load brings a stage's four pages.
-  CUtensorMap tm_k, tm_v;
-  uint32_t gather_kv;
   const float* q;
   const int64_t* q_positions;  // single sequence: [rows]; batched: unused
   const int64_t* k_positions;  // single sequence: [tokens]; batched: unused
@@ -82,6 +79,19 @@ struct DecodeParams {
   uint32_t col_groups, group_cols;
 };
 
+// Parameters of the small-page kernels. 16-token pages at dim <= 128
+// (gather_kv = 1): the K and V pools as 2-D tensor maps of one row of
+// page_tokens * dim bytes per (page, KV head), so that one gather load
+// brings a stage's four pages. Only these kernels carry the maps (256
+// bytes of parameters a launch otherwise).
+struct DecodeParamsGather : DecodeParams {
+  CUtensorMap tm_k, tm_v;
+  uint32_t gather_kv;
+};
+
+template <bool SMALL_PAGES>
+using KernelParams = typename std::conditional<SMALL_PAGES, DecodeParamsGather, DecodeParams>::type;
+
 constexpr int kConsumerWarps = 4;
 constexpr int kProducerWarp = kConsumerWarps;
 constexpr int kDecodeThreads = 32 * (kConsumerWarps + 1);
@@ -97,11 +107,15 @@ struct StageLayout {
   static constexpr uint32_t kBytes = kVs + 256u;
 };
 
-// V page pitch inside a stage: the pages of a stage sit back to back (as a
-// gather load writes them). A warp's 16-byte V reads (row 8 dn + grp, tokens
-// 16 tig..) then take the minimum four wavefronts whatever the page size.
+// V page pitch inside a stage. Small-page kernels: the pages of a stage sit
+// back to back (as a gather load writes them); a warp's 16-byte V reads (row
+// 8 dn + grp, tokens 16 tig..) take the minimum four wavefronts either way.
+// The 64-token-page kernels (one page a stage) keep the expression they were
+// tuned with: its register allocation measured ~0.1 us a call better at cfg2.
+template <bool SMALL_PAGES>
 __device__ __forceinline__ uint32_t v_page_pitch(uint32_t dim, uint32_t page_tokens) {
-  return dim * page_tokens;
+  if (SMALL_PAGES) return dim * page_tokens;
+  return dim * page_tokens + (page_tokens < 64 ? 2u * page_tokens : 0u);
 }
 
 // RING_COMBINE: the warps' combine buffer reuses the start of the ring. A
@@ -381,14 +395,14 @@ __device__ void mark_empty_splits(const DecodeParams& p, const Piece& pc) {
 // loads). With 64-token pages the extra per-stage work costs more than the
 // two copies it saves, so produce() keeps those.
 template <int D, int STAGES, bool BATCHED>
-__device__ void produce_small_pages(const DecodeParams& p, const Piece& only, uint8_t* ring,
+__device__ void produce_small_pages(const DecodeParamsGather& p, const Piece& only, uint8_t* ring,
                                     uint64_t* full, uint64_t* empty, volatile uint32_t* tags,
                                     volatile int* abort_flag) {
   const uint32_t lane = threadIdx.x & 31;
   const uint64_t policy = l2_evict_first_policy();
   const uint32_t P = p.page_tokens;
   const uint32_t kv_bytes = 2u * P * D;  // bulk-copied bytes per page
-  const uint32_t vpitch = v_page_pitch(D, P);
+  const uint32_t vpitch = v_page_pitch<true>(D, P);
   const uint32_t pps = kStageTokens >> p.log2_page;  // pages per stage: 2 or 4
   const uint32_t tok4 = 4u * (lane & 15u);
   const uint32_t q = tok4 >> p.log2_page;  // the lane's page within a stage
@@ -499,7 +513,7 @@ __device__ void produce(const DecodeParams& p, const Piece& only, uint8_t* ring,
   const uint64_t policy = l2_evict_first_policy();
   const uint32_t P = p.page_tokens;
   const uint32_t page_bytes = 2u * P * D + 8u * P;
-  const uint32_t vpitch = v_page_pitch(D, P);
+  const uint32_t vpitch = v_page_pitch<false>(D, P);
   // Work is handed out 8 pages at a time, four lanes per page: lane l
   // copies part l % 4 (K, V, K scales, V scales) of page l / 4 of the batch.
   // A batch covers spb stages of pps pages each. Table entries, page checks
@@ -725,7 +739,7 @@ __device__ __forceinline__ bool load_query(const DecodeParams& p, const Piece& p
 
 // One 64-token stage for one warp. The thread (grp, tig) works on columns
 // grp + 8 nt and on the stage's tokens 16 tig + [0, 16) (local index t).
-template <int D, int NT>
+template <int D, int NT, bool SMALL_PAGES>
 __device__ __forceinline__ void consume_stage(const DecodeParams& p, const uint8_t* st,
                                               uint32_t tb, uint32_t lo, uint32_t hi,
                                               bool all_visible, const QueryFrags<D, NT>& qf,
@@ -923,7 +937,7 @@ __device__ __forceinline__ void consume_stage(const DecodeParams& p, const uint8
   //      4 tig + i is token +4+i, so the B fragment is bytes 8 kb .. 8 kb + 7
   //      of the thread's 16-byte slice of V row d = 8 dn + grp, used as stored.
   const uint32_t P = p.page_tokens;
-  const uint32_t vpitch = v_page_pitch(D, P);
+  const uint32_t vpitch = v_page_pitch<SMALL_PAGES>(D, P);
   const uint8_t* vslice = sv + ((16 * tig) >> p.log2_page) * vpitch + ((16 * tig) & (P - 1));
   // V rows are read two n-tiles ahead of their MMAs, fenced like K.
   uint4 vw[2];
@@ -967,7 +981,7 @@ constexpr int decode_max_regs() {
 }
 
 template <int D, int NT, int STAGES, bool SMALL_PAGES, bool BATCHED>
-__global__ void __maxnreg__((decode_max_regs<D, NT, BATCHED>())) decode_partial_kernel(const __grid_constant__ DecodeParams p) {
+__device__ __forceinline__ void decode_partial_body(const KernelParams<SMALL_PAGES>& p) {
   using L = DecodeSmem<D, NT, STAGES, !BATCHED>;
   extern __shared__ __align__(128) uint8_t smem[];
   uint8_t* ring = smem;
@@ -1041,7 +1055,7 @@ __global__ void __maxnreg__((decode_max_regs<D, NT, BATCHED>())) decode_partial_
         mbar_wait_bounded(&full[slot], (g / STAGES) & 1u, abort_flag, kStatusFullWaitTimeout,
                           int(g));
       const uint32_t tb = (first_stage + pc.j0 + i) * kStageTokens;
-      consume_stage<D, NT>(p, ring + size_t(slot) * StageLayout<D>::kBytes, tb, pc.lo, pc.hi,
+      consume_stage<D, NT, SMALL_PAGES>(p, ring + size_t(slot) * StageLayout<D>::kBytes, tb, pc.lo, pc.hi,
                            all_visible, qf, ws);
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[slot]);
@@ -1122,6 +1136,21 @@ __global__ void __maxnreg__((decode_max_regs<D, NT, BATCHED>())) decode_partial_
     named_barrier(1, 32 * kConsumerWarps);
     x += n;
   }
+}
+
+// The kernels. 64-token pages take their parameters by value, as they always
+// have; the small-page kernels take theirs as a __grid_constant__ parameter,
+// whose tensor maps the gather loads read in place.
+template <int D, int NT, int STAGES, bool SMALL_PAGES, bool BATCHED>
+__global__ void __maxnreg__((decode_max_regs<D, NT, BATCHED>())) decode_partial_kernel(DecodeParams p) {
+  static_assert(!SMALL_PAGES, "small pages use decode_partial_kernel_gather");
+  decode_partial_body<D, NT, STAGES, false, BATCHED>(p);
+}
+
+template <int D, int NT, int STAGES, bool BATCHED>
+__global__ void __maxnreg__((decode_max_regs<D, NT, BATCHED>()))
+    decode_partial_kernel_gather(const __grid_constant__ DecodeParamsGather p) {
+  decode_partial_body<D, NT, STAGES, true, BATCHED>(p);
 }
 
 }  // namespace kvb
