@@ -275,10 +275,21 @@ def test_invalid_arguments_raise_before_launch(cuda_device):
         kvb.merge_attention(case.shape, scratch, 7, m, l, n)
 
 
-def test_batched_ragged(cuda_device):
-    """cfg3 flavour: ragged batch over one shared shuffled page pool."""
-    lens = synth.ragged_lengths(12, 1, 5000, seed=31) + [0, 64, 65]
-    bc = synth.make_batched(32, 8, 128, 64, lens, seed=0xC0FFEE + 3, device=cuda_device)
+@pytest.mark.parametrize(
+    "q_heads,kv_heads,dim,page_tokens,outliers",
+    [
+        (32, 8, 128, 64, 0.0),   # cfg3 flavour
+        (64, 8, 128, 16, 0.01),  # cfg4 flavour: GQA 8, Page16 (four-page gather loads), outliers
+        (16, 2, 64, 16, 0.0),    # dim 64, Page16
+    ],
+)
+def test_batched_ragged(cuda_device, q_heads, kv_heads, dim, page_tokens, outliers):
+    """Ragged batch over one shared shuffled page pool; lengths that end
+    inside a stage or a page take the per-page copies beside the gathers."""
+    lens = synth.ragged_lengths(12, 1, 5000, seed=31) + [0, 64, 65, 17, 4096]
+    bc = synth.make_batched(q_heads, kv_heads, dim, page_tokens, lens, seed=0xC0FFEE + 3, device=cuda_device,
+                            outlier_frac=outliers)
+    P, Hkv = page_tokens, kv_heads
     ws_bytes = kvb.batch_workspace_bytes(bc.shape)
     ws = torch.empty(ws_bytes // 4 + 1, dtype=torch.float32, device=cuda_device)
     B, H, D = bc.shape.batch, bc.shape.q_heads, bc.shape.dim
@@ -294,9 +305,9 @@ def test_batched_ragged(cuda_device):
         if length == 0:
             assert torch.all(l[sl] == 0) and torch.all(torch.isneginf(m[sl]))
             continue
-        npg = (length + 63) // 64
+        npg = (length + P - 1) // P
         table = bc.block_table[b, :npg].cpu()
-        shape = kvb.Shape(1, H, 8, D, 64, bc.shape.pages, length, 0, length, bc.shape.scale, True)
+        shape = kvb.Shape(1, H, Hkv, D, P, bc.shape.pages, length, 0, length, bc.shape.scale, True)
         ref = oracle.reference(shape, bc.q[b].cpu(), torch.tensor([length - 1]), torch.arange(length),
                                torch.cat([table, torch.zeros(bc.shape.pages - npg, dtype=torch.int32)]),
                                bc.k.cpu(), bc.v.cpu(), bc.k_scales.cpu(), bc.v_scales.cpu(), threads=8)
