@@ -1,24 +1,36 @@
 #!/usr/bin/env python3
 """Benchmark of the kvbridge-b200 decode-attention path (one JSON line).
 
-Workload (BASELINE cfg2): one decode call per step - batch 1, 65,536-token
-context, 32 query / 8 KV heads, head dim 128, INT8 K/V with per-(token, head)
-fp32 scales, 64-token pages shuffled, fp16 N(0,1) queries, split-K partitions
-chosen by the launcher, fp16 output. Inputs are seeded synthetic data.
+Headline workload (BASELINE cfg2): one decode call per step - batch 1,
+65,536-token context, 32 query / 8 KV heads, head dim 128, INT8 K/V with
+per-(token, head) fp32 scales, 64-token pages shuffled, fp16 N(0,1) queries,
+split-K partitions chosen by the launcher, fp16 output. Inputs are seeded
+synthetic data with BASELINE's value distributions.
 
-Each step reads a different KV "layer" out of `--layers` resident layers
-(138 MB each; 4 layers = 553 MB > 4x the 126 MB L2), so no step finds its KV
-in L2. Steps are issued as CUDA-graph replays of the public launch call, so
-host launch overhead is not in the device time.
+At N GPUs (torchrun, one rank per GPU) the headline is the SAME problem split
+over the ranks along KV heads (rank g owns KV heads [8g/N, 8(g+1)/N) and their
+query heads; no collective on the data path): strong scaling, value = the
+problem's KV bytes / the slowest rank's time per call. Two more keys:
+  * weak_replicated - every rank runs a whole cfg2 (8 KV heads of a model
+    with 8N), value = N x bytes / the slowest rank's time per call;
+  * cfg5_sequence_sharded - BASELINE cfg5 (4 sequences x 1,048,576 tokens)
+    split along the sequence: each rank decodes its page-aligned range of
+    every sequence (batched call), writes its (m, l, n) partial into one
+    packed buffer, the buffers are all-gathered in ONE NCCL collective and
+    merged by merge_attention_shards_ex, all inside the timed region.
 
-At N GPUs (torchrun, one rank per GPU) every rank runs the same per-GPU
-workload on its own 8 KV heads: KV-head sharding of a model with 8N KV heads,
-no collective on the data path (weak scaling). The timed region is bracketed
-by a barrier and cuda synchronize, timed with CUDA events, max over ranks.
+Timing: steps are replayed from CUDA graphs that hold a whole number of
+--steps-step blocks (>= --block-calls calls); the timed region repeats whole
+graph replays until it covers --min-seconds (>= 1 s), bracketed by a barrier
+and cuda synchronize, timed with CUDA events between replays on the launching
+stream; the time per call is the median over replays, max over ranks. Each
+step reads another of the resident KV "layers" (>= 553 MB in total, > 4x the
+126 MB L2), so no step finds its KV in L2. Clocks are sampled with nvidia-smi
+over exactly the headline's timed window.
 
 Metric: effective KV GB/s = algorithmic KV bytes (int8 K + V + fp32 K/V
 scales of every attended token and KV head: 2,112 B/token at 8 x 128) per
-call / time per call, summed over ranks; ms_per_step is the time per call.
+call / time per call; ms_per_step is the time per call.
 
 `--impl reference` times the reference's own CPU implementation (its FP64
 oracle compiled from its sources into oracle/_ref; the C restatement in
@@ -27,6 +39,7 @@ oracle/ when that build is absent) on the host cores, rank 0 only.
 from __future__ import annotations
 
 import argparse
+import datetime
 import json
 import math
 import os
@@ -54,18 +67,21 @@ WORKLOAD = dict(
     out_dtype="fp16",
 )
 SEED = 0xC0FFEE + 2
+L2_BYTES = 126 * 1024 * 1024
+RESIDENT_BYTES = 4 * 138_412_032  # KV bytes kept resident per timed leg (> 4x L2)
 
 
 def parse_args():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20000)
-    ap.add_argument("--warmup", type=int, default=200)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--partitions", type=int, default=0, help="split-K partitions per KV head (0 = auto)")
-    ap.add_argument("--layers", type=int, default=4, help="resident KV layers rotated over steps")
-    ap.add_argument("--graph-steps", type=int, default=100, help="calls captured per CUDA graph")
+    ap.add_argument("--min-seconds", type=float, default=1.5, help="length of each timed region")
+    ap.add_argument("--block-calls", type=int, default=500, help="calls per CUDA graph (rounded to whole step blocks)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extra", action="store_true", help="skip the weak-scaling and cfg5 keys")
     ap.add_argument("--config", choices=["cfg2", "cfg1", "cfg3", "cfg4", "cfg5"], default="cfg2",
                     help="BASELINE workload; the headline line is cfg2, the others are informational")
     return ap.parse_args()
@@ -105,7 +121,7 @@ def profiled_traffic():
 
 class ClockSampler:
     FIELDS = (
-        "index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+        "timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap"
     )
@@ -131,9 +147,10 @@ class ClockSampler:
 
     def _pump(self):
         for line in self.proc.stdout:
-            self.lines.append(line.strip())
+            self.lines.append((time.time(), line.strip()))
 
-    def stop(self):
+    def stop(self, window=None):
+        """Summary of the samples taken inside `window` (host times (t0, t1))."""
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
         self.proc.terminate()
@@ -145,16 +162,23 @@ class ClockSampler:
             self.thread.join(timeout=2)
         sms, maxes, reasons = [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in self.lines:
+        for arrived, line in self.lines:
             parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 9:
+            if len(parts) < 10:
+                continue
+            stamp = arrived
+            try:
+                stamp = datetime.datetime.strptime(parts[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+            except ValueError:
+                pass
+            if window is not None and not (window[0] <= stamp <= window[1]):
                 continue
             try:
-                sms.append(float(parts[1]))
-                maxes.append(float(parts[2]))
+                sms.append(float(parts[2]))
+                maxes.append(float(parts[3]))
             except ValueError:
                 continue
-            for name, flag in zip(names, parts[5:9]):
+            for name, flag in zip(names, parts[6:10]):
                 if flag.lower() == "active":
                     reasons.add(name)
         return {
@@ -178,10 +202,12 @@ def cpu_reference_runner(case_cpu, threads: int):
             case_cpu.k, case_cpu.v, case_cpu.k_scales, case_cpu.v_scales,
         )
         return "reference", (lambda: run.run(threads)), run
+
     def port():
         t0 = time.perf_counter()
         oracle.reference_case(case_cpu, threads=threads)
         return time.perf_counter() - t0
+
     return "port", port, None
 
 
@@ -254,7 +280,7 @@ def run_reference_arm(args):
         "warmup": warmup,
         "ms_per_step": round(per_call * 1e3, 4),
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong",
         "vs_baseline": None,
         "dtype": "f64",
         "data": "synthetic (seeded; BASELINE cfg2 value distributions)",
@@ -273,6 +299,116 @@ def run_reference_arm(args):
     }
     print(json.dumps(line), flush=True)
     return 0
+
+
+# ---------------------------------------------------------------------------
+# Timing: whole graph replays (or eager blocks) until the region is long.
+
+
+class Bench:
+    def __init__(self, args, world, rank, local_rank, device):
+        import torch
+
+        self.torch = torch
+        self.args = args
+        self.world, self.rank, self.local_rank, self.device = world, rank, local_rank, device
+        self.stream = torch.cuda.Stream(device=device)
+        self.steps = max(1, args.steps)
+        self.block = self.steps * max(1, math.ceil(args.block_calls / self.steps))
+
+    def barrier(self):
+        if self.world > 1:
+            import torch.distributed as dist
+
+            dist.barrier(device_ids=[self.local_rank])
+
+    def max_over_ranks(self, values):
+        torch = self.torch
+        if self.world == 1:
+            return list(values)
+        import torch.distributed as dist
+
+        t = torch.tensor(list(values), dtype=torch.float64, device=self.device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return [float(x) for x in t.tolist()]
+
+    def gather(self, value):
+        torch = self.torch
+        if self.world == 1:
+            return [value]
+        import torch.distributed as dist
+
+        t = torch.tensor([value], dtype=torch.float64, device=self.device)
+        out = torch.empty(self.world, dtype=torch.float64, device=self.device)
+        dist.all_gather_into_tensor(out, t)
+        return [float(x) for x in out.tolist()]
+
+    def capture(self, step, calls):
+        """A CUDA graph of `calls` steps (step(i) enqueues call i)."""
+        torch = self.torch
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=self.stream):
+            for i in range(calls):
+                step(i)
+        return g
+
+    def timed(self, block_fn, calls_per_block, warmup_blocks=1, min_seconds=None, window=None):
+        """Runs block_fn() (calls_per_block calls on self.stream) until the
+        region covers min_seconds; returns the median time per call (max over
+        ranks), the region's length and counts. `window`, when given, gets
+        the host times bracketing the timed region."""
+        torch = self.torch
+        min_seconds = self.args.min_seconds if min_seconds is None else min_seconds
+        with torch.cuda.stream(self.stream):
+            for _ in range(max(1, warmup_blocks)):
+                block_fn()
+        torch.cuda.synchronize()
+        # Calibrate the number of blocks (the same on every rank).
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(self.stream):
+            a.record(self.stream)
+            block_fn()
+            b.record(self.stream)
+        torch.cuda.synchronize()
+        t_block = max(a.elapsed_time(b), 1e-3) / 1e3
+        blocks = int(self.max_over_ranks([min(100000, max(3, math.ceil(min_seconds / t_block)))])[0])
+        events = [torch.cuda.Event(enable_timing=True) for _ in range(blocks + 1)]
+        torch.cuda.synchronize()
+        self.barrier()
+        torch.cuda.synchronize()
+        t0 = time.time()
+        with torch.cuda.stream(self.stream):
+            events[0].record(self.stream)
+            for i in range(blocks):
+                block_fn()
+                events[i + 1].record(self.stream)
+        torch.cuda.synchronize()
+        t1 = time.time()
+        self.barrier()
+        if window is not None:
+            window[:] = [t0, t1]
+        per_block = [events[i].elapsed_time(events[i + 1]) for i in range(blocks)]
+        total_ms = events[0].elapsed_time(events[-1])
+        med = statistics.median(per_block) / calls_per_block
+        mean = total_ms / (blocks * calls_per_block)
+        med_max, mean_max, total_max = self.max_over_ranks([med, mean, total_ms])
+        return {"per_call_ms": med_max, "mean_per_call_ms": mean_max, "region_s": total_max / 1e3,
+                "blocks": blocks, "calls": blocks * calls_per_block, "rank_per_call_ms": med}
+
+
+def check_status(kvb, where):
+    status = kvb.read_device_status()
+    if status != 0:
+        raise RuntimeError(f"{where}: kernel status word {status}: a bounded wait gave up or a page was bad "
+                           f"({kvb.read_wait_failure()}); numbers invalid")
+
+
+def make_layers(synth, world, rank, kv_heads, q_heads, device):
+    per_layer = kv_bytes_per_call(65536, kv_heads, 128)
+    count = max(4, math.ceil(RESIDENT_BYTES / per_layer))
+    return [synth.make_single(rows=1, q_heads=q_heads, kv_heads=kv_heads, dim=128, page_tokens=64, tokens=65536,
+                              seed=SEED + 1000 * rank + i, device=device) for i in range(count)]
 
 
 # ---------------------------------------------------------------------------
@@ -305,14 +441,18 @@ def main():
         raise RuntimeError(f"preload_attention_kernels failed: cudaError {rc}")
     if args.config != "cfg2":
         return run_other_config(args, world, rank, local_rank, device)
+    if 8 % world:
+        raise SystemExit(f"the 8 KV heads of cfg2 do not split over {world} GPUs")
 
-    # Resident KV layers of this rank.
-    layers = []
-    for i in range(args.layers):
-        layers.append(synth.make_single(rows=1, q_heads=32, kv_heads=8, dim=128, page_tokens=64, tokens=65536,
-                                        seed=SEED + 1000 * rank + i, device=device))
+    bench = Bench(args, world, rank, local_rank, device)
+    torch.cuda.synchronize()
+
+    # ---- headline: cfg2 split over the ranks along KV heads (strong scaling).
+    kv_local, q_local = 8 // world, 32 // world
+    layers = make_layers(synth, world, rank, kv_local, q_local, device)
     shape = layers[0].shape
-    nbytes = kv_bytes_per_call(shape.end - shape.begin, shape.kv_heads, shape.dim)
+    nbytes_rank = kv_bytes_per_call(shape.end - shape.begin, shape.kv_heads, shape.dim)
+    nbytes_problem = kv_bytes_per_call(65536, 8, 128)
     parts = kvb.attention_partitions(shape, args.partitions)
     scratch = torch.empty(kvb.scratch_elements(shape), device=device)
     rh = kvb.output_scalar_elements(shape)
@@ -329,68 +469,24 @@ def main():
     def partial_only(i):
         kvb.launch_attention_partials(shape, inputs[i % len(inputs)], scratch, partitions=args.partitions)
 
-    stream = torch.cuda.Stream(device=device)
-    torch.cuda.synchronize()
-
-    def capture(fn, count):
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g, stream=stream):
-            for i in range(count):
-                fn(i)
-        return g
-
-    gsteps = max(1, min(args.graph_steps, args.steps))
     # Warm the launch path (occupancy cache, opt-in) before capture.
-    with torch.cuda.stream(stream):
+    with torch.cuda.stream(bench.stream):
         for i in range(len(layers)):
             call(i)
     torch.cuda.synchronize()
-    g_call = capture(call, gsteps)
-    g_partial = capture(partial_only, gsteps)
-
-    def replay(graph, steps):
-        # CUDAGraph.replay() launches on the current stream: make it `stream`.
-        full, rest = divmod(steps, gsteps)
-        with torch.cuda.stream(stream):
-            for _ in range(full):
-                graph.replay()
-            fn = call if graph is g_call else partial_only
-            for i in range(rest):
-                fn(i)
-
+    g_call = bench.capture(call, bench.block)
+    g_partial = bench.capture(partial_only, bench.block)
     # The replayed graph must do the work of the eager calls (bitwise).
-    with torch.cuda.stream(stream):
-        call(gsteps - 1)
+    with torch.cuda.stream(bench.stream):
+        call(bench.block - 1)
     torch.cuda.synchronize()
     eager_out = out.clone()
     out.zero_()
-    replay(g_call, gsteps)
+    with torch.cuda.stream(bench.stream):
+        g_call.replay()
     torch.cuda.synchronize()
     if not torch.equal(out, eager_out):
         raise RuntimeError("graph replay output differs from the eager call")
-
-    def barrier():
-        if world > 1:
-            dist.barrier(device_ids=[local_rank])
-
-    def timed(graph, steps, warmup):
-        replay(graph, max(warmup, 3))
-        torch.cuda.synchronize()
-        barrier()
-        torch.cuda.synchronize()
-        start = torch.cuda.Event(enable_timing=True)
-        stop = torch.cuda.Event(enable_timing=True)
-        start.record(stream)
-        replay(graph, steps)
-        stop.record(stream)
-        torch.cuda.synchronize()
-        barrier()
-        ms = start.elapsed_time(stop)
-        if world > 1:
-            t = torch.tensor([ms], device=device)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            ms = float(t.item())
-        return ms
 
     # GPU id for nvidia-smi: the physical device behind this rank.
     props = torch.cuda.get_device_properties(device)
@@ -400,36 +496,25 @@ def main():
     sampler = ClockSampler(gpu_id)
     sampler.start()
     time.sleep(0.3)
-    total_ms = timed(g_call, args.steps, args.warmup)
-    # Keep the GPU busy on the same work until the sampler has >= 1 s of samples.
-    t_end = time.time() + max(0.0, 1.2 - total_ms / 1e3)
-    while time.time() < t_end:
-        replay(g_call, gsteps)
-        torch.cuda.synchronize()
-    clocks = sampler.stop()
-    kernel_ms = timed(g_partial, args.steps, args.warmup)
+    window = [0.0, 0.0]
+    head = bench.timed(g_call.replay, bench.block, warmup_blocks=max(1, math.ceil(args.warmup / bench.block)),
+                       window=window)
+    time.sleep(0.2)
+    clocks = sampler.stop(window)
+    kern = bench.timed(g_partial.replay, bench.block)
+    check_status(kvb, "headline")
+    rank_us = bench.gather(head["rank_per_call_ms"] * 1e3)
 
-    # Per-call latency distribution (events around each call, not in graphs).
-    lat = []
-    with torch.cuda.stream(stream):
-        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(200)]
-        for i, (a, b) in enumerate(evs):
-            a.record(stream)
-            call(i)
-            b.record(stream)
-    torch.cuda.synchronize()
-    lat = sorted(a.elapsed_time(b) * 1e3 for a, b in evs)
-
-    # End to end through the public API: per step, one H2D copy of the step's
-    # query, query positions and page table (packed in one pinned host
-    # buffer, as a caller stages a step's inputs) into a device staging
+    # ---- end to end through the public API: per step, one H2D copy of the
+    # step's query, query positions and page table (packed in one pinned
+    # host buffer, as a caller stages a step's inputs) into a device staging
     # buffer, the call on those device copies, and one D2H read of the fp16
     # output. As a serving loop would, the copies run on their own streams
     # with two staging and two output buffers, so that step i's input copy
     # and step i-1's output copy overlap the kernels of the neighbouring
     # steps; events order every copy against the calls that use its buffer.
     # All copies of the timed steps are inside the timed region (the streams
-    # join before the stop event). Captured as graphs like the device-time run.
+    # join before each stop event). Captured as graphs like the device run.
     q_bytes = layers[0].q.numel() * 4
     qpos_off = q_bytes
     table_off = (qpos_off + layers[0].q_positions.numel() * 8 + 15) // 16 * 16
@@ -451,6 +536,7 @@ def main():
     d2h_bytes = host_out[0].numel() * 2
     s_in = torch.cuda.Stream(device=device)
     s_out = torch.cuda.Stream(device=device)
+    stream = bench.stream
 
     def e2e_steps(count):
         """Enqueue `count` pipelined steps from `stream` and join back to it."""
@@ -483,53 +569,32 @@ def main():
 
     g_e2e = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g_e2e, stream=stream):
-        e2e_steps(gsteps)
-
-    def replay_e2e(steps):
-        full, rest = divmod(steps, gsteps)
-        with torch.cuda.stream(stream):
-            for _ in range(full):
-                g_e2e.replay()
-            if rest:
-                e2e_steps(rest)
-
-    replay_e2e(max(args.warmup, 3))
-    torch.cuda.synchronize()
-    barrier()
-    torch.cuda.synchronize()
-    a = torch.cuda.Event(enable_timing=True)
-    b = torch.cuda.Event(enable_timing=True)
-    a.record(stream)
-    replay_e2e(args.steps)
-    b.record(stream)
-    torch.cuda.synchronize()
-    barrier()
-    e2e_ms = a.elapsed_time(b)
-    if world > 1:
-        t = torch.tensor([e2e_ms], device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t.item())
+        e2e_steps(bench.block)
+    e2e = bench.timed(g_e2e.replay, bench.block)
     # The host copy of the last step's output must be that layer's result.
-    full, rest = divmod(args.steps, gsteps)
-    last = (rest if rest else gsteps) - 1
+    last = bench.block - 1
     e2e_out = host_out[last % 2].clone()
     with torch.cuda.stream(stream):
         call(last % len(layers))
     torch.cuda.synchronize()
     if not torch.equal(e2e_out, out.cpu()):
         raise RuntimeError("end-to-end output differs from the device-resident call")
+    check_status(kvb, "e2e")
+    del g_e2e, g_call, g_partial
+    torch.cuda.synchronize()
 
-    status = kvb.read_device_status()
-    if status != 0:
-        raise RuntimeError(f"kernel status word {status}: a bounded wait gave up "
-                           f"({kvb.read_wait_failure()}); numbers invalid")
+    extra = {}
+    if not args.no_extra:
+        if world > 1:
+            extra["weak_replicated"] = weak_replicated(args, bench, kvb, synth, world, rank, device)
+        extra["cfg5_sequence_sharded"] = cfg5_sequence_sharded(args, bench, kvb, synth, world, rank, device)
 
-    per_call_ms = total_ms / args.steps
-    value = world * nbytes / (per_call_ms / 1e3) / 1e9
-    kernel_per_launch_ms = kernel_ms / args.steps
-    achieved = nbytes / (kernel_per_launch_ms / 1e3) / 1e9
+    per_call_ms = head["per_call_ms"]
+    value = nbytes_problem / (per_call_ms / 1e3) / 1e9
+    kernel_per_launch_ms = kern["per_call_ms"]
+    achieved = nbytes_rank / (kernel_per_launch_ms / 1e3) / 1e9
     peak, peak_kind = measured_peak()
-    e2e_value = world * nbytes / (e2e_ms / args.steps / 1e3) / 1e9
+    e2e_value = nbytes_problem / (e2e["per_call_ms"] / 1e3) / 1e9
 
     line = {
         "metric": METRIC,
@@ -539,12 +604,17 @@ def main():
         "steps": args.steps,
         "warmup": args.warmup,
         "ms_per_step": round(per_call_ms, 6),
-        "us_per_call": {"mean": round(per_call_ms * 1e3, 3), "p50_single": round(lat[len(lat) // 2], 3),
-                        "p95_single": round(lat[int(len(lat) * 0.95)], 3)},
+        "us_per_call": {"median": round(per_call_ms * 1e3, 3), "mean": round(head["mean_per_call_ms"] * 1e3, 3),
+                        "per_rank_median": [round(x, 3) for x in rank_us]},
+        "timed_region": {"seconds": round(head["region_s"], 3), "calls": head["calls"],
+                         "graph_replays": head["blocks"], "calls_per_replay": bench.block,
+                         "how": f"{head['blocks']} replays of a CUDA graph of {bench.block} calls "
+                                f"({bench.block // bench.steps} blocks of --steps {bench.steps}), events between "
+                                "replays, median per call, max over ranks"},
         "pct_of_hbm_peak": {"of_8000_gbs": round(100 * value / world / 8000.0, 2),
                             f"of_{peak_kind}_{peak:.0f}_gbs": round(100 * value / world / peak, 2)},
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong",
         "vs_baseline": None,
         "dtype": "int8",
         "data": "synthetic (seeded; fp16 N(0,1) Q, absmax-int8 N(0,1) K/V, shuffled pages)",
@@ -553,10 +623,11 @@ def main():
             partitions=parts,
             layers_rotated=len(layers),
             l2="inputs larger than L2: each step reads another of the resident KV layers "
-               f"({len(layers)} x {nbytes / 1e6:.1f} MB)",
-            sharding=f"kv-heads: {8 * world} KV heads, 8 per GPU" if world > 1 else "single GPU",
-            launch="CUDA-graph replay of launch_attention_ex (partial kernel, then LSE merge kernel with "
-                   "the fp16 epilogue; programmatic dependent launch between them)",
+               f"({len(layers)} x {nbytes_rank / 1e6:.1f} MB per GPU)",
+            sharding=(f"kv-heads: the 8 KV heads of one cfg2 problem split {kv_local} per GPU "
+                      f"({q_local} query heads each), no collective" if world > 1 else "single GPU"),
+            launch="CUDA-graph replay of launch_attention_ex (partial kernel, then LSE merge kernel with the fp16 "
+                   "epilogue; programmatic dependent launch between them)",
             compute="QK: int8 mma.sync m16n8k32 on raw K codes x 3 int8 limbs of Q (exact s32); "
                     "PV: int8 mma.sync m16n8k32 on raw V codes x 2 int8 limbs of 14-bit fixed-point "
                     "P = softmax weight x V scale (exact s32), fp32 accumulation",
@@ -569,8 +640,8 @@ def main():
             "unit": "GB/s",
             "frac": round(achieved / peak, 4),
             "peak_kind": peak_kind,
-            "algorithmic_bytes_per_launch": nbytes,
-            "traffic": profiled_traffic(),
+            "algorithmic_bytes_per_launch": nbytes_rank,
+            "traffic": profiled_traffic() if world == 1 else None,
             "kernel_us_per_launch": round(kernel_per_launch_ms * 1e3, 3),
         },
         "e2e": {
@@ -578,16 +649,18 @@ def main():
             "unit": "GB/s",
             "h2d_bytes_per_step": h2d_bytes,
             "d2h_bytes_per_step": d2h_bytes,
-            "us_per_call": round(e2e_ms / args.steps * 1e3, 3),
-            "how": "public API launch_attention_ex; every step one H2D copy of that step's Q, q_positions "
-                   "and page table (packed in one pinned host buffer) and one D2H copy of the fp16 output, "
-                   "on two copy streams with double-buffered staging and outputs so that they overlap the "
-                   "neighbouring steps' kernels (all inside the timed region), CUDA-graph replayed; the KV "
-                   "cache is resident device state",
+            "us_per_call": round(e2e["per_call_ms"] * 1e3, 3),
+            "how": "public API launch_attention_ex; every step one H2D copy of that step's Q, q_positions and page "
+                   "table (packed in one pinned host buffer) and one D2H copy of the fp16 output, on two copy "
+                   "streams with double-buffered staging and outputs so that they overlap the neighbouring steps' "
+                   "kernels (all inside the timed region), CUDA-graph replayed; the KV cache is resident device "
+                   "state; per GPU at N > 1",
         },
-        "gpu_launches": 2 * args.steps,
-        "clocks": {k: clocks[k] for k in ("sm_mhz", "sm_max_mhz", "reasons")},
+        "gpu_launches": 2 * head["calls"],
+        "clocks": {k: clocks[k] for k in ("sm_mhz", "sm_max_mhz", "reasons", "samples")},
     }
+    if extra:
+        line["extra"] = extra
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
         case_cpu = synth.SingleCase(*(
             [layers[0].shape] + [getattr(layers[0], f).cpu() for f in
@@ -596,11 +669,98 @@ def main():
         line["cpu_baseline"] = cpu_baseline(case_cpu)
     if rank == 0:
         print(json.dumps(line), flush=True)
-    del g_call, g_partial, g_e2e
     if world > 1:
         dist.barrier(device_ids=[local_rank])
         dist.destroy_process_group()
     return 0
+
+
+def weak_replicated(args, bench, kvb, synth, world, rank, device):
+    """Every rank a whole cfg2 (8 KV heads of a model with 8N): weak scaling."""
+    import torch
+
+    layers = make_layers(synth, world, rank + 97, 8, 32, device)
+    shape = layers[0].shape
+    scratch = torch.empty(kvb.scratch_elements(shape), device=device)
+    m = torch.empty(32, device=device)
+    l = torch.empty(32, device=device)
+    n = torch.empty(32 * 128, device=device)
+    out = torch.empty(32 * 128, dtype=torch.float16, device=device)
+    inputs = [c.device_input() for c in layers]
+
+    def call(i):
+        kvb.launch_attention_ex(shape, inputs[i % len(inputs)], scratch, m, l, n, out_f16=out)
+
+    with torch.cuda.stream(bench.stream):
+        for i in range(len(layers)):
+            call(i)
+    torch.cuda.synchronize()
+    g = bench.capture(call, bench.block)
+    t = bench.timed(g.replay, bench.block)
+    check_status(kvb, "weak_replicated")
+    del g
+    nbytes = kv_bytes_per_call(65536, 8, 128)
+    value = world * nbytes / (t["per_call_ms"] / 1e3) / 1e9
+    return {"value": round(value, 2), "unit": "GB/s", "scaling": "weak",
+            "us_per_call": round(t["per_call_ms"] * 1e3, 3), "calls": t["calls"],
+            "config": f"each GPU a whole cfg2 (8 KV heads, 65,536 ctx), {8 * world} KV heads in the job"}
+
+
+def cfg5_sequence_sharded(args, bench, kvb, synth, world, rank, device):
+    """BASELINE cfg5, 4 x 1,048,576 tokens, split along the sequence: each
+    rank decodes its page-aligned range of every sequence (one batched call
+    into a packed [m | l | n] buffer); at N > 1 the buffers are all-gathered
+    in one NCCL collective and merged with merge_attention_shards_ex, inside
+    the timed region. Steps are eager launches, timed in blocks of --steps."""
+    import torch
+
+    from kvbridge_b200 import sharding
+
+    tokens, batch, H, D = 1 << 20, 4, 32, 128
+    ranges = sharding.sequence_ranges(tokens, 64, world)
+    b0, b1 = ranges[rank]
+    local = b1 - b0
+    bc = synth.make_batched(H, 8, D, 64, [local] * batch, seed=0xC0FFEE + 50 + rank, device=device)
+    ws_bytes = kvb.batch_workspace_bytes(bc.shape)
+    ws = torch.empty(ws_bytes // 4 + 16, device=device)
+    rh = batch * H
+    packed = torch.empty(rh * (D + 2), device=device)
+    pm, pl, pn = sharding.packed_views(packed, rh, D)
+    binp = bc.batch_input()
+    out = torch.empty(rh * D, dtype=torch.float16, device=device)
+    merge = sharding.gpu_packed_shard_merge(rh, D, device) if world > 1 else None
+
+    def local_step():
+        kvb.launch_attention_batched(bc.shape, binp, ws, ws_bytes, pm, pl, pn, out if world == 1 else None)
+
+    def full_step():
+        local_step()
+        if world > 1:
+            gathered = sharding.all_gather_packed(packed)
+            merge(gathered)
+
+    def block(fn):
+        def run():
+            for _ in range(bench.steps):
+                fn()
+        return run
+
+    full = bench.timed(block(full_step), bench.steps)
+    loc = bench.timed(block(local_step), bench.steps) if world > 1 else full
+    check_status(kvb, "cfg5")
+    total_bytes = batch * tokens * 8 * (2 * D + 8)
+    value = total_bytes / (full["per_call_ms"] / 1e3) / 1e9
+    del bc, ws
+    torch.cuda.empty_cache()
+    return {"value": round(value, 2), "unit": "GB/s", "scaling": "strong",
+            "us_per_call": round(full["per_call_ms"] * 1e3, 3),
+            "local_decode_us": round(loc["per_call_ms"] * 1e3, 3),
+            "exchange_and_merge_us": round((full["per_call_ms"] - loc["per_call_ms"]) * 1e3, 3),
+            "kv_bytes_per_step": total_bytes, "calls": full["calls"],
+            "pct_of_measured_hbm_per_gpu": round(100 * value / world / measured_peak()[0], 2),
+            "config": f"4 x 1,048,576 ctx, 32/8 heads, dim 128, Page64; {local} tokens of each sequence per GPU"
+                      + ("; one NCCL all-gather of the packed (m, l, n) partials + merge_attention_shards_ex"
+                         if world > 1 else "")}
 
 
 # ---------------------------------------------------------------------------
@@ -612,149 +772,90 @@ def run_other_config(args, world, rank, local_rank, device):
     32 (lengths U[1024, 32768]) with the 8 KV heads split over the ranks.
     cfg4: batch 64 x 16,384, 64 q / 8 kv heads, Page16, 1 % 10x outliers, KV
     heads split over the ranks. cfg5: batch 4 x 1,048,576 tokens, sequence
-    split over the ranks; each rank's (m, l, n) partial is all-gathered and
-    merged with merge_attention_shards. Value = all ranks' KV bytes / time."""
+    split over the ranks. Value = all ranks' KV bytes / time."""
     import torch
     import torch.distributed as dist
 
     import kvbridge_b200 as kvb
     from kvbridge_b200 import sharding, synth
 
-    stream = torch.cuda.Stream(device=device)
-    steps, warmup = args.steps, max(args.warmup, 3)
+    bench = Bench(args, world, rank, local_rank, device)
     cfg = args.config
-    if cfg == "cfg1":
-        case = synth.make_single(rows=1, q_heads=32, kv_heads=8, dim=128, page_tokens=64, tokens=4096,
-                                 seed=0xC0FFEE + 1 + rank, device=device)
-        scratch = torch.empty(kvb.scratch_elements(case.shape), device=device)
-        m = torch.empty(32, device=device)
-        l = torch.empty(32, device=device)
-        n = torch.empty(32 * 128, device=device)
-        out = torch.empty(32 * 128, dtype=torch.float16, device=device)
-        inp = case.device_input()
-
-        def step(i):
-            kvb.launch_attention_ex(case.shape, inp, scratch, m, l, n, partitions=8, out_f16=out)
-
-        total_bytes = world * case.kv_bytes()
-        desc = dict(workload="cfg1: B1, 4,096 ctx, 32/8, dim 128, Page64 shuffled, 8 partitions",
-                    scaling="weak (one call per GPU)")
-        use_graph = True
-    elif cfg in ("cfg3", "cfg4"):
-        if cfg == "cfg3":
-            lens = synth.ragged_lengths(32, 1024, 32768, seed=0xC0FFEE + 3)
-            q_heads, kv_heads, page, outl = 32, 8, 64, 0.0
-        else:
-            lens = [16384] * 64
-            q_heads, kv_heads, page, outl = 64, 8, 16, 0.01
-        h0, h1 = sharding.kv_head_range(kv_heads, world, rank)
-        kv_local = h1 - h0
-        q_local = q_heads // kv_heads * kv_local
-        bc = synth.make_batched(q_local, kv_local, 128, page, lens, seed=0xC0FFEE + 10 * rank + (3 if cfg == "cfg3" else 4),
-                                device=device, outlier_frac=outl)
-        ws_bytes = kvb.batch_workspace_bytes(bc.shape)
-        ws = torch.empty(ws_bytes // 4 + 16, device=device)
-        B = bc.shape.batch
-        m = torch.empty(B * q_local, device=device)
-        l = torch.empty(B * q_local, device=device)
-        n = torch.empty(B * q_local * 128, device=device)
-        out = torch.empty(B * q_local * 128, dtype=torch.float16, device=device)
-        binp = bc.batch_input()
-
-        def step(i):
-            kvb.launch_attention_batched(bc.shape, binp, ws, ws_bytes, m, l, n, out)
-
-        total_bytes = sum(lens) * kv_heads * (2 * 128 + 8)
-        desc = dict(workload=f"{cfg}: batch {len(lens)}, {q_heads}/{kv_heads} heads, dim 128, Page{page}"
-                             + (", ragged U[1024,32768]" if cfg == "cfg3" else ", 16,384 ctx, 1% 10x outliers"),
-                    sharding=f"kv-heads: {kv_local} of {kv_heads} per GPU", scaling="strong")
-        use_graph = True
-    else:  # cfg5
-        tokens = 1 << 20
-        ranges = sharding.sequence_ranges(tokens, 64, world)
-        b0, b1 = ranges[rank]
-        local = b1 - b0
-        bc = synth.make_batched(32, 8, 128, 64, [local] * 4, seed=0xC0FFEE + 50 + rank, device=device)
-        ws_bytes = kvb.batch_workspace_bytes(bc.shape)
-        ws = torch.empty(ws_bytes // 4 + 16, device=device)
-        rh = 4 * 32
-        m = torch.empty(rh, device=device)
-        l = torch.empty(rh, device=device)
-        n = torch.empty(rh * 128, device=device)
-        binp = bc.batch_input()
-        merge = sharding.gpu_shard_merge(rh, 128)
-
-        def step(i):
-            kvb.launch_attention_batched(bc.shape, binp, ws, ws_bytes, m, l, n, None)
-            if world > 1:
-                mp, lp, np_ = sharding.all_gather_partials(m, l, n)
-                merge(mp, lp, np_.reshape(world, rh * 128))
-
-        total_bytes = 4 * tokens * 8 * (2 * 128 + 8)
-        desc = dict(workload="cfg5: batch 4 x 1,048,576 ctx, 32/8 heads, dim 128, Page64",
-                    sharding=f"sequence: {local} tokens of each sequence per GPU, NCCL all-gather "
-                             "of (m, l, n) + merge_attention_shards",
+    if cfg == "cfg5":
+        res = cfg5_sequence_sharded(args, bench, kvb, synth, world, rank, device)
+        total_bytes, per = res["kv_bytes_per_step"], res["us_per_call"] / 1e3
+        desc = dict(workload="cfg5: batch 4 x 1,048,576 ctx, 32/8 heads, dim 128, Page64", detail=res,
                     scaling="strong")
-        use_graph = world == 1
+        timing = "eager launches"
+    else:
+        if cfg == "cfg1":
+            case = synth.make_single(rows=1, q_heads=32, kv_heads=8, dim=128, page_tokens=64, tokens=4096,
+                                     seed=0xC0FFEE + 1 + rank, device=device)
+            scratch = torch.empty(kvb.scratch_elements(case.shape), device=device)
+            m = torch.empty(32, device=device)
+            l = torch.empty(32, device=device)
+            n = torch.empty(32 * 128, device=device)
+            out = torch.empty(32 * 128, dtype=torch.float16, device=device)
+            inp = case.device_input()
 
-    def run(count):
-        with torch.cuda.stream(stream):
-            for i in range(count):
-                step(i)
+            def step(i):
+                kvb.launch_attention_ex(case.shape, inp, scratch, m, l, n, partitions=8, out_f16=out)
 
-    run(2)
-    torch.cuda.synchronize()
-    graph = None
-    if use_graph:
-        gsteps = max(1, min(args.graph_steps, steps))
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph, stream=stream):
-            for i in range(gsteps):
-                step(i)
+            total_bytes = world * case.kv_bytes()
+            desc = dict(workload="cfg1: B1, 4,096 ctx, 32/8, dim 128, Page64 shuffled, 8 partitions",
+                        scaling="weak")
+        else:
+            if cfg == "cfg3":
+                lens = synth.ragged_lengths(32, 1024, 32768, seed=0xC0FFEE + 3)
+                q_heads, kv_heads, page, outl = 32, 8, 64, 0.0
+            else:
+                lens = [16384] * 64
+                q_heads, kv_heads, page, outl = 64, 8, 16, 0.01
+            h0, h1 = sharding.kv_head_range(kv_heads, world, rank)
+            kv_local = h1 - h0
+            q_local = q_heads // kv_heads * kv_local
+            bc = synth.make_batched(q_local, kv_local, 128, page, lens,
+                                    seed=0xC0FFEE + 10 * rank + (3 if cfg == "cfg3" else 4),
+                                    device=device, outlier_frac=outl)
+            ws_bytes = kvb.batch_workspace_bytes(bc.shape)
+            ws = torch.empty(ws_bytes // 4 + 16, device=device)
+            B = bc.shape.batch
+            m = torch.empty(B * q_local, device=device)
+            l = torch.empty(B * q_local, device=device)
+            n = torch.empty(B * q_local * 128, device=device)
+            out = torch.empty(B * q_local * 128, dtype=torch.float16, device=device)
+            binp = bc.batch_input()
 
-        def run(count):  # noqa: F811 - graph replays from here on
-            full, rest = divmod(count, gsteps)
-            with torch.cuda.stream(stream):
-                for _ in range(full):
-                    graph.replay()
-                for i in range(rest):
-                    step(i)
+            def step(i):
+                kvb.launch_attention_batched(bc.shape, binp, ws, ws_bytes, m, l, n, out)
 
-    run(warmup)
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier(device_ids=[local_rank])
-    torch.cuda.synchronize()
-    a = torch.cuda.Event(enable_timing=True)
-    b = torch.cuda.Event(enable_timing=True)
-    a.record(stream)
-    run(steps)
-    b.record(stream)
-    torch.cuda.synchronize()
-    ms = a.elapsed_time(b)
-    if world > 1:
-        t = torch.tensor([ms], device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-    status = kvb.read_device_status()
-    if status != 0:
-        raise RuntimeError(f"kernel status word {status} ({kvb.read_wait_failure()}); numbers invalid")
-    per = ms / steps
+            total_bytes = sum(lens) * kv_heads * (2 * 128 + 8)
+            desc = dict(workload=f"{cfg}: batch {len(lens)}, {q_heads}/{kv_heads} heads, dim 128, Page{page}"
+                                 + (", ragged U[1024,32768]" if cfg == "cfg3" else ", 16,384 ctx, 1% 10x outliers"),
+                        sharding=f"kv-heads: {kv_local} of {kv_heads} per GPU", scaling="strong")
+        with torch.cuda.stream(bench.stream):
+            step(0)
+        torch.cuda.synchronize()
+        calls = bench.steps * max(1, math.ceil(50 / bench.steps))
+        graph = bench.capture(step, calls)
+        t = bench.timed(graph.replay, calls)
+        check_status(kvb, cfg)
+        del graph
+        per = t["per_call_ms"]
+        timing = f"CUDA-graph replays of {calls} calls, >= {args.min_seconds} s, median per call"
     peak, peak_kind = measured_peak()
     value = total_bytes / (per / 1e3) / 1e9
     line = {
-        "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": steps,
-        "warmup": warmup, "ms_per_step": round(per, 6), "higher_is_better": True,
+        "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(per, 6), "higher_is_better": True,
         "scaling": desc.pop("scaling"), "vs_baseline": None, "dtype": "int8",
         "data": "synthetic (seeded; BASELINE value distributions)",
         "pct_of_hbm_peak_per_gpu": round(100 * value / world / peak, 2), "peak": f"{peak} GB/s ({peak_kind})",
-        "config": dict(desc, kv_bytes_per_step=total_bytes,
-                       launch="CUDA-graph replays" if graph is not None else "eager launches + NCCL"),
+        "config": dict(desc, kv_bytes_per_step=total_bytes, launch=timing),
         "informational": "not the headline workload (cfg2)",
     }
     if rank == 0:
         print(json.dumps(line), flush=True)
-    del graph
     if world > 1:
         dist.barrier(device_ids=[local_rank])
         dist.destroy_process_group()

@@ -24,6 +24,9 @@ struct LaunchOptions {
   unsigned partitions;
   // Optional __half[rows * q_heads * dim]: out = n / l where l > 0, else 0.
   void* out_f16;
+  // Optional __nv_bfloat16[rows * q_heads * dim], the same n / l in bf16 (for
+  // an out-projection that takes bf16 activations). Either, both or neither.
+  void* out_bf16 = nullptr;
 };
 
 // True when launch_attention(_ex) will use the TMA/tensor-core kernel for this
@@ -52,6 +55,9 @@ unsigned launch_attention_partials(const Shape&, const DeviceInput&, unsigned pa
                                    float* scratch, cudaStream_t);
 void merge_attention_ex(const Shape&, const float* scratch, unsigned partitions, float* m,
                         float* l, float* n, void* out_f16, cudaStream_t);
+// The same with an optional bf16 output beside (or instead of) the fp16 one.
+void merge_attention_ex(const Shape&, const float* scratch, unsigned partitions, float* m,
+                        float* l, float* n, void* out_f16, void* out_bf16, cudaStream_t);
 
 // Ragged batch: sequence b attends its tokens [0, seq_lens[b]) (all visible;
 // the query is the next token). Logical page j of sequence b lives at physical
@@ -81,6 +87,10 @@ size_t batch_workspace_bytes(const BatchShape&);
 void launch_attention_batched(const BatchShape&, const BatchInput&, void* workspace,
                               size_t workspace_bytes, float* m, float* l, float* n,
                               void* out_f16, cudaStream_t);
+// The same with an optional bf16 output beside (or instead of) the fp16 one.
+void launch_attention_batched(const BatchShape&, const BatchInput&, void* workspace,
+                              size_t workspace_bytes, float* m, float* l, float* n,
+                              void* out_f16, void* out_bf16, cudaStream_t);
 
 // Merge `shards` partial results, shard-major: m_parts/l_parts
 // float[shards * row_heads], n_parts float[shards * row_heads * dim]. The
@@ -89,6 +99,15 @@ void launch_attention_batched(const BatchShape&, const BatchInput&, void* worksp
 void merge_attention_shards(unsigned shards, unsigned row_heads, unsigned dim,
                             const float* m_parts, const float* l_parts, const float* n_parts,
                             float* m, float* l, float* n, void* out_f16, cudaStream_t);
+// The same with a shard stride and an optional bf16 output. shard_stride is
+// the distance in floats from one shard's m (and l, and n) to the next
+// shard's: 0 keeps the layout above; row_heads * (dim + 2) reads a packed
+// exchange buffer [shard][m | l | n] (one all-gather of every rank's
+// partial, m at 0, l at row_heads, n at 2 * row_heads of each block).
+void merge_attention_shards_ex(unsigned shards, unsigned row_heads, unsigned dim,
+                               const float* m_parts, const float* l_parts, const float* n_parts,
+                               size_t shard_stride, float* m, float* l, float* n, void* out_f16,
+                               void* out_bf16, cudaStream_t);
 
 // Paged KV append (the step before decode; no counterpart in the reference,
 // whose fixtures write codes and scales directly): quantises new K and V rows
@@ -123,5 +142,27 @@ cudaError_t read_device_status(int* status);
 // {status code, block, warp, stage, waited ns, waited SM cycles}. Reading
 // clears it.
 cudaError_t read_wait_failure(long long* record6);
+
+// Upper bound, in nanoseconds, of any single pipeline wait inside the kernels
+// launched after this call (process-wide; 0 restores the default of 2 s). A
+// correct call never waits more than microseconds; the bound only turns a
+// broken pipeline into a status code instead of a held GPU.
+void set_wait_limit_ns(unsigned long long ns) noexcept;
+unsigned long long wait_limit_ns() noexcept;
+
+namespace detail {
+// Test hooks for the failure paths (no effect unless armed; both are
+// thread-local and one-shot).
+//  * fail_launch(nth, code): the nth kernel launch this library makes on the
+//    calling thread after the call (1 = the next one) is not made; the call
+//    that would make it throws std::runtime_error with cudaGetErrorString(code)
+//    as if the launch had failed. nth = 0 disarms.
+//  * skip_stage(stage): in the next tensor-core partial launch on the calling
+//    thread, the producer of CTA 0 leaves its pipeline stage `stage` unarmed,
+//    so that a consumer wait runs into the wait limit and the kernel reports
+//    status 1 and returns.
+void fail_launch(unsigned nth, cudaError_t code) noexcept;
+void skip_stage(unsigned stage) noexcept;
+}  // namespace detail
 
 }  // namespace kvbridge

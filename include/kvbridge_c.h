@@ -87,6 +87,12 @@ int kvb_launch_attention_ex(const kvb_shape* s, const kvb_device_input* in, unsi
                             void* out_f16, float* scratch, float* m, float* l, float* n,
                             void* stream);
 
+/* kvb_launch_attention_ex with an optional bf16 output beside (or instead
+ * of) the fp16 one (kvbridge::LaunchOptions::out_bf16); either may be NULL. */
+int kvb_launch_attention_ex2(const kvb_shape* s, const kvb_device_input* in, unsigned partitions,
+                             void* out_f16, void* out_bf16, float* scratch, float* m, float* l,
+                             float* n, void* stream);
+
 /* the two halves of kvb_launch_attention_ex (partial kernel; merge of the
  * leading `partitions` splits). *partitions_used may be NULL. */
 int kvb_launch_attention_partials(const kvb_shape* s, const kvb_device_input* in,
@@ -94,6 +100,10 @@ int kvb_launch_attention_partials(const kvb_shape* s, const kvb_device_input* in
                                   void* stream);
 int kvb_merge_attention_ex(const kvb_shape* s, const float* scratch, unsigned partitions,
                            float* m, float* l, float* n, void* out_f16, void* stream);
+/* kvb_merge_attention_ex with an optional bf16 output as well. */
+int kvb_merge_attention_ex2(const kvb_shape* s, const float* scratch, unsigned partitions,
+                            float* m, float* l, float* n, void* out_f16, void* out_bf16,
+                            void* stream);
 
 typedef struct kvb_batch_shape {
   uint32_t batch, q_heads, kv_heads, dim, page_tokens, pages, table_stride, max_tokens;
@@ -115,6 +125,10 @@ int kvb_batch_workspace_bytes(const kvb_batch_shape* s, size_t* bytes);
 int kvb_launch_attention_batched(const kvb_batch_shape* s, const kvb_batch_input* in,
                                  void* workspace, size_t workspace_bytes, float* m, float* l,
                                  float* n, void* out_f16, void* stream);
+/* kvb_launch_attention_batched with an optional bf16 output as well. */
+int kvb_launch_attention_batched2(const kvb_batch_shape* s, const kvb_batch_input* in,
+                                  void* workspace, size_t workspace_bytes, float* m, float* l,
+                                  float* n, void* out_f16, void* out_bf16, void* stream);
 /* paged KV append: quantise and write new K/V rows (kvbridge/attention_b200.h) */
 typedef struct kvb_append_shape {
   uint32_t tokens, kv_heads, dim, page_tokens, pages;
@@ -137,6 +151,15 @@ int kvb_merge_attention_shards(unsigned shards, unsigned row_heads, unsigned dim
                                const float* m_parts, const float* l_parts,
                                const float* n_parts, float* m, float* l, float* n,
                                void* out_f16, void* stream);
+/* kvb_merge_attention_shards with a shard stride (floats from one shard's m,
+ * l and n to the next shard's; 0 = the layout above) and an optional bf16
+ * output. A packed all-gather buffer [shard][m | l | n] is read with
+ * m_parts = buf, l_parts = buf + row_heads, n_parts = buf + 2 * row_heads and
+ * shard_stride = row_heads * (dim + 2). */
+int kvb_merge_attention_shards_ex(unsigned shards, unsigned row_heads, unsigned dim,
+                                  const float* m_parts, const float* l_parts,
+                                  const float* n_parts, size_t shard_stride, float* m, float* l,
+                                  float* n, void* out_f16, void* out_bf16, void* stream);
 /* Reads and clears the kernels' device status word (0 = ok). Returns the
  * cudaError_t of the read. */
 int kvb_read_device_status(int* status);
@@ -144,6 +167,21 @@ int kvb_read_device_status(int* status);
  * {code, block, warp, stage, waited ns, waited SM cycles}; all zero if none.
  * Reading clears it. Returns the cudaError_t of the read. */
 int kvb_read_wait_failure(long long* record6);
+/* Upper bound in ns of any single pipeline wait in kernels launched after
+ * the call (process-wide; 0 = the default 2 s). */
+void kvb_set_wait_limit_ns(unsigned long long ns);
+unsigned long long kvb_wait_limit_ns(void);
+
+/* Test hooks for the failure paths; thread-local and one-shot.
+ * kvb_debug_fail_launch: the nth kernel launch (1 = the next) this library
+ * makes on the calling thread is not made and the call that would make it
+ * returns KVB_ECUDA with cudaGetErrorString(cuda_error) in its message; 0
+ * disarms. kvb_debug_skip_stage: in the next tensor-core partial launch on
+ * the calling thread, the producer of CTA 0 leaves pipeline stage `stage`
+ * unarmed, so a consumer wait runs into the wait limit, status 1 is recorded
+ * (kvb_read_device_status, kvb_read_wait_failure) and the kernel returns. */
+int kvb_debug_fail_launch(unsigned nth, int cuda_error);
+int kvb_debug_skip_stage(unsigned stage);
 
 /* Decode call that allocates nothing. It has no counterpart in the
  * reference. kvb_launch_attention_ex needs a caller-provided scratch buffer

@@ -31,6 +31,12 @@ from .api import (  # noqa: F401
     merge_attention,
     merge_attention_ex,
     merge_attention_shards,
+    merge_attention_shards_ex,
+    set_wait_limit_ns,
+    wait_limit_ns,
+    debug_fail_launch,
+    debug_skip_stage,
+    launch_attention_noalloc,
     output_numerator_elements,
     output_scalar_elements,
     preload_attention_kernels,

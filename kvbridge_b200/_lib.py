@@ -164,6 +164,26 @@ SIGNATURES = {
             c_void_p,
         ],
     ),
+    "kvb_launch_attention_ex2": (
+        c_int,
+        [POINTER(KvbShape), POINTER(KvbDeviceInput), ctypes.c_uint] + [c_void_p] * 7,
+    ),
+    "kvb_merge_attention_ex2": (
+        c_int,
+        [POINTER(KvbShape), c_void_p, ctypes.c_uint] + [c_void_p] * 6,
+    ),
+    "kvb_launch_attention_batched2": (
+        c_int,
+        [POINTER(KvbBatchShape), POINTER(KvbBatchInput), c_void_p, c_size_t] + [c_void_p] * 6,
+    ),
+    "kvb_merge_attention_shards_ex": (
+        c_int,
+        [ctypes.c_uint, ctypes.c_uint, ctypes.c_uint, c_void_p, c_void_p, c_void_p, c_size_t] + [c_void_p] * 6,
+    ),
+    "kvb_set_wait_limit_ns": (None, [ctypes.c_ulonglong]),
+    "kvb_wait_limit_ns": (ctypes.c_ulonglong, []),
+    "kvb_debug_fail_launch": (c_int, [ctypes.c_uint, c_int]),
+    "kvb_debug_skip_stage": (c_int, [ctypes.c_uint]),
     "kvb_read_device_status": (c_int, [POINTER(c_int)]),
     "kvb_read_wait_failure": (c_int, [POINTER(ctypes.c_longlong)]),
     "kvb_schedule_cta_of": (c_uint32, [c_uint64, c_uint64, c_uint32]),

@@ -201,21 +201,20 @@ def attention_partitions(s: Shape, requested: int = 0) -> int:
 
 
 def launch_attention_ex(
-    s: Shape, inp: DeviceInput, scratch, m, l, n, partitions: int = 0, out_f16=None, stream=None
+    s: Shape, inp: DeviceInput, scratch, m, l, n, partitions: int = 0, out_f16=None, stream=None,
+    out_bf16=None,
 ) -> None:
-    check(
-        _lib.load().kvb_launch_attention_ex(
-            ctypes.byref(s.c()),
-            ctypes.byref(inp.c()),
-            partitions,
-            _ptr(out_f16),
-            _ptr(scratch),
-            _ptr(m),
-            _ptr(l),
-            _ptr(n),
-            _stream(stream),
-        )
-    )
+    """launch_attention with explicit partitions and optional normalised
+    outputs n / l in fp16 (``out_f16``) and/or bf16 (``out_bf16``)."""
+    if out_bf16 is None:
+        status = _lib.load().kvb_launch_attention_ex(
+            ctypes.byref(s.c()), ctypes.byref(inp.c()), partitions, _ptr(out_f16), _ptr(scratch),
+            _ptr(m), _ptr(l), _ptr(n), _stream(stream))
+    else:
+        status = _lib.load().kvb_launch_attention_ex2(
+            ctypes.byref(s.c()), ctypes.byref(inp.c()), partitions, _ptr(out_f16), _ptr(out_bf16),
+            _ptr(scratch), _ptr(m), _ptr(l), _ptr(n), _stream(stream))
+    check(status)
 
 
 def launch_attention_partials(s: Shape, inp: DeviceInput, scratch, partitions: int = 0, stream=None) -> int:
@@ -229,12 +228,17 @@ def launch_attention_partials(s: Shape, inp: DeviceInput, scratch, partitions: i
     return used.value
 
 
-def merge_attention_ex(s: Shape, scratch, partitions: int, m, l, n, out_f16=None, stream=None) -> None:
-    check(
-        _lib.load().kvb_merge_attention_ex(
-            ctypes.byref(s.c()), _ptr(scratch), partitions, _ptr(m), _ptr(l), _ptr(n), _ptr(out_f16), _stream(stream)
-        )
-    )
+def merge_attention_ex(s: Shape, scratch, partitions: int, m, l, n, out_f16=None, stream=None,
+                       out_bf16=None) -> None:
+    if out_bf16 is None:
+        status = _lib.load().kvb_merge_attention_ex(
+            ctypes.byref(s.c()), _ptr(scratch), partitions, _ptr(m), _ptr(l), _ptr(n), _ptr(out_f16),
+            _stream(stream))
+    else:
+        status = _lib.load().kvb_merge_attention_ex2(
+            ctypes.byref(s.c()), _ptr(scratch), partitions, _ptr(m), _ptr(l), _ptr(n), _ptr(out_f16),
+            _ptr(out_bf16), _stream(stream))
+    check(status)
 
 
 @dataclass
@@ -289,21 +293,18 @@ def batch_workspace_bytes(s: BatchShape) -> int:
 
 
 def launch_attention_batched(
-    s: BatchShape, inp: BatchInput, workspace, workspace_bytes: int, m, l, n, out_f16=None, stream=None
+    s: BatchShape, inp: BatchInput, workspace, workspace_bytes: int, m, l, n, out_f16=None, stream=None,
+    out_bf16=None,
 ) -> None:
-    check(
-        _lib.load().kvb_launch_attention_batched(
-            ctypes.byref(s.c()),
-            ctypes.byref(inp.c()),
-            _ptr(workspace),
-            workspace_bytes,
-            _ptr(m),
-            _ptr(l),
-            _ptr(n),
-            _ptr(out_f16),
-            _stream(stream),
-        )
-    )
+    if out_bf16 is None:
+        status = _lib.load().kvb_launch_attention_batched(
+            ctypes.byref(s.c()), ctypes.byref(inp.c()), _ptr(workspace), workspace_bytes, _ptr(m), _ptr(l),
+            _ptr(n), _ptr(out_f16), _stream(stream))
+    else:
+        status = _lib.load().kvb_launch_attention_batched2(
+            ctypes.byref(s.c()), ctypes.byref(inp.c()), _ptr(workspace), workspace_bytes, _ptr(m), _ptr(l),
+            _ptr(n), _ptr(out_f16), _ptr(out_bf16), _stream(stream))
+    check(status)
 
 
 def merge_attention_shards(
@@ -321,6 +322,54 @@ def merge_attention_shards(
             _ptr(l),
             _ptr(n),
             _ptr(out_f16),
+            _stream(stream),
+        )
+    )
+
+
+def merge_attention_shards_ex(
+    shards: int, row_heads: int, dim: int, m_parts, l_parts, n_parts, shard_stride: int, m, l, n,
+    out_f16=None, out_bf16=None, stream=None,
+) -> None:
+    """merge_attention_shards with a shard stride in floats (0 = separate
+    m/l/n arrays; row_heads * (dim + 2) = a packed [shard][m | l | n] buffer)
+    and an optional bf16 output."""
+    check(
+        _lib.load().kvb_merge_attention_shards_ex(
+            shards, row_heads, dim, _ptr(m_parts), _ptr(l_parts), _ptr(n_parts), shard_stride, _ptr(m), _ptr(l),
+            _ptr(n), _ptr(out_f16), _ptr(out_bf16), _stream(stream),
+        )
+    )
+
+
+def set_wait_limit_ns(ns: int) -> None:
+    """Bound of any single pipeline wait in later launches (0 = default 2 s)."""
+    _lib.load().kvb_set_wait_limit_ns(int(ns))
+
+
+def wait_limit_ns() -> int:
+    return int(_lib.load().kvb_wait_limit_ns())
+
+
+def debug_fail_launch(nth: int, cuda_error: int) -> None:
+    """Test hook: the nth kernel launch (1 = next) on this thread fails with
+    ``cuda_error`` instead of being made (0 disarms)."""
+    check(_lib.load().kvb_debug_fail_launch(nth, cuda_error))
+
+
+def debug_skip_stage(stage: int) -> None:
+    """Test hook: the next tensor-core partial launch on this thread leaves
+    pipeline stage ``stage`` of CTA 0 unarmed (a consumer wait runs out)."""
+    check(_lib.load().kvb_debug_skip_stage(stage))
+
+
+def launch_attention_noalloc(s: Shape, inp: DeviceInput, m, l, n, partitions: int = 0, out_f16=None,
+                             stream=None) -> None:
+    """The decode call that allocates nothing: split-K partials in the
+    library's static device array (see kvb_launch_attention_noalloc)."""
+    check(
+        _lib.load().kvb_launch_attention_noalloc(
+            ctypes.byref(s.c()), ctypes.byref(inp.c()), partitions, _ptr(m), _ptr(l), _ptr(n), _ptr(out_f16),
             _stream(stream),
         )
     )

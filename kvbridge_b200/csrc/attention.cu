@@ -63,8 +63,32 @@ struct FastVariant {
   void (*launch)(const kvb::DecodeParamsGather&, cudaStream_t) = nullptr;
 };
 
+// Failure-path test hooks (attention_b200.h, detail::fail_launch and
+// detail::skip_stage): thread-local, one-shot, off unless armed.
+thread_local unsigned t_fail_countdown = 0;
+thread_local cudaError_t t_fail_code = cudaSuccess;
+thread_local uint32_t t_skip_stage = 0xffffffffu;
+
+// The armed launch-failure hook's error for this launch (cudaSuccess when the
+// launch is to be made).
+cudaError_t injected_launch_failure() {
+  if (t_fail_countdown == 0 || --t_fail_countdown != 0) return cudaSuccess;
+  return t_fail_code;
+}
+
+// The skipped stage for the next partial launch (0xffffffff = none); reading
+// disarms the hook.
+uint32_t take_skip_stage() {
+  const uint32_t stage = t_skip_stage;
+  t_skip_stage = 0xffffffffu;
+  return stage;
+}
+
+std::atomic<unsigned long long> g_wait_limit_ns{kvb::kDefaultWaitLimitNs};
+
 void launch_pdl(const void* fn, dim3 grid, dim3 block, uint32_t smem, cudaStream_t stream,
                 void** args, const char* what) {
+  if (const cudaError_t injected = injected_launch_failure()) cuda_ok(injected, what);
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = grid;
   cfg.blockDim = block;
@@ -233,13 +257,15 @@ void launch_merge(int mode, const kvb::MergeParams& prm, cudaStream_t stream) {
 }
 
 kvb::MergeParams scratch_merge_params(const Shape& s, float* scratch, uint32_t np, uint32_t stride,
-                                      bool fill_empty, float* m, float* l, float* n, void* out) {
+                                      bool fill_empty, float* m, float* l, float* n, void* out,
+                                      void* out_bf16 = nullptr) {
   kvb::MergeParams mp{};
   mp.part = scratch;
   mp.m = m;
   mp.l = l;
   mp.n = n;
   mp.out = static_cast<__half*>(out);
+  mp.out_bf16 = static_cast<__nv_bfloat16*>(out_bf16);
   mp.row_heads = s.rows * s.q_heads;
   mp.dim = s.dim;
   mp.np = np;
@@ -446,6 +472,8 @@ kvb::DecodeParamsGather single_params(const Shape& s, const DeviceInput& in, uin
   prm.ctas = parts * s.kv_heads * plan.groups;
   prm.total_stages = uint64_t(prm.seg_stages) * s.kv_heads;
   prm.score_scale = s.scale;
+  prm.wait_limit_ns = wait_limit_ns();
+  prm.fault_stage = take_skip_stage();
   set_gather_maps(prm, s.dim, s.pages);
   return prm;
 }
@@ -469,15 +497,20 @@ unsigned launch_attention_partials(const Shape& s, const DeviceInput& in, unsign
 }
 
 void merge_attention_ex(const Shape& s, const float* scratch, unsigned partitions, float* m,
-                        float* l, float* n, void* out_f16, cudaStream_t stream) {
+                        float* l, float* n, void* out_f16, void* out_bf16, cudaStream_t stream) {
   detail::check_outputs(s, scratch, m, l, n);
   const uint32_t splits = split_count(s);
   if (partitions > splits)
     throw std::invalid_argument("merge partitions exceed split_count(shape)");
   launch_merge(kvb::kMergeScratch,
                scratch_merge_params(s, const_cast<float*>(scratch), partitions, splits,
-                                    partitions < splits, m, l, n, out_f16),
+                                    partitions < splits, m, l, n, out_f16, out_bf16),
                stream);
+}
+
+void merge_attention_ex(const Shape& s, const float* scratch, unsigned partitions, float* m,
+                        float* l, float* n, void* out_f16, cudaStream_t stream) {
+  merge_attention_ex(s, scratch, partitions, m, l, n, out_f16, nullptr, stream);
 }
 
 void launch_attention_ex(const Shape& s, const DeviceInput& in, const LaunchOptions& opt,
@@ -487,14 +520,17 @@ void launch_attention_ex(const Shape& s, const DeviceInput& in, const LaunchOpti
   if (!attention_b200_supported(s, in)) {
     launch_simt(s, in, scratch, splits, stream);
     launch_merge(kvb::kMergeScratch,
-                 scratch_merge_params(s, scratch, splits, splits, false, m, l, n, opt.out_f16),
+                 scratch_merge_params(s, scratch, splits, splits, false, m, l, n, opt.out_f16,
+                                      opt.out_bf16),
                  stream);
     return;
   }
   const uint32_t parts = launch_attention_partials(s, in, opt.partitions, scratch, stream);
   // The partial kernel has already marked splits [parts, splits) empty.
   launch_merge(kvb::kMergeScratch,
-               scratch_merge_params(s, scratch, parts, splits, false, m, l, n, opt.out_f16), stream);
+               scratch_merge_params(s, scratch, parts, splits, false, m, l, n, opt.out_f16,
+                                    opt.out_bf16),
+               stream);
 }
 
 void launch_attention(const Shape& s, const DeviceInput& in, float* scratch, float* m, float* l,
@@ -559,6 +595,12 @@ size_t batch_workspace_bytes(const BatchShape& s) {
 void launch_attention_batched(const BatchShape& s, const BatchInput& in, void* workspace,
                               size_t workspace_bytes, float* m, float* l, float* n, void* out_f16,
                               cudaStream_t stream) {
+  launch_attention_batched(s, in, workspace, workspace_bytes, m, l, n, out_f16, nullptr, stream);
+}
+
+void launch_attention_batched(const BatchShape& s, const BatchInput& in, void* workspace,
+                              size_t workspace_bytes, float* m, float* l, float* n, void* out_f16,
+                              void* out_bf16, cudaStream_t stream) {
   if (const char* e = batch_shape_error(s)) throw std::invalid_argument(e);
   if (!in.q || !in.seq_lens || !in.block_table || !in.k || !in.v || !in.k_scales ||
       !in.v_scales || !workspace || !m || !l || !n)
@@ -594,6 +636,8 @@ void launch_attention_batched(const BatchShape& s, const BatchInput& in, void* w
   prm.col_groups = 1;
   prm.group_cols = 8 * ((group + 7) / 8);
   prm.score_scale = s.scale;
+  prm.wait_limit_ns = wait_limit_ns();
+  prm.fault_stage = take_skip_stage();
   set_gather_maps(prm, s.dim, s.pages);
   v.launch(prm, stream);
 
@@ -603,6 +647,7 @@ void launch_attention_batched(const BatchShape& s, const BatchInput& in, void* w
   mp.l = l;
   mp.n = n;
   mp.out = static_cast<__half*>(out_f16);
+  mp.out_bf16 = static_cast<__nv_bfloat16*>(out_bf16);
   mp.row_heads = s.batch * s.q_heads;
   mp.dim = s.dim;
   mp.seq_lens = in.seq_lens;
@@ -615,13 +660,16 @@ void launch_attention_batched(const BatchShape& s, const BatchInput& in, void* w
   launch_merge(kvb::kMergeBatched, mp, stream);
 }
 
-void merge_attention_shards(unsigned shards, unsigned row_heads, unsigned dim,
-                            const float* m_parts, const float* l_parts, const float* n_parts,
-                            float* m, float* l, float* n, void* out_f16, cudaStream_t stream) {
+void merge_attention_shards_ex(unsigned shards, unsigned row_heads, unsigned dim,
+                               const float* m_parts, const float* l_parts, const float* n_parts,
+                               size_t shard_stride, float* m, float* l, float* n, void* out_f16,
+                               void* out_bf16, cudaStream_t stream) {
   if (shards == 0 || row_heads == 0 || dim == 0 || dim > 256)
     throw std::invalid_argument("shards, row_heads must be positive and dim in [1,256]");
   if (!m_parts || !l_parts || !n_parts || !m || !l || !n)
     throw std::invalid_argument("shard merge buffers must be non-null");
+  if (shard_stride != 0 && shard_stride < row_heads)
+    throw std::invalid_argument("shard_stride must be 0 or at least row_heads");
   kvb::MergeParams mp{};
   mp.m_parts = m_parts;
   mp.l_parts = l_parts;
@@ -630,10 +678,19 @@ void merge_attention_shards(unsigned shards, unsigned row_heads, unsigned dim,
   mp.l = l;
   mp.n = n;
   mp.out = static_cast<__half*>(out_f16);
+  mp.out_bf16 = static_cast<__nv_bfloat16*>(out_bf16);
   mp.row_heads = row_heads;
   mp.dim = dim;
   mp.np = shards;
+  mp.shard_stride = shard_stride;
   launch_merge(kvb::kMergeShards, mp, stream);
+}
+
+void merge_attention_shards(unsigned shards, unsigned row_heads, unsigned dim,
+                            const float* m_parts, const float* l_parts, const float* n_parts,
+                            float* m, float* l, float* n, void* out_f16, cudaStream_t stream) {
+  merge_attention_shards_ex(shards, row_heads, dim, m_parts, l_parts, n_parts, 0, m, l, n, out_f16,
+                            nullptr, stream);
 }
 
 // ---------------------------------------------------------------------------
@@ -675,6 +732,7 @@ void append_kv(const AppendShape& s, const AppendInput& in, cudaStream_t stream)
   prm.dim = s.dim;
   prm.page_tokens = s.page_tokens;
   prm.slots_total = uint64_t(s.pages) * s.page_tokens;
+  if (const cudaError_t injected = injected_launch_failure()) cuda_ok(injected, "append launch");
   kvb::append_kv_kernel<<<dim3(uint32_t(blocks)), dim3(32 * kvb::kAppendWarps), 0, stream>>>(prm);
   cuda_ok(cudaGetLastError(), "append launch");
 }
@@ -698,40 +756,90 @@ cudaError_t read_wait_failure(long long* record6) {
   return cudaMemcpyToSymbol(kvb::g_kvb_first_failure, zeros, sizeof(zeros));
 }
 
+void set_wait_limit_ns(unsigned long long ns) noexcept {
+  g_wait_limit_ns.store(ns == 0 ? kvb::kDefaultWaitLimitNs : ns);
+}
+
+unsigned long long wait_limit_ns() noexcept { return g_wait_limit_ns.load(); }
+
+namespace detail {
+
+void fail_launch(unsigned nth, cudaError_t code) noexcept {
+  t_fail_countdown = nth;
+  t_fail_code = code == cudaSuccess ? cudaErrorLaunchFailure : code;
+}
+
+void skip_stage(unsigned stage) noexcept { t_skip_stage = stage; }
+
+}  // namespace detail
+
 // ---------------------------------------------------------------------------
 // Decode call that allocates nothing (kvb_launch_attention_noalloc in
-// include/kvbridge_c.h). For callers that cannot obtain device memory at call
-// time - e.g. a serving loop whose every byte of HBM is pre-reserved by its
-// KV-cache allocator, or code running inside CUDA-graph stream capture, where
-// cudaMalloc is not permitted - the split-K partials live in this file-scope
-// device array instead of a caller-provided scratch buffer.
+// include/kvbridge_c.h). Some callers cannot call cudaMalloc when they
+// decode: an inference server whose memory pool reserved every byte of HBM
+// up front for its KV cache, or a host whose decode path must not allocate.
+// For them the split-K partials live in this file-scope device array instead
+// of a caller-provided scratch buffer.
 //
 // Every GPU that loads the library holds the array (2 MiB) until process
 // exit. All calls share it and it keeps the last call's contents; nothing in
 // it needs to start at zero, because the partial kernel of a call writes
 // every slot that call's merge reads. Calls that may run concurrently on the
-// GPU (different streams, or graphs replayed in parallel) race on the array
-// and must be serialised by the caller.
+// GPU (different streams) race on the array and must be serialised by the
+// caller.
 
 namespace {
 
 constexpr size_t kNoAllocScratchFloats = size_t(1) << 19;  // 2 MiB
 static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchFloats];
 
-// Device address of g_noalloc_scratch on the current device. In host code the
-// array's name is only a host-side stand-in, so the address is looked up with
-// cudaGetSymbolAddress once per device, with that device current, and cached.
-float* noalloc_scratch_on_current_device() {
+// Unique ID of the calling thread's current CUDA context (0 when there is
+// none, or when the driver does not offer cuCtxGetId). IDs are never reused
+// in a process, so the context that replaces a destroyed one (after
+// cudaDeviceReset) has a new ID even if its handle value is reused.
+unsigned long long current_context_id() {
+  using GetCurrent = CUresult (*)(CUcontext*);
+  using GetId = CUresult (*)(CUcontext, unsigned long long*);
+  static const std::pair<GetCurrent, GetId> fns = [] {
+    void* cur = nullptr;
+    void* id = nullptr;
+    cudaDriverEntryPointQueryResult found{};
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &cur, cudaEnableDefault, &found) != cudaSuccess ||
+        found != cudaDriverEntryPointSuccess)
+      cur = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &id, cudaEnableDefault, &found) != cudaSuccess ||
+        found != cudaDriverEntryPointSuccess)
+      id = nullptr;
+    return std::make_pair(reinterpret_cast<GetCurrent>(cur), reinterpret_cast<GetId>(id));
+  }();
+  if (fns.first == nullptr || fns.second == nullptr) return 0;
+  CUcontext ctx = nullptr;
+  if (fns.first(&ctx) != CUDA_SUCCESS || ctx == nullptr) return 0;
+  unsigned long long id = 0;
+  if (fns.second(ctx, &id) != CUDA_SUCCESS) return 0;
+  return id;
+}
+
+// Device address of g_noalloc_scratch in the current context. In host code
+// the array's name is only a host-side stand-in, so the address is looked up
+// with cudaGetSymbolAddress (with the device current) once per CUDA context
+// and cached under the context's unique ID; a context created after
+// cudaDeviceReset gets a fresh lookup. The first call in a context does the
+// lookup, so it should come before any stream capture.
+float* noalloc_scratch_in_current_context() {
   static std::mutex mu;
-  static std::map<int, float*> cache;
-  int dev = 0;
-  cuda_ok(cudaGetDevice(&dev), "cudaGetDevice");
+  static std::map<unsigned long long, float*> cache;
   std::lock_guard<std::mutex> lock(mu);
-  auto it = cache.find(dev);
-  if (it != cache.end()) return it->second;
+  const unsigned long long before = current_context_id();
+  if (before != 0) {
+    auto it = cache.find(before);
+    if (it != cache.end()) return it->second;
+  }
   void* ptr = nullptr;
   cuda_ok(cudaGetSymbolAddress(&ptr, g_noalloc_scratch), "cudaGetSymbolAddress(static scratch)");
-  cache.emplace(dev, static_cast<float*>(ptr));
+  // The lookup makes the device's primary context current if none was.
+  const unsigned long long id = current_context_id();
+  if (id != 0) cache[id] = static_cast<float*>(ptr);
   return static_cast<float*>(ptr);
 }
 
@@ -756,10 +864,12 @@ void launch_attention_noalloc(const Shape& s, const DeviceInput& in, unsigned pa
         "no-allocation call");
   uint32_t parts = attention_partitions(s, partitions);
   parts = uint32_t(std::min<size_t>(parts, fit));
-  float* scratch = noalloc_scratch_on_current_device();
+  float* scratch = noalloc_scratch_in_current_context();
   if (parts > 0) {
-    // Partials packed [row-head][partition]: split stride = parts.
-    const kvb::DecodeParamsGather prm = single_params(s, in, parts, scratch, parts);
+    // Partials packed [row-head][partition]: split stride = parts. Same
+    // launch as launch_attention_partials, L2 prefetch included.
+    kvb::DecodeParamsGather prm = single_params(s, in, parts, scratch, parts);
+    prm.prefetch_stages = kPrefetchStages;
     fast_variant(s.dim, prm.group_cols / 8, s.page_tokens, false).launch(prm, stream);
   }
   launch_merge(kvb::kMergeScratch,

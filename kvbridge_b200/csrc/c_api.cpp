@@ -191,6 +191,17 @@ int kvb_launch_attention_ex(const kvb_shape* s, const kvb_device_input* in, unsi
   });
 }
 
+int kvb_launch_attention_ex2(const kvb_shape* s, const kvb_device_input* in, unsigned partitions,
+                             void* out_f16, void* out_bf16, float* scratch, float* m, float* l,
+                             float* n, void* stream) {
+  return guarded([&] {
+    kvbridge::LaunchOptions opt{partitions, out_f16};
+    opt.out_bf16 = out_bf16;
+    kvbridge::launch_attention_ex(to_shape(s), to_input(in), opt, scratch, m, l, n,
+                                  as_stream(stream));
+  });
+}
+
 int kvb_launch_attention_partials(const kvb_shape* s, const kvb_device_input* in,
                                   unsigned partitions, float* scratch, unsigned* partitions_used,
                                   void* stream) {
@@ -205,6 +216,15 @@ int kvb_merge_attention_ex(const kvb_shape* s, const float* scratch, unsigned pa
                            float* l, float* n, void* out_f16, void* stream) {
   return guarded([&] {
     kvbridge::merge_attention_ex(to_shape(s), scratch, partitions, m, l, n, out_f16,
+                                 as_stream(stream));
+  });
+}
+
+int kvb_merge_attention_ex2(const kvb_shape* s, const float* scratch, unsigned partitions,
+                            float* m, float* l, float* n, void* out_f16, void* out_bf16,
+                            void* stream) {
+  return guarded([&] {
+    kvbridge::merge_attention_ex(to_shape(s), scratch, partitions, m, l, n, out_f16, out_bf16,
                                  as_stream(stream));
   });
 }
@@ -228,6 +248,16 @@ int kvb_launch_attention_batched(const kvb_batch_shape* s, const kvb_batch_input
   return guarded([&] {
     kvbridge::launch_attention_batched(to_batch_shape(s), to_batch_input(in), workspace,
                                        workspace_bytes, m, l, n, out_f16, as_stream(stream));
+  });
+}
+
+int kvb_launch_attention_batched2(const kvb_batch_shape* s, const kvb_batch_input* in,
+                                  void* workspace, size_t workspace_bytes, float* m, float* l,
+                                  float* n, void* out_f16, void* out_bf16, void* stream) {
+  return guarded([&] {
+    kvbridge::launch_attention_batched(to_batch_shape(s), to_batch_input(in), workspace,
+                                       workspace_bytes, m, l, n, out_f16, out_bf16,
+                                       as_stream(stream));
   });
 }
 
@@ -258,7 +288,32 @@ int kvb_merge_attention_shards(unsigned shards, unsigned row_heads, unsigned dim
   });
 }
 
+int kvb_merge_attention_shards_ex(unsigned shards, unsigned row_heads, unsigned dim,
+                                  const float* m_parts, const float* l_parts,
+                                  const float* n_parts, size_t shard_stride, float* m, float* l,
+                                  float* n, void* out_f16, void* out_bf16, void* stream) {
+  return guarded([&] {
+    kvbridge::merge_attention_shards_ex(shards, row_heads, dim, m_parts, l_parts, n_parts,
+                                        shard_stride, m, l, n, out_f16, out_bf16,
+                                        as_stream(stream));
+  });
+}
+
 int kvb_read_device_status(int* status) { return int(kvbridge::read_device_status(status)); }
+
+void kvb_set_wait_limit_ns(unsigned long long ns) { kvbridge::set_wait_limit_ns(ns); }
+
+unsigned long long kvb_wait_limit_ns(void) { return kvbridge::wait_limit_ns(); }
+
+int kvb_debug_fail_launch(unsigned nth, int cuda_error) {
+  kvbridge::detail::fail_launch(nth, static_cast<cudaError_t>(cuda_error));
+  return KVB_OK;
+}
+
+int kvb_debug_skip_stage(unsigned stage) {
+  kvbridge::detail::skip_stage(stage);
+  return KVB_OK;
+}
 
 int kvb_read_wait_failure(long long* record6) { return int(kvbridge::read_wait_failure(record6)); }
 

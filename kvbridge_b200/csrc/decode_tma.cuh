@@ -77,6 +77,14 @@ struct DecodeParams {
   // group c % col_groups, so the CTAs of one KV range and different groups
   // run side by side and share its pages in L2. Batched: 1 and 8 * NT.
   uint32_t col_groups, group_cols;
+  // Upper bound of every pipeline wait of the launch (kDefaultWaitLimitNs
+  // unless the host set another).
+  unsigned long long wait_limit_ns;
+  // Test hook for the bounded waits: the producer of CTA 0 neither arms nor
+  // loads its stage number `fault_stage` (0xffffffff = off), so the consumer
+  // of that stage waits until wait_limit_ns, records the failure and the CTA
+  // returns. No memory access depends on it.
+  uint32_t fault_stage;
 };
 
 // Parameters of the small-page kernels. 16-token pages at dim <= 128
@@ -347,13 +355,14 @@ __device__ void prefetch_query_lines(const DecodeParams& p, const Piece& pc) {
 // Drain: every copy the producer issued (stages 0..g-1) must land before the
 // CTA can exit; only the last STAGES of them can still be in flight.
 template <int STAGES>
-__device__ __forceinline__ void drain_copies(uint64_t* full, uint32_t g) {
+__device__ __forceinline__ void drain_copies(uint64_t* full, uint32_t g,
+                                             unsigned long long limit_ns) {
   const uint32_t first = g > STAGES ? g - STAGES : 0u;
   for (uint32_t s = first; s < g; ++s) {
     // Copies land whatever the consumers do, so this wait ignores an abort.
     volatile int no_abort = 0;
     if (mbar_wait_bounded(&full[s % STAGES], (s / STAGES) & 1u, &no_abort, kStatusDrainTimeout,
-                          int(s)) != kWaitOk)
+                          int(s), limit_ns) != kWaitOk)
       break;
   }
 }
@@ -447,8 +456,16 @@ __device__ void produce_small_pages(const DecodeParamsGather& p, const Piece& on
       const int32_t unit32 = int32_t(uint32_t(ok ? t : 0u) * p.kv_heads + pc.h);
       const uint32_t slot = g % STAGES;
       if (mbar_wait_bounded(&empty[slot], ((g / STAGES) & 1u) ^ 1u, abort_flag,
-                            kStatusEmptyWaitTimeout, int(g)) != kWaitOk)
+                            kStatusEmptyWaitTimeout, int(g), p.wait_limit_ns) != kWaitOk)
         return false;
+      if (g == p.fault_stage && blockIdx.x == 0) {
+        // Test hook: the stage is never published (no tag) and loads nothing;
+        // its barrier phase completes with zero bytes so that the ring, and
+        // the drain at exit, stay in step.
+        if (lane == 0) mbar_arrive_expect_tx(&full[slot], 0u);
+        ++g;
+        return true;
+      }
       uint8_t* st = ring + size_t(slot) * StageLayout<D>::kBytes;
       *reinterpret_cast<float4*>(st + scale_off + tok4 * 4u) = sc;
       // The warp's scale stores come before lane 0's arrive (release).
@@ -503,7 +520,7 @@ __device__ void produce_small_pages(const DecodeParamsGather& p, const Piece& on
     x = piece_end_stage(p, pc, x);
   }
   if (!BATCHED && !failed) mark_empty_splits<D>(p, only);
-  drain_copies<STAGES>(full, g);
+  drain_copies<STAGES>(full, g, p.wait_limit_ns);
 }
 
 template <int D, int STAGES, bool BATCHED>
@@ -582,9 +599,17 @@ __device__ void produce(const DecodeParams& p, const Piece& only, uint8_t* ring,
         const uint32_t slot = g % STAGES;
         const uint32_t use = g / STAGES;
         if (mbar_wait_bounded(&empty[slot], (use & 1u) ^ 1u, abort_flag, kStatusEmptyWaitTimeout,
-                              int(g)) != kWaitOk) {
+                              int(g), p.wait_limit_ns) != kWaitOk) {
           failed = true;
           break;
+        }
+        if (g == p.fault_stage && blockIdx.x == 0) {
+          // Test hook: the stage is never published (no tag) and loads
+          // nothing; its barrier phase completes with zero bytes so that the
+          // ring, and the drain at exit, stay in step.
+          if (lane == 0) mbar_arrive_expect_tx(&full[slot], 0u);
+          ++g;
+          continue;
         }
         if (lane == 0) {
           // The slot is free, so its full barrier has completed the phase of
@@ -604,7 +629,7 @@ __device__ void produce(const DecodeParams& p, const Piece& only, uint8_t* ring,
     x = piece_end_stage(p, pc, x);
   }
   if (!BATCHED && !failed) mark_empty_splits<D>(p, only);
-  drain_copies<STAGES>(full, g);
+  drain_copies<STAGES>(full, g, p.wait_limit_ns);
 }
 
 // ---------------------------------------------------------------------------
@@ -1051,9 +1076,10 @@ __device__ __forceinline__ void decode_partial_body(const KernelParams<SMALL_PAG
       // would mistake that phase for this one. Wait for the producer to tag
       // the slot with g first; from then on the barrier is in the phase of
       // stage g or past it, and the parity test is exact.
-      if (wait_tag_bounded(&tags[slot], g, abort_flag, kStatusFullWaitTimeout, int(g)) == kWaitOk)
+      if (wait_tag_bounded(&tags[slot], g, abort_flag, kStatusFullWaitTimeout, int(g),
+                           p.wait_limit_ns) == kWaitOk)
         mbar_wait_bounded(&full[slot], (g / STAGES) & 1u, abort_flag, kStatusFullWaitTimeout,
-                          int(g));
+                          int(g), p.wait_limit_ns);
       const uint32_t tb = (first_stage + pc.j0 + i) * kStageTokens;
       consume_stage<D, NT, SMALL_PAGES>(p, ring + size_t(slot) * StageLayout<D>::kBytes, tb, pc.lo, pc.hi,
                            all_visible, qf, ws);

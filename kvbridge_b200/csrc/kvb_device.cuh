@@ -1,8 +1,8 @@
 #pragma once
 // sm_100a device helpers for the decode-attention kernels: mbarrier
-// pipelines, bulk (TMA) global->shared copies, warp-level f16 tensor-core
-// MMA, fragment transposition and bounded waits. Everything is inline PTX of
-// documented instructions; nothing here restates a CUDA math-library routine.
+// pipelines, bulk (TMA) global->shared copies, the warp-level int8 tensor-core
+// MMA, L2 prefetch and bounded waits. Everything is inline PTX of documented
+// instructions; nothing here restates a CUDA math-library routine.
 #include <cuda_runtime.h>
 #include <cuda_fp16.h>
 #include <cstdint>
@@ -39,10 +39,10 @@ __device__ __forceinline__ void record_wait_failure(int code, int stage, long lo
   atomicMax(&g_kvb_status, code);
 }
 
-// Upper bound of any single pipeline wait. A correct pipeline never waits
-// more than a few microseconds; the bound only keeps a broken one from
-// holding the GPU.
-constexpr unsigned long long kWaitLimitNs = 2000000000ull;
+// Default upper bound of any single pipeline wait (the kernels take the bound
+// as a launch parameter). A correct pipeline never waits more than a few
+// microseconds; the bound only keeps a broken one from holding the GPU.
+constexpr unsigned long long kDefaultWaitLimitNs = 2000000000ull;
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -87,12 +87,13 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 
 enum WaitResult : int { kWaitOk = 0, kWaitTimeout = 1, kWaitAborted = 2 };
 
-// Wait for phase `parity` of `bar` to complete, giving up after kWaitLimitNs.
+// Wait for phase `parity` of `bar` to complete, giving up after `limit_ns`.
 // `abort_flag` (shared memory) ends every later wait of the CTA once one wait
 // has timed out. A timeout is recorded (first failure wins) with `code` and
 // `stage`; an abort is not, so the record names the wait that gave up first.
 __device__ __forceinline__ int mbar_wait_bounded(uint64_t* bar, uint32_t parity,
-                                                 volatile int* abort_flag, int code, int stage) {
+                                                 volatile int* abort_flag, int code, int stage,
+                                                 unsigned long long limit_ns) {
   if (mbar_try_wait(bar, parity)) return kWaitOk;
   const unsigned long long start = global_ns();
   const long long start_cycles = clock64();
@@ -101,7 +102,7 @@ __device__ __forceinline__ int mbar_wait_bounded(uint64_t* bar, uint32_t parity,
     if ((spin & 255u) == 0) {
       if (*abort_flag) return kWaitAborted;
       const unsigned long long waited = global_ns() - start;
-      if (waited > kWaitLimitNs) {
+      if (waited > limit_ns) {
         *abort_flag = 1;
         record_wait_failure(code, stage, static_cast<long long>(waited), clock64() - start_cycles);
         return kWaitTimeout;
@@ -113,7 +114,8 @@ __device__ __forceinline__ int mbar_wait_bounded(uint64_t* bar, uint32_t parity,
 // Wait until the shared word `*tag` equals `value` (bounded like
 // mbar_wait_bounded; same codes and abort behaviour).
 __device__ __forceinline__ int wait_tag_bounded(const volatile uint32_t* tag, uint32_t value,
-                                                volatile int* abort_flag, int code, int stage) {
+                                                volatile int* abort_flag, int code, int stage,
+                                                unsigned long long limit_ns) {
   if (*tag == value) return kWaitOk;
   const unsigned long long start = global_ns();
   const long long start_cycles = clock64();
@@ -122,7 +124,7 @@ __device__ __forceinline__ int wait_tag_bounded(const volatile uint32_t* tag, ui
     if ((spin & 255u) == 0) {
       if (*abort_flag) return kWaitAborted;
       const unsigned long long waited = global_ns() - start;
-      if (waited > kWaitLimitNs) {
+      if (waited > limit_ns) {
         *abort_flag = 1;
         record_wait_failure(code, stage, static_cast<long long>(waited), clock64() - start_cycles);
         return kWaitTimeout;
@@ -183,28 +185,9 @@ __device__ __forceinline__ void grid_launch_dependents() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
-// Warpgroup register reallocation (all four warps of a warpgroup execute it).
-template <int N>
-__device__ __forceinline__ void warpgroup_reg_release() {
-  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
-}
-template <int N>
-__device__ __forceinline__ void warpgroup_reg_acquire() {
-  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
-}
-
 // Named barrier over `threads` threads (multiple of 32), id 1..15.
 __device__ __forceinline__ void named_barrier(uint32_t id, uint32_t threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
-}
-
-// D += A * B for one m16n8k16 tile, f16 operands, f32 accumulators.
-__device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
-                                          uint32_t a3, uint32_t b0, uint32_t b1) {
-  asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
-      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
 // D += A * B for one m16n8k32 tile, s8 operands, exact s32 accumulators.
@@ -216,46 +199,11 @@ __device__ __forceinline__ void imma_16832(int (&d)[4], uint32_t a0, uint32_t a1
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-// D += A * B for one m16n8k32 tile, s8 A and u8 B, exact s32 accumulators.
-__device__ __forceinline__ void imma_16832_s8u8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
-                                                uint32_t a3, uint32_t b0, uint32_t b1) {
-  asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.u8.s32 "
-      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
-      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
-      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
-
-// Transpose an 8x8 b16 matrix held one row-pair per lane (lane holds row
-// lane/4, columns 2*(lane%4) and +1) into the same fragment of its transpose.
-__device__ __forceinline__ uint32_t transpose_8x8_b16(uint32_t x) {
-  uint32_t y;
-  asm("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
-  return y;
-}
-
 // 2^x on the MUFU unit (ex2.approx, denormal results flushed to zero).
 __device__ __forceinline__ float fast_exp2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
-}
-
-// Exact int8 -> f16 widening of four packed codes. Biasing each byte by 128
-// gives an unsigned u in [0,255]; the f16 bit pattern 0x6400|u is 1024+u
-// exactly, and subtracting 1152 (0x6480) leaves the signed code. Returns the
-// f16x2 pairs (byte0, byte1) in `lo` and (byte2, byte3) in `hi`, lower byte
-// in the lower half.
-__device__ __forceinline__ void int8x4_to_f16x4(uint32_t packed, uint32_t& lo, uint32_t& hi) {
-  const uint32_t biased = packed ^ 0x80808080u;
-  const uint32_t l = __byte_perm(biased, 0x64646464u, 0x4140u);
-  const uint32_t h = __byte_perm(biased, 0x64646464u, 0x4342u);
-  asm("sub.f16x2 %0, %1, %2;" : "=r"(lo) : "r"(l), "r"(0x64806480u));
-  asm("sub.f16x2 %0, %1, %2;" : "=r"(hi) : "r"(h), "r"(0x64806480u));
-}
-
-__device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
-  const __half2 h = __floats2half2_rn(lo, hi);
-  return *reinterpret_cast<const uint32_t*>(&h);
 }
 
 __device__ __forceinline__ float warp_max(float x) {

@@ -4,12 +4,15 @@
 //   M = max over partials with l_p > 0 of m_p
 //   L = sum_p exp(m_p - M) * l_p,   N[d] = sum_p exp(m_p - M) * n_p[d]
 // with m = -inf, l = 0, n = 0 when no partial has l_p > 0. The optional
-// fp16 epilogue writes out = N / L (0 for empty rows).
+// fp16 and bf16 epilogues write out = N / L (0 for empty rows), rounded to
+// nearest even.
 //
 // The same kernel serves three partial layouts:
 //   kScratch - the reference scratch layout [rh][split][dim+2]
 //   kBatched - the batched workspace [piece][qrow][dim+2] (kvb_schedule.h)
 //   kShards  - shard-major m/l/n triples from several GPUs
+#include <cuda_bf16.h>
+
 #include "kvb_device.cuh"
 #include "kvb_schedule.h"
 
@@ -26,10 +29,15 @@ struct MergeParams {
   float* l;
   float* n;
   __half* out;
+  __nv_bfloat16* out_bf16;
   uint32_t row_heads, dim;
   uint32_t np;            // kScratch: partials per row-head; kShards: shards
   uint32_t split_stride;  // kScratch: S of the layout
   uint32_t fill_empty;    // kScratch: write empty partials into splits [np, S)
+  // kShards: floats from one shard's m (l, n) to the next shard's; 0 = the
+  // separate arrays [shard][row_head] and [shard][row_head][dim]. A packed
+  // exchange buffer [shard][m | l | n] uses row_heads * (dim + 2).
+  uint64_t shard_stride;
   // kBatched
   const uint32_t* seq_lens;
   uint32_t batch, q_heads, kv_heads, group, max_tokens, ctas;
@@ -101,8 +109,8 @@ __global__ void __launch_bounds__(32 * kMergeWarps, 6) merge_kernel(MergeParams 
     mb = p.m_parts + rh;
     lb = p.l_parts + rh;
     nb = p.n_parts + size_t(rh) * D;
-    ms = ls = p.row_heads;
-    ns = size_t(p.row_heads) * D;
+    ms = ls = p.shard_stride ? p.shard_stride : p.row_heads;
+    ns = p.shard_stride ? p.shard_stride : size_t(p.row_heads) * D;
   } else {
     const uint32_t b = rh / p.q_heads, hq = rh % p.q_heads;
     const uint32_t h = hq / p.group, g = hq % p.group;
@@ -194,6 +202,7 @@ __global__ void __launch_bounds__(32 * kMergeWarps, 6) merge_kernel(MergeParams 
     v = L > 0.f ? v : 0.f;
     p.n[size_t(rh) * D + d] = v;
     if (p.out != nullptr) p.out[size_t(rh) * D + d] = __float2half_rn(v * inv);
+    if (p.out_bf16 != nullptr) p.out_bf16[size_t(rh) * D + d] = __float2bfloat16_rn(v * inv);
   }
   if (MODE == kMergeScratch && p.fill_empty) {
     float* row = p.part + size_t(rh) * p.split_stride * (D + 2);

@@ -71,6 +71,29 @@ def all_gather_partials(m, l, n, group=None):
     return tuple(out)
 
 
+def all_gather_packed(buf, group=None):
+    """One all-gather of every rank's packed partial buffer [m | l | n]:
+    returns [G, buf.numel()], rank-major. On GPU this is a single NCCL
+    collective; merge_attention_shards_ex reads the result in place with
+    shard_stride = buf.numel()."""
+    import torch
+    import torch.distributed as dist
+
+    world = dist.get_world_size(group)
+    flat = buf.contiguous().view(-1)
+    out = torch.empty((world, flat.numel()), dtype=flat.dtype, device=flat.device)
+    if flat.device.type == "cuda":
+        dist.all_gather_into_tensor(out, flat, group=group)
+    else:
+        dist.all_gather(list(out.unbind(0)), flat, group=group)
+    return out
+
+
+def packed_views(buf, row_heads: int, dim: int):
+    """(m, l, n) views of a packed partial buffer [m (rh) | l (rh) | n (rh*dim)]."""
+    return buf[:row_heads], buf[row_heads:2 * row_heads], buf[2 * row_heads:2 * row_heads + row_heads * dim]
+
+
 def sequence_sharded_decode(
     local_partial: Callable[[], Tuple["object", "object", "object"]],
     merge: Callable[["object", "object", "object"], "object"],
@@ -84,6 +107,28 @@ def sequence_sharded_decode(
     m, l, n = local_partial()
     mp, lp, np_ = exchange(m, l, n, group)
     return merge(mp, lp, np_)
+
+
+def gpu_packed_shard_merge(rh: int, dim: int, device, out_f16: bool = True):
+    """merge() of the packed exchange: gathered [G, rh * (dim + 2)] from
+    all_gather_packed is merged in place (merge_attention_shards_ex with
+    shard_stride = rh * (dim + 2)) into preallocated outputs."""
+    import torch
+
+    from . import api
+
+    m = torch.empty(rh, device=device)
+    l = torch.empty(rh, device=device)
+    n = torch.empty(rh * dim, device=device)
+    out = torch.empty(rh * dim, dtype=torch.float16, device=device) if out_f16 else None
+
+    def merge(gathered):
+        shards = gathered.shape[0]
+        api.merge_attention_shards_ex(shards, rh, dim, gathered, gathered[:, rh:], gathered[:, 2 * rh:],
+                                      rh * (dim + 2), m, l, n, out_f16=out)
+        return m, l, n, out
+
+    return merge
 
 
 def gpu_shard_merge(rh: int, dim: int, out_f16: bool = True):

@@ -20,6 +20,7 @@ import this package, and only as the checker; the product path never calls it.
 from __future__ import annotations
 
 import ctypes
+import os
 import subprocess
 from ctypes import POINTER, c_char_p, c_double, c_float, c_int, c_int32, c_uint8, c_uint32, c_uint64, c_void_p
 from pathlib import Path
@@ -28,6 +29,10 @@ from typing import Optional
 import numpy as np
 
 HERE = Path(__file__).resolve().parent
+# The reference checkout the checkers are built from: $KVB_REFERENCE_DIR when
+# set, else a directory named `reference` beside this repository. Only build
+# steps read it; nothing at test or bench time does.
+REFERENCE_DIR = Path(os.environ.get("KVB_REFERENCE_DIR") or (HERE.parent.parent / "reference"))
 ORACLE_LIB = HERE / "libkvb_oracle.so"
 REF_ORACLE_LIB = HERE / "_ref" / "libkvbref_oracle.so"
 REF_CUDA_LIB = HERE / "_ref" / "libkvbref_cuda.so"
@@ -63,7 +68,7 @@ _oracle = None
 def build(ref: bool = False) -> None:
     """Run oracle/Makefile (the C oracle; with ``ref`` also oracle/_ref)."""
     target = "all" if ref else "oracle"
-    subprocess.run(["make", "-s", "-C", str(HERE), target], check=True)
+    subprocess.run(["make", "-s", "-C", str(HERE), target, f"REF={REFERENCE_DIR}"], check=True)
 
 
 def _load_oracle():

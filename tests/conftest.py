@@ -37,7 +37,7 @@ def kvb_lib():
 def oracle_lib():
     import oracle
 
-    oracle.build(ref=Path("/root/reference").exists() and not oracle.REF_ORACLE_LIB.exists())
+    oracle.build(ref=oracle.REFERENCE_DIR.exists() and not oracle.REF_ORACLE_LIB.exists())
     return oracle
 
 

@@ -7,6 +7,7 @@ import torch
 
 import kvbridge_b200 as kvb
 from kvbridge_b200 import synth
+from kvbridge_b200.api import Shape
 
 # Acceptance tolerances of this path against the FP64 oracle: max-abs 2e-3
 # and rel-L2 1e-3. They apply as stated to the fp32 n/l the kernels compute.
@@ -93,4 +94,81 @@ def check_against_oracle(res, shape, ref, label=""):
         ma16 = float(excess.max()) if excess.size else 0.0
         _, rl16 = errors(out, expect)
         assert ma16 <= MAX_ABS and rl16 <= REL_L2, f"{label}: fp16 out max_abs-halfulp={ma16:.3e} rel_l2={rl16:.3e}"
+    return ma, rl
+
+
+def report(label: str, **values) -> None:
+    """Records an achieved-error line: printed, and appended as JSON to the
+    file named by $KVB_PARITY_REPORT when that is set."""
+    import json
+    import os
+
+    line = {"case": label, **{k: (float(v) if isinstance(v, (int, float, np.floating)) else v)
+                              for k, v in values.items()}}
+    print(f"[parity] {json.dumps(line)}")
+    path = os.environ.get("KVB_PARITY_REPORT")
+    if path:
+        with open(path, "a") as fh:
+            fh.write(json.dumps(line) + "\n")
+
+
+def host_pool(bc):
+    """The batched case's K/V pool and scales as numpy arrays (copied once)."""
+    return tuple(getattr(bc, f).cpu().numpy() for f in ("k", "v", "k_scales", "v_scales"))
+
+
+def check_batched(bc, m, l, n, out=None, label="batched", threads=None, out_bf16=None, pool=None):
+    """Every sequence of a batched call against the FP64 oracle (n/l, m, l,
+    the fp16 output and optionally the bf16 output). Returns the worst
+    (max_abs, rel_l2) of n/l over the batch."""
+    import os
+
+    import oracle
+
+    threads = threads or os.cpu_count() or 8
+    k, v, ks, vs = pool if pool is not None else host_pool(bc)
+    s = bc.shape
+    H, D, P = s.q_heads, s.dim, s.page_tokens
+    m, l, n = m.cpu(), l.cpu(), n.cpu()
+    out = out.cpu() if out is not None else None
+    out_bf16 = out_bf16.cpu() if out_bf16 is not None else None
+    table_all = bc.block_table.cpu()
+    q_all = bc.q.cpu()
+    worst = (0.0, 0.0)
+    for b, length in enumerate(bc.lens):
+        sl = slice(b * H, (b + 1) * H)
+        if length == 0:
+            assert torch.all(l[sl] == 0) and torch.all(torch.isneginf(m[sl])), f"{label}: seq {b} not empty"
+            continue
+        npg = (length + P - 1) // P
+        table = torch.zeros(s.pages, dtype=torch.int64)
+        table[:npg] = table_all[b, :npg].to(torch.int64)
+        shape = Shape(1, H, s.kv_heads, D, P, s.pages, length, 0, length, s.scale, True)
+        ref = oracle.reference(shape, q_all[b], torch.tensor([length - 1]), torch.arange(length), table,
+                               k, v, ks, vs, threads=threads)
+        res = {"m": m[sl], "l": l[sl], "n": n[b * H * D:(b + 1) * H * D]}
+        if out is not None:
+            res["out"] = out[b * H * D:(b + 1) * H * D]
+        ma, rl = check_against_oracle(res, shape, ref, f"{label} seq {b}")
+        if out_bf16 is not None:
+            check_bf16(out_bf16[b * H * D:(b + 1) * H * D], shape, ref, f"{label} seq {b} bf16")
+        worst = (max(worst[0], ma), max(worst[1], rl))
+    return worst
+
+
+def check_bf16(out_bf16, shape, ref, label=""):
+    """bf16 output n/l against the oracle: max-abs 2e-3 beyond half a bf16
+    ulp of the value (bf16 keeps 8 significant bits), rel-L2 within 1e-3 plus
+    the bf16 rounding (2^-9 relative)."""
+    got = out_bf16.float().double().numpy().reshape(shape.rows, shape.q_heads, shape.dim)
+    expect = ref["normalized"]
+    mag = np.abs(expect)
+    # half an ulp of bf16 at |x|: 2^(floor(log2|x|) - 8)
+    with np.errstate(divide="ignore"):
+        e = np.floor(np.log2(np.where(mag > 0, mag, 1.0)))
+    half_ulp = np.where(mag > 0, np.exp2(e - 8), 0.0)
+    excess = np.abs(got - expect) - half_ulp
+    ma = float(excess.max()) if excess.size else 0.0
+    _, rl = errors(got, expect)
+    assert ma <= MAX_ABS and rl <= REL_L2 + 2.0 ** -9, f"{label}: bf16 max_abs-halfulp={ma:.3e} rel_l2={rl:.3e}"
     return ma, rl

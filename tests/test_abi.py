@@ -53,7 +53,8 @@ def test_every_cpp_entry_point_is_exported(kvb_lib):
     for expected in ("launch_attention", "launch_attention_mma", "merge_attention", "split_count",
                      "preload_attention_kernels", "attention_mma_supported", "launch_attention_batched"):
         assert expected in names
-    missing = [n for n in sorted(names) if f"kvbridge::{n}(" not in syms]
+    missing = [n for n in sorted(names)
+               if f"kvbridge::{n}(" not in syms and f"kvbridge::detail::{n}(" not in syms]
     assert not missing, missing
 
 
@@ -123,3 +124,27 @@ def test_b200_predicate(kvb_lib):
                                                    pages=128), aligned)
     shifted = kvb.DeviceInput(FAKE, FAKE, FAKE, FAKE, FAKE + 4, FAKE, FAKE, FAKE)
     assert not kvb.attention_b200_supported(_shape(), shifted)
+
+
+def test_wait_limit_setting(kvb_lib):
+    """The bound of the kernels' pipeline waits is a launch parameter the host
+    sets (no GPU needed to read it back)."""
+    assert kvb.wait_limit_ns() == 2_000_000_000
+    kvb.set_wait_limit_ns(5_000_000)
+    assert kvb.wait_limit_ns() == 5_000_000
+    kvb.set_wait_limit_ns(0)
+    assert kvb.wait_limit_ns() == 2_000_000_000
+
+
+def test_launch_failure_hook_does_not_mask_validation(kvb_lib):
+    """An armed launch-failure hook only replaces a launch: a call that fails
+    validation first still reports KVB_EINVAL, and disarming is a no-op."""
+    inp = kvb.DeviceInput(FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, FAKE)
+    kvb.debug_fail_launch(1, 2)
+    try:
+        with pytest.raises(ValueError, match="dim must be in"):
+            kvb.launch_attention(_shape(dim=0), inp, FAKE, FAKE, FAKE, FAKE)
+    finally:
+        kvb.debug_fail_launch(0, 0)
+    with pytest.raises(ValueError, match="shard_stride"):
+        kvb.merge_attention_shards_ex(2, 32, 128, FAKE, FAKE, FAKE, 16, FAKE, FAKE, FAKE)

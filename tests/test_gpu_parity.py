@@ -541,3 +541,65 @@ def test_independent_streams(cuda_device):
     torch.cuda.synchronize()
     for o, e in zip(outs, expect):
         assert torch.equal(o, e)
+
+
+@pytest.mark.parametrize("page_tokens", [64, 16])
+def test_bf16_output(cuda_device, page_tokens):
+    """The bf16 epilogue (beside the fp16 one): each element is n * (1 / l)
+    in fp32 rounded to nearest-even bf16, within the path tolerance of the
+    FP64 oracle; both outputs come from the same merge."""
+    case = make(cuda_device, rows=1, q_heads=32, kv_heads=8, dim=128, page_tokens=page_tokens, tokens=6000,
+                seed=0xC0FFEE + 9)
+    s = case.shape
+    scratch, m, l, n = outputs_for(s, cuda_device)
+    nd = kvb.output_numerator_elements(s)
+    out16 = torch.full((nd,), float("nan"), dtype=torch.float16, device=cuda_device)
+    outbf = torch.full((nd,), float("nan"), dtype=torch.bfloat16, device=cuda_device)
+    kvb.launch_attention_ex(s, case.device_input(), scratch, m, l, n, out_f16=out16, out_bf16=outbf)
+    torch.cuda.synchronize()
+    ref = oracle.reference_case(case, threads=8)
+    res = {"m": m.cpu(), "l": l.cpu(), "n": n.cpu(), "out": out16.cpu()}
+    check_against_oracle(res, s, ref, "bf16 run")
+    from kvb_testutil import check_bf16
+
+    check_bf16(outbf.cpu(), s, ref, "bf16")
+    lh = res["l"].repeat_interleave(s.dim)
+    expect = (res["n"] * torch.where(lh > 0, 1.0 / lh, torch.zeros_like(lh))).to(torch.bfloat16)
+    assert torch.equal(outbf.cpu().view(torch.int16), expect.view(torch.int16))
+    # bf16 alone (no fp16 buffer) through merge_attention_ex over the same scratch.
+    outbf2 = torch.empty_like(outbf)
+    _, m2, l2, n2 = outputs_for(s, cuda_device)
+    parts = kvb.attention_partitions(s, 0)
+    kvb.merge_attention_ex(s, scratch, parts, m2, l2, n2, out_bf16=outbf2)
+    torch.cuda.synchronize()
+    assert torch.equal(outbf2.cpu().view(torch.int16), outbf.cpu().view(torch.int16))
+
+
+def test_packed_shard_merge(cuda_device):
+    """Sequence sharding with one packed exchange buffer per rank
+    ([m | l | n] of every row-head, as one all-gather delivers them): the
+    strided shard merge equals the separate-array merge bit for bit and the
+    full-range result within tolerance."""
+    case = make(cuda_device, rows=1, q_heads=32, kv_heads=8, dim=128, page_tokens=64, tokens=8192, seed=56)
+    rh, D = 32, 128
+    cuts = [0, 1024, 4096, 6144, 8192]
+    packed = torch.empty(len(cuts) - 1, rh * (D + 2), device=cuda_device)
+    for i, (a, b) in enumerate(zip(cuts[:-1], cuts[1:])):
+        shape = kvb.Shape(**{**case.shape.__dict__, "begin": a, "end": b})
+        scratch = torch.empty(kvb.scratch_elements(shape), device=cuda_device)
+        blk = packed[i]
+        kvb.launch_attention_ex(shape, case.device_input(), scratch, blk[:rh], blk[rh:2 * rh], blk[2 * rh:])
+    outs = []
+    for stride, parts in ((rh * (D + 2), (packed, packed[:, rh:], packed[:, 2 * rh:])),
+                          (0, (packed[:, :rh].contiguous(), packed[:, rh:2 * rh].contiguous(),
+                               packed[:, 2 * rh:].contiguous()))):
+        m = torch.empty(rh, device=cuda_device)
+        l = torch.empty(rh, device=cuda_device)
+        n = torch.empty(rh * D, device=cuda_device)
+        out = torch.empty(rh * D, dtype=torch.float16, device=cuda_device)
+        kvb.merge_attention_shards_ex(len(cuts) - 1, rh, D, *parts, stride, m, l, n, out_f16=out)
+        torch.cuda.synchronize()
+        outs.append({"m": m.cpu(), "l": l.cpu(), "n": n.cpu(), "out": out.cpu()})
+    for k in ("m", "l", "n", "out"):
+        assert torch.equal(outs[0][k], outs[1][k]), k
+    check_against_oracle(outs[0], case.shape, oracle.reference_case(case, threads=8), "packed shards")

@@ -19,7 +19,7 @@ import kvbridge_b200 as kvb
 import oracle
 
 ROOT = Path(__file__).resolve().parents[1]
-REF = Path("/root/reference")
+REF = oracle.REFERENCE_DIR
 U32 = 0xFFFFFFFF
 
 BASE = dict(rows=8, q_heads=24, kv_heads=4, dim=256, page_tokens=32, pages=2048, tokens=65536,
