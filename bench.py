@@ -82,8 +82,11 @@ def parse_args():
     ap.add_argument("--block-calls", type=int, default=500, help="calls per CUDA graph (rounded to whole step blocks)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extra", action="store_true", help="skip the weak-scaling and cfg5 keys")
-    ap.add_argument("--config", choices=["cfg2", "cfg1", "cfg3", "cfg4", "cfg5"], default="cfg2",
-                    help="BASELINE workload; the headline line is cfg2, the others are informational")
+    ap.add_argument("--config", choices=["cfg2", "cfg1", "cfg3", "cfg4", "cfg5", "native"], default="cfg2",
+                    help="BASELINE workload; the headline line is cfg2, the others are informational "
+                         "(native: the reference MMA kernel's rows-8 / 24-4 heads / dim-256 / Page32 shape)")
+    ap.add_argument("--kernel", choices=["auto", "warp", "tcgen05"], default="auto",
+                    help="single-sequence partial kernel (auto = chosen by shape)")
     return ap.parse_args()
 
 
@@ -439,6 +442,8 @@ def main():
     rc = kvb.preload_attention_kernels()
     if rc != 0:
         raise RuntimeError(f"preload_attention_kernels failed: cudaError {rc}")
+    kvb.set_decode_kernel({"auto": kvb.KERNEL_AUTO, "warp": kvb.KERNEL_WARP_MMA,
+                           "tcgen05": kvb.KERNEL_TCGEN05}[args.kernel])
     if args.config != "cfg2":
         return run_other_config(args, world, rank, local_rank, device)
     if 8 % world:
@@ -450,6 +455,7 @@ def main():
     # ---- headline: cfg2 split over the ranks along KV heads (strong scaling).
     kv_local, q_local = 8 // world, 32 // world
     layers = make_layers(synth, world, rank, kv_local, q_local, device)
+    torch.cuda.synchronize()  # generated on the default stream; calls run on bench.stream
     shape = layers[0].shape
     nbytes_rank = kv_bytes_per_call(shape.end - shape.begin, shape.kv_heads, shape.dim)
     nbytes_problem = kv_bytes_per_call(65536, 8, 128)
@@ -634,7 +640,8 @@ def main():
         ),
         "roofline": {
             "bound": "hbm",
-            "kernel": "decode_partial_kernel<128,1,6,false,false>",
+            "kernel": ("kvb::decode_partial_tc_kernel<128,64,8,6> (tcgen05, TMEM accumulators)"
+                       if args.kernel == "tcgen05" else "kvb::decode_partial_kernel<128,1,6,false,false>"),
             "achieved": round(achieved, 2),
             "peak": peak,
             "unit": "GB/s",
@@ -680,6 +687,7 @@ def weak_replicated(args, bench, kvb, synth, world, rank, device):
     import torch
 
     layers = make_layers(synth, world, rank + 97, 8, 32, device)
+    torch.cuda.synchronize()  # generated on the default stream; calls run on bench.stream
     shape = layers[0].shape
     scratch = torch.empty(kvb.scratch_elements(shape), device=device)
     m = torch.empty(32, device=device)
@@ -729,6 +737,7 @@ def cfg5_sequence_sharded(args, bench, kvb, synth, world, rank, device):
     binp = bc.batch_input()
     out = torch.empty(rh * D, dtype=torch.float16, device=device)
     merge = sharding.gpu_packed_shard_merge(rh, D, device) if world > 1 else None
+    torch.cuda.synchronize()  # generated on the default stream; calls run on bench.stream
 
     def local_step():
         kvb.launch_attention_batched(bc.shape, binp, ws, ws_bytes, pm, pl, pn, out if world == 1 else None)
@@ -804,6 +813,27 @@ def run_other_config(args, world, rank, local_rank, device):
             total_bytes = world * case.kv_bytes()
             desc = dict(workload="cfg1: B1, 4,096 ctx, 32/8, dim 128, Page64 shuffled, 8 partitions",
                         scaling="weak")
+        elif cfg == "native":
+            # The reference MMA kernel's shape (examples/attention_bench.cu): 8
+            # causal query rows, 24/4 heads, dim 256, 32-token pages, 32,768
+            # tokens; eight resident layers (545 MB) rotated over the steps.
+            tokens, rows = 32768, 8
+            cases = [synth.make_single(rows, 24, 4, 256, 32, tokens, 0xC0FFEE + 8 + 100 * rank + i, device,
+                                       q_positions=[tokens - rows + r for r in range(rows)]) for i in range(8)]
+            shape = cases[0].shape
+            scratch = torch.empty(kvb.scratch_elements(shape), device=device)
+            m = torch.empty(rows * 24, device=device)
+            l = torch.empty(rows * 24, device=device)
+            n = torch.empty(rows * 24 * 256, device=device)
+            inps = [c.device_input() for c in cases]
+
+            def step(i):
+                kvb.launch_attention_mma(shape, inps[i % len(inps)], scratch, m, l, n)
+
+            total_bytes = world * cases[0].kv_bytes()
+            desc = dict(workload="native: rows 8 (causal), 24/4 heads, dim 256, Page32, 32,768 ctx, "
+                                 "launch_attention_mma", scaling="weak",
+                        kernel=args.kernel, partitions=kvb.attention_partitions(shape, 0))
         else:
             if cfg == "cfg3":
                 lens = synth.ragged_lengths(32, 1024, 32768, seed=0xC0FFEE + 3)
@@ -833,6 +863,7 @@ def run_other_config(args, world, rank, local_rank, device):
             desc = dict(workload=f"{cfg}: batch {len(lens)}, {q_heads}/{kv_heads} heads, dim 128, Page{page}"
                                  + (", ragged U[1024,32768]" if cfg == "cfg3" else ", 16,384 ctx, 1% 10x outliers"),
                         sharding=f"kv-heads: {kv_local} of {kv_heads} per GPU", scaling="strong")
+        torch.cuda.synchronize()  # generated on the default stream; calls run on bench.stream
         with torch.cuda.stream(bench.stream):
             step(0)
         torch.cuda.synchronize()

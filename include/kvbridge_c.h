@@ -183,25 +183,39 @@ unsigned long long kvb_wait_limit_ns(void);
 int kvb_debug_fail_launch(unsigned nth, int cuda_error);
 int kvb_debug_skip_stage(unsigned stage);
 
+/* Which single-sequence partial kernel later calls use (process-wide):
+ * KVB_KERNEL_AUTO chooses by shape, KVB_KERNEL_WARP_MMA the warp-level int8
+ * MMA kernel, KVB_KERNEL_TCGEN05 the TMEM-accumulator tcgen05 kernel wherever
+ * it has a variant for the shape (else the warp-level one). For side-by-side
+ * measurements and tests; results agree within the path tolerance.
+ * kvb_decode_kernel returns the current choice. */
+#define KVB_KERNEL_AUTO 0
+#define KVB_KERNEL_WARP_MMA 1
+#define KVB_KERNEL_TCGEN05 2
+int kvb_set_decode_kernel(int choice);
+int kvb_decode_kernel(void);
+
 /* Decode call that allocates nothing. It has no counterpart in the
  * reference. kvb_launch_attention_ex needs a caller-provided scratch buffer
- * of scratch_elements(shape) floats; callers that cannot allocate device
- * memory when they make the call - a serving loop whose HBM is fully
- * reserved up front by its KV-cache allocator, or code that issues the call
- * inside CUDA-graph stream capture, where cudaMalloc is not permitted - use
- * this one instead. It is kvb_launch_attention_ex (same inputs, outputs,
- * partitions and optional fp16 output) with the split-K partials kept in a
- * static device array of KVB_NOALLOC_SCRATCH_FLOATS floats (2 MiB) that
- * every GPU loading the library holds until process exit.
+ * of scratch_elements(shape) floats; callers that cannot call cudaMalloc
+ * when they decode - an inference server whose memory pool reserved all of
+ * HBM up front for its KV cache, or a host whose decode path must not
+ * allocate - use this one instead. It is kvb_launch_attention_ex (same
+ * inputs, outputs, partitions and optional fp16 output) with the split-K
+ * partials kept in a static device array of KVB_NOALLOC_SCRATCH_FLOATS
+ * floats (2 MiB) that every GPU loading the library holds until process
+ * exit.
  *   - Limits: the tensor-core geometry only (kvb_attention_b200_supported);
  *     partitions are clamped so rows * q_heads * partitions * (dim + 2)
- *     fits the array; larger shapes return KVB_EINVAL with a message.
- *   - The first call on each device looks up the array's device address
- *     (cudaGetSymbolAddress); make that first call outside stream capture.
+ *     fits the array; a shape whose single partition does not fit returns
+ *     KVB_EINVAL with a message.
+ *   - The first call in each CUDA context looks up the array's device
+ *     address (cudaGetSymbolAddress); make that first call before any
+ *     stream capture.
  *   - It calls no cudaMalloc, cudaFree or other allocating routine.
  *   - All calls share the array: calls that can overlap on the GPU (other
- *     streams, concurrent graph replays) race and must be serialised. No
- *     part of the array needs clearing between calls. */
+ *     streams) race and must be serialised. No part of the array needs
+ *     clearing between calls. */
 #define KVB_NOALLOC_SCRATCH_FLOATS 524288
 int kvb_launch_attention_noalloc(const kvb_shape* s, const kvb_device_input* in,
                                  unsigned partitions, float* m, float* l, float* n,

@@ -184,6 +184,8 @@ SIGNATURES = {
     "kvb_wait_limit_ns": (ctypes.c_ulonglong, []),
     "kvb_debug_fail_launch": (c_int, [ctypes.c_uint, c_int]),
     "kvb_debug_skip_stage": (c_int, [ctypes.c_uint]),
+    "kvb_set_decode_kernel": (c_int, [c_int]),
+    "kvb_decode_kernel": (c_int, []),
     "kvb_read_device_status": (c_int, [POINTER(c_int)]),
     "kvb_read_wait_failure": (c_int, [POINTER(ctypes.c_longlong)]),
     "kvb_schedule_cta_of": (c_uint32, [c_uint64, c_uint64, c_uint32]),

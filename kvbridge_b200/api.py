@@ -363,6 +363,19 @@ def debug_skip_stage(stage: int) -> None:
     check(_lib.load().kvb_debug_skip_stage(stage))
 
 
+KERNEL_AUTO, KERNEL_WARP_MMA, KERNEL_TCGEN05 = 0, 1, 2
+
+
+def set_decode_kernel(choice: int) -> None:
+    """Which single-sequence partial kernel later calls use: KERNEL_AUTO (by
+    shape), KERNEL_WARP_MMA or KERNEL_TCGEN05 (where a variant exists)."""
+    check(_lib.load().kvb_set_decode_kernel(int(choice)))
+
+
+def decode_kernel() -> int:
+    return int(_lib.load().kvb_decode_kernel())
+
+
 def launch_attention_noalloc(s: Shape, inp: DeviceInput, m, l, n, partitions: int = 0, out_f16=None,
                              stream=None) -> None:
     """The decode call that allocates nothing: split-K partials in the

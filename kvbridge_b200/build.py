@@ -27,6 +27,7 @@ HEADERS = [
     "kvb_device.cuh",
     "kvb_schedule.h",
     "decode_tma.cuh",
+    "decode_tc.cuh",
     "decode_simt.cuh",
     "merge.cuh",
     "append_kv.cuh",

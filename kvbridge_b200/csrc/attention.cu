@@ -21,6 +21,7 @@
 #include "launch_checks.h"
 #include "decode_simt.cuh"
 #include "decode_tma.cuh"
+#include "decode_tc.cuh"
 #include "merge.cuh"
 #include "append_kv.cuh"
 
@@ -175,28 +176,83 @@ FastVariant fast_variant(uint32_t dim, uint32_t nt, uint32_t page_tokens, bool b
   return FastVariant{};
 }
 
-// Resident CTAs of a variant per SM on the current device (cached).
-int resident_ctas(const FastVariant& v) {
+// Resident CTAs of a kernel per SM on the current device (cached).
+int resident_ctas(const void* fn, int threads, uint32_t smem) {
   static std::mutex mu;
   static std::map<std::pair<int, const void*>, int> cache;
   int dev = 0;
   cuda_ok(cudaGetDevice(&dev), "cudaGetDevice");
   {
     std::lock_guard<std::mutex> lock(mu);
-    auto it = cache.find({dev, v.fn});
+    auto it = cache.find({dev, fn});
     if (it != cache.end()) return it->second;
   }
-  cuda_ok(cudaFuncSetAttribute(v.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(v.smem)),
+  cuda_ok(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)),
           "decode kernel shared-memory opt-in");
   int blocks = 0;
-  cuda_ok(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, v.fn, kvb::kDecodeThreads,
-                                                        v.smem),
+  cuda_ok(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, fn, threads, smem),
           "occupancy query");
   blocks = std::max(blocks, 1);
   std::lock_guard<std::mutex> lock(mu);
-  cache[{dev, v.fn}] = blocks;
+  cache[{dev, fn}] = blocks;
   return blocks;
 }
+
+int resident_ctas(const FastVariant& v) { return resident_ctas(v.fn, kvb::kDecodeThreads, v.smem); }
+
+// ---------------------------------------------------------------------------
+// tcgen05 (TMEM accumulator) variants of the single-sequence partial kernel:
+// (head dim, page tokens, query columns per KV head, ring slots, column
+// halves per thread group).
+
+struct TcVariant {
+  const void* fn = nullptr;
+  uint32_t smem = 0;
+  int threads = 0;
+  uint32_t columns = 0;  // query columns per KV head it holds
+  void (*launch)(const kvb::DecodeParamsTc&, cudaStream_t) = nullptr;
+};
+
+template <int D, int P, int NC, int SLOTS, int NH>
+const void* tc_kernel_fn() {
+  return reinterpret_cast<const void*>(&kvb::decode_partial_tc_kernel<D, P, NC, SLOTS, NH>);
+}
+
+template <int D, int P, int NC, int SLOTS, int NH>
+void launch_tc_variant(const kvb::DecodeParamsTc& prm, cudaStream_t stream) {
+  using L = kvb::TcSmem<D, P, NC, SLOTS, NH>;
+  const void* fn = tc_kernel_fn<D, P, NC, SLOTS, NH>();
+  constexpr uint32_t smem = L::kDynamicBytes;
+  cuda_ok(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)),
+          "decode kernel shared-memory opt-in");
+  cuda_ok(prefer_max_shared(fn), "decode kernel carveout");
+  kvb::DecodeParamsTc copy = prm;
+  void* args[] = {&copy};
+  launch_pdl(fn, dim3(prm.ctas), dim3(L::kThreads), smem, stream, args, "decode partial launch");
+}
+
+template <int D, int P, int NC, int SLOTS, int NH>
+TcVariant make_tc_variant() {
+  using L = kvb::TcSmem<D, P, NC, SLOTS, NH>;
+  TcVariant v;
+  v.fn = tc_kernel_fn<D, P, NC, SLOTS, NH>();
+  v.smem = L::kDynamicBytes;
+  v.threads = int(L::kThreads);
+  v.columns = NC;
+  v.launch = &launch_tc_variant<D, P, NC, SLOTS, NH>;
+  return v;
+}
+
+TcVariant tc_variant(uint32_t dim, uint32_t page_tokens, uint32_t qrows) {
+  if (dim == 256 && page_tokens == 32 && qrows <= 48) return make_tc_variant<256, 32, 48, 4, 2>();
+  if (dim == 128 && page_tokens == 64 && qrows <= 8) return make_tc_variant<128, 64, 8, 6, 1>();
+  return TcVariant{};
+}
+
+// Which single-sequence partial kernel runs: 0 = by shape (tcgen05 where it
+// was measured to win), 1 = the warp-level MMA kernel, 2 = tcgen05 wherever
+// a variant exists. Process-wide (detail::set_decode_kernel).
+std::atomic<int> g_decode_kernel{0};
 
 uint32_t query_rows(const Shape& s) { return s.rows * (s.q_heads / s.kv_heads); }
 
@@ -307,6 +363,19 @@ uint32_t batched_ctas(const FastVariant& v) {
   return uint32_t(current_device_facts().sms) * uint32_t(resident_ctas(v));
 }
 
+// The tcgen05 variant a single-sequence call on the tensor-core path uses,
+// or none (the warp-level MMA kernel).
+TcVariant chosen_tc_variant(const Shape& s) {
+  const int choice = g_decode_kernel.load();
+  if (choice == 1) return TcVariant{};
+  const TcVariant v = tc_variant(s.dim, s.page_tokens, query_rows(s));
+  if (v.fn == nullptr) return v;
+  if (choice == 2) return v;
+  // By shape: many query columns per KV head at dim 256, where the warp-level
+  // kernel splits the columns over CTAs that each re-read the pages.
+  return (s.dim == 256 && query_rows(s) > 8) ? v : TcVariant{};
+}
+
 }  // namespace
 
 // ---------------------------------------------------------------------------
@@ -325,11 +394,18 @@ unsigned attention_partitions(const Shape& s, unsigned requested) {
   if (stages == 0) return 0;
   uint32_t parts = requested;
   if (parts == 0) {
-    const ColumnPlan plan = column_plan(s.dim, query_rows(s));
-    const FastVariant v = fast_variant(s.dim, plan.nt, s.page_tokens, false);
-    const uint32_t wave =
-        v.fn ? uint32_t(current_device_facts().sms) * uint32_t(resident_ctas(v)) : 1u;
-    parts = std::max(1u, wave / (s.kv_heads * plan.groups));
+    const TcVariant tcv = chosen_tc_variant(s);
+    if (tcv.fn != nullptr) {
+      const uint32_t wave = uint32_t(current_device_facts().sms) *
+                            uint32_t(resident_ctas(tcv.fn, tcv.threads, tcv.smem));
+      parts = std::max(1u, wave / s.kv_heads);
+    } else {
+      const ColumnPlan plan = column_plan(s.dim, query_rows(s));
+      const FastVariant v = fast_variant(s.dim, plan.nt, s.page_tokens, false);
+      const uint32_t wave =
+          v.fn ? uint32_t(current_device_facts().sms) * uint32_t(resident_ctas(v)) : 1u;
+      parts = std::max(1u, wave / (s.kv_heads * plan.groups));
+    }
   }
   parts = std::min(parts, stages);
   parts = std::min(parts, split_count(s));
@@ -478,7 +554,61 @@ kvb::DecodeParamsGather single_params(const Shape& s, const DeviceInput& in, uin
   return prm;
 }
 
+// Tensor maps of the tcgen05 kernel: K rows of `dim` bytes per (page, KV
+// head, slot) in boxes of 128 bytes x page_tokens rows, 128-byte swizzle;
+// V rows of page_tokens bytes per (page, KV head, dim) in boxes of
+// page_tokens bytes x dim rows, 32- or 64-byte swizzle (the K-major operand
+// layouts of tcgen05.mma). False when they cannot be encoded.
+bool set_tc_maps(kvb::DecodeParamsTc& prm, uint32_t dim) {
+  const PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
+  if (encode == nullptr) return false;
+  const uint64_t P = prm.page_tokens;
+  const uint64_t units = uint64_t(prm.pages) * prm.kv_heads;
+  const cuuint32_t elem_strides[2] = {1, 1};
+  const cuuint64_t k_dims[2] = {dim, units * P};
+  const cuuint64_t k_strides[1] = {dim};
+  const cuuint32_t k_box[2] = {128, cuuint32_t(P)};
+  const cuuint64_t v_dims[2] = {P, units * dim};
+  const cuuint64_t v_strides[1] = {P};
+  const cuuint32_t v_box[2] = {cuuint32_t(P), dim};
+  if (k_dims[1] > 0x7fffffffull || v_dims[1] > 0x7fffffffull) return false;
+  return encode(&prm.tm_k, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t*>(prm.k), k_dims, k_strides,
+                k_box, elem_strides, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS &&
+         encode(&prm.tm_v, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t*>(prm.v), v_dims, v_strides,
+                v_box, elem_strides, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                P == 32 ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_64B,
+                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// The single-sequence partial kernel (tcgen05 or warp-level MMA, as chosen
+// for the shape) over `parts` partitions; partials go to `scratch` with
+// `split_stride` slots per row-head.
+void launch_single_partials(const Shape& s, const DeviceInput& in, uint32_t parts, float* scratch,
+                            uint32_t split_stride, cudaStream_t stream) {
+  kvb::DecodeParamsGather prm = single_params(s, in, parts, scratch, split_stride);
+  prm.prefetch_stages = kPrefetchStages;
+  const TcVariant tcv = chosen_tc_variant(s);
+  if (tcv.fn != nullptr) {
+    kvb::DecodeParamsTc tp{};
+    static_cast<kvb::DecodeParams&>(tp) = static_cast<const kvb::DecodeParams&>(prm);
+    tp.col_groups = 1;
+    tp.group_cols = tcv.columns;
+    tp.ctas = parts * s.kv_heads;
+    if (set_tc_maps(tp, s.dim)) {
+      tcv.launch(tp, stream);
+      return;
+    }
+  }
+  fast_variant(s.dim, prm.group_cols / 8, s.page_tokens, false).launch(prm, stream);
+}
+
 }  // namespace
+
+namespace detail {
+void set_decode_kernel(int choice) noexcept { g_decode_kernel.store(choice < 0 || choice > 2 ? 0 : choice); }
+int decode_kernel() noexcept { return g_decode_kernel.load(); }
+}  // namespace detail
 
 unsigned launch_attention_partials(const Shape& s, const DeviceInput& in, unsigned partitions,
                                    float* scratch, cudaStream_t stream) {
@@ -490,9 +620,7 @@ unsigned launch_attention_partials(const Shape& s, const DeviceInput& in, unsign
   const uint32_t splits = split_count(s);
   const uint32_t parts = attention_partitions(s, partitions);
   if (parts == 0) return 0;
-  kvb::DecodeParamsGather prm = single_params(s, in, parts, scratch, splits);
-  prm.prefetch_stages = kPrefetchStages;
-  fast_variant(s.dim, prm.group_cols / 8, s.page_tokens, false).launch(prm, stream);
+  launch_single_partials(s, in, parts, scratch, splits, stream);
   return parts;
 }
 
@@ -867,10 +995,8 @@ void launch_attention_noalloc(const Shape& s, const DeviceInput& in, unsigned pa
   float* scratch = noalloc_scratch_in_current_context();
   if (parts > 0) {
     // Partials packed [row-head][partition]: split stride = parts. Same
-    // launch as launch_attention_partials, L2 prefetch included.
-    kvb::DecodeParamsGather prm = single_params(s, in, parts, scratch, parts);
-    prm.prefetch_stages = kPrefetchStages;
-    fast_variant(s.dim, prm.group_cols / 8, s.page_tokens, false).launch(prm, stream);
+    // kernel and launch as launch_attention_partials.
+    launch_single_partials(s, in, parts, scratch, parts, stream);
   }
   launch_merge(kvb::kMergeScratch,
                scratch_merge_params(s, scratch, parts, parts, false, m, l, n, out_f16), stream);

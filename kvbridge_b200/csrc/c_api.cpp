@@ -310,6 +310,13 @@ int kvb_debug_fail_launch(unsigned nth, int cuda_error) {
   return KVB_OK;
 }
 
+int kvb_set_decode_kernel(int choice) {
+  kvbridge::detail::set_decode_kernel(choice);
+  return KVB_OK;
+}
+
+int kvb_decode_kernel(void) { return kvbridge::detail::decode_kernel(); }
+
 int kvb_debug_skip_stage(unsigned stage) {
   kvbridge::detail::skip_stage(stage);
   return KVB_OK;
