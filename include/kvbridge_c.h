@@ -195,6 +195,12 @@ int kvb_debug_skip_stage(unsigned stage);
 int kvb_set_decode_kernel(int choice);
 int kvb_decode_kernel(void);
 
+/* Event timeline of the tcgen05 partial kernel, in libraries built with the
+ * trace flag (python -m kvbridge_b200.build --trace): copies up to `count`
+ * SM clock stamps [16 CTAs][16 tiles][15 events] of the latest launches
+ * and clears them. Other builds return KVB_EINVAL. */
+int kvb_debug_read_tc_trace(unsigned long long* out, size_t count);
+
 /* Decode call that allocates nothing. It has no counterpart in the
  * reference. kvb_launch_attention_ex needs a caller-provided scratch buffer
  * of scratch_elements(shape) floats; callers that cannot call cudaMalloc

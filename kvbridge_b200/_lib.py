@@ -11,6 +11,9 @@ from ctypes import POINTER, c_bool, c_char_p, c_float, c_int, c_size_t, c_uint32
 from pathlib import Path
 
 LIB_PATH = Path(__file__).resolve().parent / "libkvbridge_b200.so"
+# The event-trace build of the same library (python -m kvbridge_b200.build
+# --trace); loaded instead of LIB_PATH when $KVB_TRACE_LIBRARY is set to 1.
+TRACE_LIB_PATH = Path(__file__).resolve().parent / "libkvbridge_b200_trace.so"
 
 KVB_OK = 0
 KVB_EINVAL = 1
@@ -185,6 +188,7 @@ SIGNATURES = {
     "kvb_debug_fail_launch": (c_int, [ctypes.c_uint, c_int]),
     "kvb_debug_skip_stage": (c_int, [ctypes.c_uint]),
     "kvb_set_decode_kernel": (c_int, [c_int]),
+    "kvb_debug_read_tc_trace": (c_int, [POINTER(ctypes.c_ulonglong), c_size_t]),
     "kvb_decode_kernel": (c_int, []),
     "kvb_read_device_status": (c_int, [POINTER(c_int)]),
     "kvb_read_wait_failure": (c_int, [POINTER(ctypes.c_longlong)]),
@@ -207,11 +211,14 @@ def load() -> ctypes.CDLL:
     global _lib
     if _lib is not None:
         return _lib
-    if not LIB_PATH.exists():
+    import os
+
+    path = TRACE_LIB_PATH if os.environ.get("KVB_TRACE_LIBRARY") == "1" else LIB_PATH
+    if not path.exists():
         raise LibraryMissing(
-            f"{LIB_PATH} not found: run `python -m kvbridge_b200.build` (nvcc, sm_100a)"
+            f"{path} not found: run `python -m kvbridge_b200.build` (nvcc, sm_100a)"
         )
-    lib = ctypes.CDLL(str(LIB_PATH))
+    lib = ctypes.CDLL(str(path))
     for name, (restype, argtypes) in SIGNATURES.items():
         fn = getattr(lib, name)
         fn.restype = restype

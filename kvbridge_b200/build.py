@@ -56,15 +56,24 @@ def _run(cmd: list[str]) -> None:
         raise RuntimeError(f"command failed ({proc.returncode}): {' '.join(cmd)}")
 
 
-def build(force: bool = False, verbose_ptxas: bool = False) -> Path:
-    """Compile the library if any input changed (or ``force``); return its path."""
-    if not force and not needs_build():
-        return LIB
-    BUILD_DIR.mkdir(exist_ok=True)
+TRACE_LIB = PKG / "libkvbridge_b200_trace.so"
+TRACE_BUILD_DIR = PKG / "_build_trace"
+
+
+def build(force: bool = False, verbose_ptxas: bool = False, trace: bool = False) -> Path:
+    """Compile the library if any input changed (or ``force``); return its path.
+    ``trace`` builds the event-trace variant (-DKVB_TC_TRACE) beside it."""
+    lib, build_dir = (TRACE_LIB, TRACE_BUILD_DIR) if trace else (LIB, BUILD_DIR)
+    if not force and lib.exists() and not any(
+            f.stat().st_mtime > lib.stat().st_mtime for f in _inputs() if f.exists()):
+        return lib
+    build_dir.mkdir(exist_ok=True)
     common = ["-std=c++17", "-O3", f"-I{INCLUDE}", f"-I{CSRC}", "-Xcompiler", "-fPIC"]
+    if trace:
+        common.append("-DKVB_TC_TRACE")
     objects = []
     for src in SOURCES:
-        obj = BUILD_DIR / (Path(src).stem + ".o")
+        obj = build_dir / (Path(src).stem + ".o")
         cmd = [NVCC, *common, "-c", str(CSRC / src), "-o", str(obj)]
         if src.endswith(".cu"):
             cmd[1:1] = [*ARCH, "-lineinfo", "--expt-relaxed-constexpr"]
@@ -72,12 +81,12 @@ def build(force: bool = False, verbose_ptxas: bool = False) -> Path:
                 cmd.insert(1, "-Xptxas=-v")
         _run(cmd)
         objects.append(str(obj))
-    tmp = LIB.with_suffix(".so.tmp")
+    tmp = lib.with_suffix(".so.tmp")
     _run([NVCC, *ARCH, "-shared", "-o", str(tmp), *objects, "-Xlinker", "-Bsymbolic"])
-    os.replace(tmp, LIB)
-    return LIB
+    os.replace(tmp, lib)
+    return lib
 
 
 if __name__ == "__main__":
     force = "--force" in sys.argv
-    print(build(force=force, verbose_ptxas="--ptxas-v" in sys.argv))
+    print(build(force=force, verbose_ptxas="--ptxas-v" in sys.argv, trace="--trace" in sys.argv))

@@ -244,7 +244,7 @@ TcVariant make_tc_variant() {
 }
 
 TcVariant tc_variant(uint32_t dim, uint32_t page_tokens, uint32_t qrows) {
-  if (dim == 256 && page_tokens == 32 && qrows <= 48) return make_tc_variant<256, 32, 48, 4, 2>();
+  if (dim == 256 && page_tokens == 32 && qrows <= 48) return make_tc_variant<256, 32, 48, 4, 3>();
   if (dim == 128 && page_tokens == 64 && qrows <= 8) return make_tc_variant<128, 64, 8, 6, 1>();
   return TcVariant{};
 }
@@ -556,9 +556,9 @@ kvb::DecodeParamsGather single_params(const Shape& s, const DeviceInput& in, uin
 
 // Tensor maps of the tcgen05 kernel: K rows of `dim` bytes per (page, KV
 // head, slot) in boxes of 128 bytes x page_tokens rows, 128-byte swizzle;
-// V rows of page_tokens bytes per (page, KV head, dim) in boxes of
-// page_tokens bytes x dim rows, 32- or 64-byte swizzle (the K-major operand
-// layouts of tcgen05.mma). False when they cannot be encoded.
+// V as 64-byte rows (one dim of a 64-token page, two of a 32-token page) in
+// boxes of one page's rows, 64-byte swizzle (the K-major operand layouts of
+// tcgen05.mma). False when they cannot be encoded.
 bool set_tc_maps(kvb::DecodeParamsTc& prm, uint32_t dim) {
   const PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
   if (encode == nullptr) return false;
@@ -568,16 +568,17 @@ bool set_tc_maps(kvb::DecodeParamsTc& prm, uint32_t dim) {
   const cuuint64_t k_dims[2] = {dim, units * P};
   const cuuint64_t k_strides[1] = {dim};
   const cuuint32_t k_box[2] = {128, cuuint32_t(P)};
-  const cuuint64_t v_dims[2] = {P, units * dim};
-  const cuuint64_t v_strides[1] = {P};
-  const cuuint32_t v_box[2] = {cuuint32_t(P), dim};
+  // 64-byte V rows: one dim of a 64-token page, or two dims of a 32-token page.
+  const uint64_t v_rows_per_page = dim * P / 64;
+  const cuuint64_t v_dims[2] = {64, units * v_rows_per_page};
+  const cuuint64_t v_strides[1] = {64};
+  const cuuint32_t v_box[2] = {64, cuuint32_t(v_rows_per_page)};
   if (k_dims[1] > 0x7fffffffull || v_dims[1] > 0x7fffffffull) return false;
   return encode(&prm.tm_k, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t*>(prm.k), k_dims, k_strides,
                 k_box, elem_strides, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS &&
          encode(&prm.tm_v, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t*>(prm.v), v_dims, v_strides,
-                v_box, elem_strides, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                P == 32 ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_64B,
+                v_box, elem_strides, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
@@ -891,6 +892,22 @@ void set_wait_limit_ns(unsigned long long ns) noexcept {
 unsigned long long wait_limit_ns() noexcept { return g_wait_limit_ns.load(); }
 
 namespace detail {
+
+cudaError_t read_tc_trace(unsigned long long* out, size_t count, bool* available) noexcept {
+#ifdef KVB_TC_TRACE
+  *available = true;
+  const size_t all = size_t(kvb::kTraceCtas) * kvb::kTraceTiles * kvb::kTraceEvents;
+  cudaError_t code = cudaMemcpyFromSymbol(out, kvb::g_tc_trace, std::min(count, all) * sizeof(unsigned long long));
+  if (code != cudaSuccess) return code;
+  static const unsigned long long zeros[kvb::kTraceCtas][kvb::kTraceTiles][kvb::kTraceEvents] = {};
+  return cudaMemcpyToSymbol(kvb::g_tc_trace, zeros, sizeof(zeros));
+#else
+  (void)out;
+  (void)count;
+  *available = false;
+  return cudaSuccess;
+#endif
+}
 
 void fail_launch(unsigned nth, cudaError_t code) noexcept {
   t_fail_countdown = nth;

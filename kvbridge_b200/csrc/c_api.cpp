@@ -14,6 +14,7 @@
 #include "kvb_schedule.h"
 
 namespace kvbridge::detail {
+cudaError_t read_tc_trace(unsigned long long* out, size_t count, bool* available) noexcept;
 void launch_attention_noalloc(const Shape&, const DeviceInput&, unsigned partitions, float* m,
                               float* l, float* n, void* out_f16, cudaStream_t);
 }  // namespace kvbridge::detail
@@ -308,6 +309,17 @@ unsigned long long kvb_wait_limit_ns(void) { return kvbridge::wait_limit_ns(); }
 int kvb_debug_fail_launch(unsigned nth, int cuda_error) {
   kvbridge::detail::fail_launch(nth, static_cast<cudaError_t>(cuda_error));
   return KVB_OK;
+}
+
+int kvb_debug_read_tc_trace(unsigned long long* out, size_t count) {
+  return guarded([&] {
+    if (out == nullptr) throw std::invalid_argument("output pointer is null");
+    bool available = false;
+    const cudaError_t code = kvbridge::detail::read_tc_trace(out, count, &available);
+    if (!available)
+      throw std::invalid_argument("this library was built without the tcgen05 event trace (KVB_TC_TRACE)");
+    if (code != cudaSuccess) throw std::runtime_error(std::string("trace read: ") + cudaGetErrorString(code));
+  });
 }
 
 int kvb_set_decode_kernel(int choice) {

@@ -28,9 +28,9 @@
 //       argument - written as two signed int8 digits into P^T[n][token], the
 //       B operand of PV.
 //   PV  O^T[d][n] = V[d][token] . P^T[n][token]       (tcgen05.mma kind::i8)
-//       A = the V codes exactly as stored (dim-major pages, loaded by TMA in
-//       the 32/64-byte-swizzled K-major layout), 128 dims per MMA; the s32
-//       accumulator has one TMEM lane per dim.
+//       A = the V codes exactly as stored (dim-major pages, loaded by TMA
+//       as 64-byte rows in the 64-byte-swizzled K-major layout), 128 rows per
+//       MMA; the s32 accumulator has one TMEM lane per dim (or dim pair).
 //   fold (4 NH warps, one thread per dim and column half): O[d][c] =
 //       O[d][c] * alpha_c + (lo + 256 hi) / pscale_c in fp32 registers.
 // One warp issues the TMA copies into the ring, one owns TMEM and issues the
@@ -52,50 +52,98 @@ namespace kvb {
 // Parameters: the single-sequence block of DecodeParams plus the tensor
 // maps of the K pool (rows of `dim` bytes per (page, KV head, slot), boxes of
 // 128 bytes x page_tokens rows, 128-byte swizzle) and of the V pool (rows of
-// page_tokens bytes per (page, KV head, dim), boxes of page_tokens bytes x
-// dim rows, 32- or 64-byte swizzle).
+// 64 bytes - one dim of a 64-token page or two dims of a 32-token page -
+// boxes of 64 bytes x one page's rows, 64-byte swizzle).
 struct DecodeParamsTc : DecodeParams {
   CUtensorMap tm_k, tm_v;
 };
+
+// Event timeline (trace builds only, -DKVB_TC_TRACE): SM clock stamps
+// (clock64; one CTA runs on one SM, so differences within a CTA are exact) of
+// the first kTraceCtas CTAs and kTraceTiles tiles of the last launch, read by
+// the host with kvb_debug_read_tc_trace. Events per tile: see kTrace*.
+constexpr uint32_t kTraceCtas = 16, kTraceTiles = 16, kTraceEvents = 15;
+enum : uint32_t {
+  kTraceStart = 0,       // tile 0 only: the CTA passed its setup barrier
+  kTraceQkIssued = 1,    // MMA thread issued QK(t) (its stages had landed)
+  kTraceSoftmaxIn = 2,   // softmax warp 0 saw S(t) ready
+  kTraceSoftmaxOut = 3,  // softmax warp 0 published P(t)
+  kTracePvIssued = 4,    // MMA thread issued PV(t)
+  kTraceFoldIn = 5,      // fold warp 0 saw O(t) ready
+  kTraceFoldOut = 6,     // fold warp 0 released O(t)
+  kTraceCopyIssued = 7,  // producer armed the tile's first stage
+  kTraceSmLoaded = 8,    // softmax warp 0 has S(t) in registers
+  kTraceSmReduced = 9,   // softmax warp 0 passed the column-max barrier
+  kTraceSmParams = 10,   // softmax warp 0 passed the column-parameter barrier
+  kTracePReadySeen = 11,  // MMA thread first saw P(t) published by every softmax warp
+  kTraceOFreeSeen = 12,   // MMA thread first saw O^T released for PV(t)
+  kTraceVSeen = 13,       // MMA thread first saw V(t) landed
+  kTraceSmStored = 14,    // softmax warp 0 finished its P digit stores (before the proxy fence)
+};
+#ifdef KVB_TC_TRACE
+__device__ unsigned long long g_tc_trace[kTraceCtas][kTraceTiles][kTraceEvents];
+#define KVB_TC_MARK(tile, event)                                                    \
+  do {                                                                              \
+    if (blockIdx.x < kTraceCtas && (tile) < kTraceTiles)                            \
+      g_tc_trace[blockIdx.x][(tile)][(event)] = clock64();                          \
+  } while (0)
+#else
+#define KVB_TC_MARK(tile, event) \
+  do {                           \
+  } while (0)
+#endif
 
 // Shared-memory layout (byte offsets; the dynamic shared memory base is
 // rounded up to 1024 bytes first) and warp roles. NC query columns per KV
 // head, split into NH halves between the softmax (and fold) warp groups; the
 // QK MMA has N = 3 NC (query digits), the PV MMA N = 2 NC (P digits), each
-// rounded up to a multiple of 16.
+// rounded up to a multiple of 16. K and V stages have rings of their own
+// (SLOTS 64-token slots each; a K slot is free once QK has read it, a V slot
+// once PV has), and the K/V scales a ring twice as deep, freed once the
+// softmax warps have read them.
 template <int D, int P, int NC, int SLOTS, int NH>
 struct TcSmem {
   static constexpr uint32_t kCH = NC / NH;  // columns per softmax / fold thread
   static constexpr uint32_t kSoftmaxWarps = 4 * NH;
   static constexpr uint32_t kFoldWarps = 4 * NH;
-  static constexpr uint32_t kProducerWarp = 8 * NH;
+  static constexpr uint32_t kProducerKWarp = 8 * NH;
   static constexpr uint32_t kMmaWarp = 8 * NH + 1;
-  static constexpr uint32_t kThreads = 32 * (8 * NH + 2);
+  static constexpr uint32_t kProducerVWarp = 8 * NH + 2;
+  static constexpr uint32_t kWarps = 8 * NH + 3;
+  static constexpr uint32_t kThreads = 32 * kWarps;
   // Registers are split between the SM's four sub-partitions (16K each) and
   // the warps are spread over them round-robin.
-  static constexpr uint32_t kWarpsPerSubpartition = (8 * NH + 2 + 3) / 4;
+  static constexpr uint32_t kWarpsPerSubpartition = (kWarps + 3) / 4;
   static constexpr uint32_t kMaxRegs = (16384 / (32 * kWarpsPerSubpartition)) / 8 * 8;
   static constexpr uint32_t kNQK = (3 * NC + 15) / 16 * 16;
   static constexpr uint32_t kNPV = (2 * NC + 15) / 16 * 16;
+  static constexpr uint32_t kScaleSlots = 2 * SLOTS;
   static constexpr uint32_t kChunks = D / 128;             // 128-byte K chunks of a K row
   static constexpr uint32_t kKChunkBytes = SLOTS * 8192u;  // one chunk of every slot (64 rows)
   static constexpr uint32_t kOffK = 0;
   static constexpr uint32_t kOffV = kOffK + kChunks * kKChunkBytes;
   static constexpr uint32_t kVSlotBytes = 64u * D;
-  static constexpr uint32_t kOffScales = kOffV + SLOTS * kVSlotBytes;  // [slot][k|v][64] floats
-  static constexpr uint32_t kOffQ = (kOffScales + SLOTS * 512u + 1023u) / 1024u * 1024u;
+  // V pages are loaded as rows of 64 bytes (64-byte swizzle): with 32-token
+  // pages a row holds two dims (2i: bytes 0-31, 2i + 1: bytes 32-63), which
+  // halves the TMA rows per page; the PV MMA reads the even dims at K offset
+  // 0 and the odd dims at K offset 32 into two accumulator regions.
+  static constexpr bool kVPair = P == 32;
+  static constexpr uint32_t kVRows = kVPair ? D / 2 : D;  // 64-byte rows per page
+  static constexpr uint32_t kOffScales = kOffV + SLOTS * kVSlotBytes;  // [scale slot][k|v][64] floats
+  static constexpr uint32_t kOffQ = (kOffScales + kScaleSlots * 512u + 1023u) / 1024u * 1024u;
   static constexpr uint32_t kQBytes = kChunks * kNQK * 128u;
   static constexpr uint32_t kPBufBytes = kNPV * 128u;  // [8 token chunks][kNPV rows][16 B]
   static constexpr uint32_t kOffP = kOffQ + kQBytes;
-  static constexpr uint32_t kOffStats = kOffP + 2 * kPBufBytes;  // [2][NC][alpha, 1/pscale]
-  static constexpr uint32_t kRedStride = kCH + 1;                // per softmax warp
-  static constexpr uint32_t kOffRed = kOffStats + 2 * NC * 8;    // [2][softmax warps][kCH + 1]
+  static constexpr uint32_t kOffStats = kOffP + 2 * kPBufBytes;  // [2][NC][alpha, 1/pscale] (fold)
+  static constexpr uint32_t kOffColP = kOffStats + 2 * NC * 8;   // [2][NC] float4 {cf, off, inv, alpha}
+  static constexpr uint32_t kOffRed = kOffColP + 2 * NC * 16;    // [2][softmax warps][32]
   // qpos[NC] (int64), then cf[NC] and the running max m[2][NC] (float)
-  static constexpr uint32_t kOffCol = (kOffRed + 2 * kSoftmaxWarps * kRedStride * 4 + 7) / 8 * 8;
+  static constexpr uint32_t kOffCol = kOffRed + 2 * kSoftmaxWarps * 32 * 4;
   static constexpr uint32_t kOffBar = (kOffCol + NC * 8 + NC * 4 + 2 * NC * 4 + 7) / 8 * 8;
-  // barriers: full[SLOTS], empty[SLOTS], s_ready[2], s_free[2], p_ready[2],
-  // p_free[2], stats_free[2], o_ready, o_free, mma_done
-  static constexpr uint32_t kBars = 2 * SLOTS + 10 + 3;
+  // barriers: full_k[SLOTS], empty_k[SLOTS], full_v[SLOTS], empty_v[SLOTS],
+  // empty_s[2 SLOTS], s_ready[2], s_free[2], p_ready[2], p_free[2],
+  // stats_free[2], o_ready, o_free, mma_done
+  static constexpr uint32_t kBars = 6 * SLOTS + 10 + 3;
   static constexpr uint32_t kOffMisc = kOffBar + kBars * 8;  // tmem address, abort flag
   static constexpr uint32_t kBytes = kOffMisc + 64;
   static constexpr uint32_t kDynamicBytes = kBytes + 1024;  // room to align the base
@@ -107,22 +155,26 @@ struct TcSmem {
   static constexpr uint32_t kTmemCols = kTmemUsed <= 32 ? 32 : kTmemUsed <= 64 ? 64 : kTmemUsed <= 128 ? 128
                                         : kTmemUsed <= 256 ? 256 : 512;
   static_assert(kTmemUsed <= 512, "TMEM columns");
-  static_assert(NC % (8 * NH) == 0 && kNQK <= 256, "columns: whole 8-column chunks per half");
+  static_assert(NC % (8 * NH) == 0 && kCH < 32 && kNQK <= 256, "columns: whole 8-column chunks per half");
   static_assert(SLOTS % 2 == 0, "tiles are slot pairs");
+  static_assert((P == 32 && D == 256) || P == 64, "V view: dim-paired 32-token pages at dim 256, or 64-token pages");
 };
 
 template <int D, int P, int NC, int SLOTS, int NH>
 __global__ void __maxnreg__((TcSmem<D, P, NC, SLOTS, NH>::kMaxRegs))
     decode_partial_tc_kernel(const __grid_constant__ DecodeParamsTc p) {
   using L = TcSmem<D, P, NC, SLOTS, NH>;
-  constexpr uint32_t NQK = L::kNQK, NPV = L::kNPV, CH = L::kCH;
+  constexpr uint32_t NQK = L::kNQK, NPV = L::kNPV, CH = L::kCH, SS = L::kScaleSlots;
   constexpr uint32_t kPps = 64 / P;  // pages per 64-token stage
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kOffBar);
-  uint64_t* full = bars;
-  uint64_t* empty = bars + SLOTS;
-  uint64_t* s_ready = bars + 2 * SLOTS;
+  uint64_t* full_k = bars;
+  uint64_t* empty_k = bars + SLOTS;
+  uint64_t* full_v = bars + 2 * SLOTS;
+  uint64_t* empty_v = bars + 3 * SLOTS;
+  uint64_t* empty_s = bars + 4 * SLOTS;  // SS of them
+  uint64_t* s_ready = bars + 6 * SLOTS;
   uint64_t* s_free = s_ready + 2;
   uint64_t* p_ready = s_ready + 4;
   uint64_t* p_free = s_ready + 6;
@@ -136,9 +188,10 @@ __global__ void __maxnreg__((TcSmem<D, P, NC, SLOTS, NH>::kMaxRegs))
   int64_t* col_qpos = reinterpret_cast<int64_t*>(smem + L::kOffCol);
   float* col_cf = reinterpret_cast<float*>(smem + L::kOffCol + NC * 8);
   // Running max per column (log2 units), double-buffered by tile parity: tile
-  // t reads buffer (t + 1) & 1 and column c's thread writes buffer t & 1.
+  // t reads buffer (t + 1) & 1 and writes buffer t & 1.
   float* col_m = col_cf + NC;
   float* stats = reinterpret_cast<float*>(smem + L::kOffStats);
+  float4* colp = reinterpret_cast<float4*>(smem + L::kOffColP);
   float* red = reinterpret_cast<float*>(smem + L::kOffRed);
 
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -149,9 +202,12 @@ __global__ void __maxnreg__((TcSmem<D, P, NC, SLOTS, NH>::kMaxRegs))
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < SLOTS; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
+      mbar_init(&full_k[s], 1);
+      mbar_init(&empty_k[s], 1);
+      mbar_init(&full_v[s], 1);
+      mbar_init(&empty_v[s], 1);
     }
+    for (int s = 0; s < int(SS); ++s) mbar_init(&empty_s[s], L::kSoftmaxWarps);
     for (int b = 0; b < 2; ++b) {
       mbar_init(&s_ready[b], 1);
       mbar_init(&s_free[b], L::kSoftmaxWarps);
@@ -165,10 +221,8 @@ __global__ void __maxnreg__((TcSmem<D, P, NC, SLOTS, NH>::kMaxRegs))
     *abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == L::kProducerWarp && lane == 0) {
-    tc::prefetch_tmap(&p.tm_k);
-    tc::prefetch_tmap(&p.tm_v);
-  }
+  if (warp == L::kProducerKWarp && lane == 0) tc::prefetch_tmap(&p.tm_k);
+  if (warp == L::kProducerVWarp && lane == 0) tc::prefetch_tmap(&p.tm_v);
   if (warp == L::kMmaWarp) {
     tc::tmem_alloc(const_cast<uint32_t*>(tmem_holder), L::kTmemCols);
     tc::tmem_relinquish();
@@ -186,17 +240,23 @@ __global__ void __maxnreg__((TcSmem<D, P, NC, SLOTS, NH>::kMaxRegs))
   const uint32_t ntiles = (nstages + 1) / 2;
   const uint32_t cols = p.qr;  // <= NC
   grid_dependency_wait();
+  if (threadIdx.x == 0) KVB_TC_MARK(0u, kTraceStart);
 
-  if (warp == L::kProducerWarp) {
-    // ---- TMA producer: stage g of the piece goes to slot g % SLOTS.
+  if (warp == L::kProducerKWarp || warp == L::kProducerVWarp) {
+    // ---- TMA producers: stage g of the piece goes to K (or V) slot
+    // g % SLOTS and, with its scales, to scale slot g % (2 SLOTS).
+    const bool kside = warp == L::kProducerKWarp;
     const uint64_t policy = l2_evict_first_policy();
     const uint32_t page_lo = max(pc.lo, (first_stage + pc.j0) * kStageTokens) / P;
     const uint32_t page_hi = (min(pc.hi, (first_stage + pc.j1) * kStageTokens) - 1) / P;
+    uint64_t* full = kside ? full_k : full_v;
+    uint64_t* empty = kside ? empty_k : empty_v;
     uint32_t g = 0;
     bool failed = false;
     for (; g < nstages && !failed; ++g) {
       const uint32_t slot = g % SLOTS, use = g / SLOTS;
-      if (!wait(&empty[slot], (use & 1u) ^ 1u, kStatusEmptyWaitTimeout, int(g))) {
+      if (!wait(&empty[slot], (use & 1u) ^ 1u, kStatusEmptyWaitTimeout, int(g)) ||
+          (kside && !wait(&empty_s[g % SS], ((g / SS) & 1u) ^ 1u, kStatusEmptyWaitTimeout, int(g)))) {
         failed = true;
         break;
       }
@@ -205,23 +265,29 @@ __global__ void __maxnreg__((TcSmem<D, P, NC, SLOTS, NH>::kMaxRegs))
       const bool mine = lane < kPps && pg >= page_lo && pg <= page_hi;
       const uint32_t phys = mine ? __ldg(p.table + pg) : 0u;
       const bool ok = mine && phys < p.pages;
-      if (__ballot_sync(0xffffffffu, mine && !ok) && lane == 0) atomicMax(&g_kvb_status, kStatusBadPage);
+      if (kside && __ballot_sync(0xffffffffu, mine && !ok) && lane == 0) atomicMax(&g_kvb_status, kStatusBadPage);
       const uint32_t nok = __popc(__ballot_sync(0xffffffffu, ok));
-      if (lane == 0) mbar_arrive_expect_tx(&full[slot], nok * (2u * P * D + 8u * P));
+      if (lane == 0) {
+        mbar_arrive_expect_tx(&full[slot], nok * (kside ? P * D + 8u * P : P * D));
+        if (kside && (g & 1u) == 0) KVB_TC_MARK(g / 2, kTraceCopyIssued);
+      }
       __syncwarp();
       if (ok) {
         const uint32_t unit = phys * p.kv_heads + pc.h;  // < 2^32 / (P * D): 32-bit extent
-        for (uint32_t c = 0; c < L::kChunks; ++c)
-          tc::tma_load_2d(smem + L::kOffK + c * L::kKChunkBytes + slot * 8192u + lane * P * 128u, &p.tm_k,
-                          int32_t(c * 128u), int32_t(unit * P), &full[slot], policy);
-        tc::tma_load_2d(smem + L::kOffV + slot * L::kVSlotBytes + lane * P * D, &p.tm_v, 0,
-                        int32_t(unit * D), &full[slot], policy);
-        float* sc = reinterpret_cast<float*>(smem + L::kOffScales + slot * 512u);
-        bulk_copy_g2s(sc + lane * P, p.k_scales + size_t(unit) * P, 4 * P, &full[slot], policy);
-        bulk_copy_g2s(sc + 64 + lane * P, p.v_scales + size_t(unit) * P, 4 * P, &full[slot], policy);
+        if (kside) {
+          for (uint32_t c = 0; c < L::kChunks; ++c)
+            tc::tma_load_2d(smem + L::kOffK + c * L::kKChunkBytes + slot * 8192u + lane * P * 128u, &p.tm_k,
+                            int32_t(c * 128u), int32_t(unit * P), &full[slot], policy);
+          float* sc = reinterpret_cast<float*>(smem + L::kOffScales + (g % SS) * 512u);
+          bulk_copy_g2s(sc + lane * P, p.k_scales + size_t(unit) * P, 4 * P, &full[slot], policy);
+          bulk_copy_g2s(sc + 64 + lane * P, p.v_scales + size_t(unit) * P, 4 * P, &full[slot], policy);
+        } else {
+          tc::tma_load_2d(smem + L::kOffV + slot * L::kVSlotBytes + lane * P * D, &p.tm_v, 0,
+                          int32_t(unit * L::kVRows), &full[slot], policy);
+        }
       }
     }
-    if (!failed) mark_empty_splits<D>(p, pc);
+    if (kside && !failed) mark_empty_splits<D>(p, pc);
     // Drain: copies of the last SLOTS stages may still be in flight.
     for (uint32_t s = g > SLOTS ? g - SLOTS : 0u; s < g; ++s) {
       volatile int no_abort = 0;
@@ -241,6 +307,9 @@ __global__ void __maxnreg__((TcSmem<D, P, NC, SLOTS, NH>::kMaxRegs))
       constexpr uint32_t kIdescQk = tc::idesc_i8(128, NQK);
       constexpr uint32_t kIdescPv = tc::idesc_i8(128, NPV);
       uint32_t qk = 0, pv = 0, spins = 0;
+#ifdef KVB_TC_TRACE
+      uint32_t seen = 0;  // which PV inputs of tile pv were seen ready (trace only)
+#endif
       unsigned long long idle_since = 0;
       while (pv < ntiles) {
         bool progressed = false;
@@ -248,7 +317,7 @@ __global__ void __maxnreg__((TcSmem<D, P, NC, SLOTS, NH>::kMaxRegs))
           const uint32_t b = qk & 1u, s0 = 2 * qk, nst = min(2u, nstages - s0);
           bool ready = mbar_test(&s_free[b], ((qk >> 1) & 1u) ^ 1u);
           for (uint32_t si = 0; si < nst && ready; ++si)
-            ready = mbar_test(&full[(s0 + si) % SLOTS], ((s0 + si) / SLOTS) & 1u);
+            ready = mbar_test(&full_k[(s0 + si) % SLOTS], ((s0 + si) / SLOTS) & 1u);
           if (ready) {
             tc::fence_after_sync();
             // 128 token rows: slots s0 and s0 + 1 are adjacent in every K
@@ -263,15 +332,29 @@ __global__ void __maxnreg__((TcSmem<D, P, NC, SLOTS, NH>::kMaxRegs))
                 tc::mma_i8(tm_s[b], a, bq, kIdescQk, c != 0 || kk != 0);
               }
             tc::commit(&s_ready[b]);
+            for (uint32_t si = 0; si < nst; ++si) tc::commit(&empty_k[(s0 + si) % SLOTS]);
+            KVB_TC_MARK(qk, kTraceQkIssued);
             ++qk;
             progressed = true;
           }
         }
         if (pv < qk) {
           const uint32_t b = pv & 1u;
-          if (mbar_test(&p_ready[b], (pv >> 1) & 1u) && mbar_test(o_free, (pv & 1u) ^ 1u)) {
+          const uint32_t s0 = 2 * pv, nst = min(2u, nstages - s0);
+          const bool p_in = mbar_test(&p_ready[b], (pv >> 1) & 1u);
+          const bool o_in = mbar_test(o_free, (pv & 1u) ^ 1u);
+          bool v_in = true;
+          for (uint32_t si = 0; si < nst && v_in; ++si)
+            v_in = mbar_test(&full_v[(s0 + si) % SLOTS], ((s0 + si) / SLOTS) & 1u);
+#ifdef KVB_TC_TRACE
+          if (p_in && !(seen & 1u)) KVB_TC_MARK(pv, kTracePReadySeen);
+          if (o_in && !(seen & 2u)) KVB_TC_MARK(pv, kTraceOFreeSeen);
+          if (v_in && !(seen & 4u)) KVB_TC_MARK(pv, kTraceVSeen);
+          seen |= (p_in ? 1u : 0u) | (o_in ? 2u : 0u) | (v_in ? 4u : 0u);
+#endif
+          const bool ready = p_in && o_in && v_in;
+          if (ready) {
             tc::fence_after_sync();
-            const uint32_t s0 = 2 * pv, nst = min(2u, nstages - s0);
             const uint8_t* pbuf = smem + L::kOffP + b * L::kPBufBytes;
             for (uint32_t h = 0; h < D / 128; ++h) {
               bool acc = false;
@@ -279,8 +362,9 @@ __global__ void __maxnreg__((TcSmem<D, P, NC, SLOTS, NH>::kMaxRegs))
                 const uint8_t* vslot = smem + L::kOffV + ((s0 + si) % SLOTS) * L::kVSlotBytes;
                 for (uint32_t pg = 0; pg < kPps; ++pg)
                   for (uint32_t kk = 0; kk < P / 32; ++kk) {
-                    const uint64_t a = tc::smem_desc(vslot + pg * P * D + h * 128u * P + kk * 32u, 16u, 8u * P,
-                                                     P == 32 ? tc::kSwizzle32 : tc::kSwizzle64);
+                    // Region h: dims 2i + h (dim-paired pages) or 128 h + i.
+                    const uint32_t off = L::kVPair ? h * 32u : h * 128u * 64u + kk * 32u;
+                    const uint64_t a = tc::smem_desc(vslot + pg * P * D + off, 16u, 512u, tc::kSwizzle64);
                     const uint32_t tok = si * 64u + pg * P + kk * 32u;  // token offset in the tile
                     const uint64_t bd = tc::smem_desc(pbuf + (tok / 16u) * (NPV * 16u), NPV * 16u, 128u,
                                                       tc::kSwizzleNone);
@@ -291,7 +375,11 @@ __global__ void __maxnreg__((TcSmem<D, P, NC, SLOTS, NH>::kMaxRegs))
             }
             tc::commit(o_ready);
             tc::commit(&p_free[b]);
-            for (uint32_t si = 0; si < nst; ++si) tc::commit(&empty[(s0 + si) % SLOTS]);
+            for (uint32_t si = 0; si < nst; ++si) tc::commit(&empty_v[(s0 + si) % SLOTS]);
+            KVB_TC_MARK(pv, kTracePvIssued);
+#ifdef KVB_TC_TRACE
+            seen = 0;
+#endif
             ++pv;
             progressed = true;
           }
@@ -301,6 +389,9 @@ __global__ void __maxnreg__((TcSmem<D, P, NC, SLOTS, NH>::kMaxRegs))
           idle_since = 0;
           continue;
         }
+        // Idle: back off briefly, so that the poll does not take issue slots
+        // from the softmax and fold warps of this SM sub-partition.
+        __nanosleep(64);
         if ((++spins & 63u) == 0) {
           if (*abort_flag) break;
           const unsigned long long now = global_ns();
@@ -323,19 +414,34 @@ __global__ void __maxnreg__((TcSmem<D, P, NC, SLOTS, NH>::kMaxRegs))
     // operand in the 128-byte-swizzled K-major layout [chunk][NQK rows][128 B].
     // Rows past 3 NC only feed TMEM columns that nothing reads.
     uint8_t* qt = smem + L::kOffQ;
-    for (uint32_t c = warp; c < NC; c += L::kSoftmaxWarps + L::kFoldWarps) {
-      constexpr uint32_t kPer = D / 32;  // dims per lane, contiguous
+    constexpr uint32_t kComputeWarps = L::kSoftmaxWarps + L::kFoldWarps;
+    constexpr uint32_t kColsPerWarp = (NC + kComputeWarps - 1) / kComputeWarps;
+    constexpr uint32_t kPer = D / 32;  // dims per lane, contiguous
+    // Every load of the warp's query rows is issued before any is used.
+    float4 qv[kColsPerWarp][kPer / 4];
+#pragma unroll
+    for (uint32_t k = 0; k < kColsPerWarp; ++k) {
+      const uint32_t c = warp + k * kComputeWarps;
       const bool valid = c < cols;
       const uint32_t r = valid ? c / p.group : 0, gq = valid ? c % p.group : 0;
       const float* qrow = p.q + (size_t(r) * p.q_heads + size_t(pc.h) * p.group + gq) * D + lane * kPer;
+#pragma unroll
+      for (uint32_t i = 0; i < kPer / 4; ++i)
+        qv[k][i] = valid ? __ldg(reinterpret_cast<const float4*>(qrow) + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (uint32_t k = 0; k < kColsPerWarp; ++k) {
+      const uint32_t c = warp + k * kComputeWarps;
+      if (c >= NC) break;
+      const bool valid = c < cols;
+      const uint32_t r = valid ? c / p.group : 0;
       float v[kPer];
 #pragma unroll
-      for (uint32_t i = 0; i < kPer; i += 4) {
-        const float4 f = valid ? __ldg(reinterpret_cast<const float4*>(qrow + i)) : make_float4(0.f, 0.f, 0.f, 0.f);
-        v[i] = f.x;
-        v[i + 1] = f.y;
-        v[i + 2] = f.z;
-        v[i + 3] = f.w;
+      for (uint32_t i = 0; i < kPer / 4; ++i) {
+        v[4 * i] = qv[k][i].x;
+        v[4 * i + 1] = qv[k][i].y;
+        v[4 * i + 2] = qv[k][i].z;
+        v[4 * i + 3] = qv[k][i].w;
       }
       float amax = 0.f;
 #pragma unroll
@@ -410,10 +516,14 @@ __global__ void __maxnreg__((TcSmem<D, P, NC, SLOTS, NH>::kMaxRegs))
       for (uint32_t t = 0; t < ntiles; ++t) {
         const uint32_t b = t & 1u;
         const bool got = wait(&s_ready[b], (t >> 1) & 1u, kStatusFullWaitTimeout, int(2 * t));
+        if (threadIdx.x == 0) KVB_TC_MARK(t, kTraceSoftmaxIn);
         tc::fence_after_sync();
         // Columns 3c + k of S^T hold digit k's dot of query column c (exact
-        // s32): x = dot0 + 256 dot1 + 65536 dot2 (the first two summed in
-        // s32, |dot1| < 2^22), then scaled by the token's K scale.
+        // s32, each below 2^22 in magnitude): x = dot0 + 256 dot1 + 65536
+        // dot2, then scaled by the token's K scale. Each dot becomes a float
+        // exactly without the conversion pipe: the bits of 1.5 * 2^23 + i
+        // are 0x4B400000 + i for |i| < 2^22, and subtracting 1.5 * 2^23 is
+        // exact.
         float x[CH];
 #pragma unroll
         for (uint32_t c8 = 0; c8 < CH; c8 += 8) {
@@ -426,22 +536,27 @@ __global__ void __maxnreg__((TcSmem<D, P, NC, SLOTS, NH>::kMaxRegs))
           const uint32_t* raw[3] = {r0, r1, r2};
 #pragma unroll
           for (uint32_t j = 0; j < 8; ++j) {
-            const int d0 = int(raw[(3 * j) / 8][(3 * j) % 8]);
-            const int d1 = int(raw[(3 * j + 1) / 8][(3 * j + 1) % 8]);
-            const int d2 = int(raw[(3 * j + 2) / 8][(3 * j + 2) % 8]);
-            x[c8 + j] = fmaf(float(d2), 65536.f, float(d0 + 256 * d1));
+            constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
+            const float f0 = __uint_as_float(raw[(3 * j) / 8][(3 * j) % 8] + 0x4B400000u) - kRound;
+            const float f1 = __uint_as_float(raw[(3 * j + 1) / 8][(3 * j + 1) % 8] + 0x4B400000u) - kRound;
+            const float f2 = __uint_as_float(raw[(3 * j + 2) / 8][(3 * j + 2) % 8] + 0x4B400000u) - kRound;
+            x[c8 + j] = fmaf(f2, 65536.f, fmaf(f1, 256.f, f0));
           }
         }
         tc::fence_before_sync();
         __syncwarp();
         if (lane == 0) mbar_arrive(&s_free[b]);
-        // This thread's token.
-        const uint32_t tok = (first_stage + pc.j0 + 2 * t) * kStageTokens + r;
-        const uint32_t slot = (2 * t + (r >> 6)) % SLOTS;
-        const float* sc = reinterpret_cast<const float*>(smem + L::kOffScales + slot * 512u);
-        const bool in_piece = got && (2 * t + (r >> 6)) < nstages && tok >= pc.lo && tok < pc.hi;
+        if (threadIdx.x == 0) KVB_TC_MARK(t, kTraceSmLoaded);
+        // This thread's token, its scales (then the scale slots are released).
+        const uint32_t s0 = 2 * t, nst = min(2u, nstages - s0);
+        const uint32_t tok = (first_stage + pc.j0 + s0) * kStageTokens + r;
+        const float* sc = reinterpret_cast<const float*>(smem + L::kOffScales + ((s0 + (r >> 6)) % SS) * 512u);
+        const bool in_piece = got && (s0 + (r >> 6)) < nstages && tok >= pc.lo && tok < pc.hi;
         const float ks = in_piece ? sc[r & 63] : 0.f;
         const float vs = in_piece ? sc[64 + (r & 63)] : 0.f;
+        __syncwarp();
+        if (lane == 0)
+          for (uint32_t si = 0; si < nst; ++si) mbar_arrive(&empty_s[(s0 + si) % SS]);
         if (all_visible) {
 #pragma unroll
           for (uint32_t j = 0; j < CH; ++j) x[j] = in_piece ? x[j] * ks : -INFINITY;
@@ -451,66 +566,99 @@ __global__ void __maxnreg__((TcSmem<D, P, NC, SLOTS, NH>::kMaxRegs))
           for (uint32_t j = 0; j < CH; ++j)
             x[j] = (in_piece && kp <= col_qpos[cbase + j]) ? x[j] * ks : -INFINITY;
         }
-        // Per-column tile max of x (and the tile's max |vscale|) over the 128
-        // tokens: the warp's max, then the four quadrant warps of the half.
-        float* rw = red + b * (L::kSoftmaxWarps * L::kRedStride);
+        // Warp max of every column (and of |vscale|) by reduce-scatter: after
+        // the five exchange steps lane j holds column j's max over the
+        // warp's 32 tokens (j = CH: the max |vscale|).
+        float v[16];
 #pragma unroll
-        for (uint32_t j = 0; j < CH; ++j) {
-          const float m = warp_max(x[j]);
-          if (lane == 0) rw[warp * L::kRedStride + j] = m;
+        for (uint32_t i = 0; i < 16; ++i) {
+          const float lo_v = i < CH ? x[i] : (i == CH ? fabsf(vs) : -INFINITY);
+          const float hi_v = i + 16 < CH ? x[i + 16] : (i + 16 == CH ? fabsf(vs) : -INFINITY);
+          const bool up = lane & 16u;
+          const float send = up ? lo_v : hi_v, keep = up ? hi_v : lo_v;
+          v[i] = fmaxf(keep, __shfl_xor_sync(0xffffffffu, send, 16));
         }
-        {
-          const float m = warp_max(fabsf(vs));
-          if (lane == 0) rw[warp * L::kRedStride + CH] = m;
+#pragma unroll
+        for (uint32_t w = 8; w >= 1; w >>= 1) {
+          const bool up = lane & w;
+#pragma unroll
+          for (uint32_t i = 0; i < w; ++i) {
+            const float send = up ? v[i] : v[i + w], keep = up ? v[i + w] : v[i];
+            v[i] = fmaxf(keep, __shfl_xor_sync(0xffffffffu, send, w));
+          }
         }
+        float* rw = red + b * (L::kSoftmaxWarps * 32);
+        rw[warp * 32 + lane] = v[0];
         named_barrier(2, 32 * L::kSoftmaxWarps);
-        float vsmax = 0.f;
+        if (threadIdx.x == 0) KVB_TC_MARK(t, kTraceSmReduced);
+        // Per-column scalars, once per column (lane j of the half's first
+        // quadrant warp): the tile max score tm, the new running max, alpha,
+        // and the power of two 2^sh that puts |P| <= exp2(tm - mnew) * vsmax
+        // in [2^13, 2^14) (kept a normal float); published as {cf, sh - msub,
+        // 2^-sh, alpha} for every thread, and {alpha, 1/pscale} for the fold.
+        if (qd == 0 && lane < CH) {
+          const uint32_t c = cbase + lane;
+          float tx = rw[(4 * hh) * 32 + lane], vsmax = rw[(4 * hh) * 32 + CH];
 #pragma unroll
-        for (uint32_t w = 0; w < 4; ++w) vsmax = fmaxf(vsmax, rw[w * L::kRedStride + CH]);
-        const bool room = wait(&p_free[b], ((t >> 1) & 1u) ^ 1u, kStatusFullWaitTimeout, int(2 * t)) &&
-                          wait(&stats_free[b], ((t >> 1) & 1u) ^ 1u, kStatusFullWaitTimeout, int(2 * t));
-        // P digits of this token: row 2c = low digit, 2c + 1 = high digit.
-        uint8_t* pt = smem + L::kOffP + b * L::kPBufBytes + (r / 16u) * (NPV * 16u) + (r & 15u);
-        float* st = stats + b * NC * 2;
-        const float* m_old = col_m + ((t + 1) & 1u) * NC;
-        float* m_cur = col_m + b * NC;
-#pragma unroll
-        for (uint32_t j = 0; j < CH; ++j) {
-          const uint32_t c = cbase + j;
-          float tx = rw[(4 * hh) * L::kRedStride + j];
-#pragma unroll
-          for (uint32_t w = 1; w < 4; ++w) tx = fmaxf(tx, rw[(4 * hh + w) * L::kRedStride + j]);
+          for (uint32_t w = 1; w < 4; ++w) {
+            tx = fmaxf(tx, rw[(4 * hh + w) * 32 + lane]);
+            vsmax = fmaxf(vsmax, rw[(4 * hh + w) * 32 + CH]);
+          }
           const float cf = col_cf[c];
-          const float tm = tx * cf;  // tile max score (log2 units), -inf if none visible
-          const float mo = m_old[c];
+          const float tm = tx * cf;  // -inf when no token of the tile is visible
+          const float mo = col_m[((t + 1) & 1u) * NC + c];
           const float mnew = fmaxf(mo, tm);
           const float msub = mnew == -INFINITY ? 0.f : mnew;
           const float alpha = mnew == -INFINITY ? 1.f : fast_exp2(mo - msub);
-          // |P| <= exp2(tm - mnew) * vsmax; the power of two 2^sh puts the
-          // bound in [2^13, 2^14) (kept a normal float) and rides in the
-          // exp2 argument: wp = w * 2^sh.
           const float bound = (tm == -INFINITY ? 0.f : fast_exp2(tm - msub)) * vsmax;
           const int xb = int((__float_as_uint(bound) >> 23) & 0xffu);
           const int sh = max(-126, min(126, 140 - xb));
-          const float wp = fast_exp2(fmaf(x[j], cf, float(sh) - msub));  // 0 where x = -inf
-          const float inv = __uint_as_float(uint32_t(127 - sh) << 23);   // 2^-sh
-          lp[j] = fmaf(wp, inv, lp[j] * alpha);
-          // u = rint(w vscale 2^sh), |u| < 2^14: low digit = its low byte,
-          // high digit = (u + 128) >> 8.
-          const int u = __float2int_rn(wp * vs);
+          const float inv = __uint_as_float(uint32_t(127 - sh) << 23);  // 2^-sh
+          colp[b * NC + c] = make_float4(cf, float(sh) - msub, inv, alpha);
+          col_m[b * NC + c] = mnew;
+          if (wait(&stats_free[b], ((t >> 1) & 1u) ^ 1u, kStatusFullWaitTimeout, int(2 * t))) {
+            stats[(b * NC + c) * 2] = alpha;
+            stats[(b * NC + c) * 2 + 1] = bound > 0.f ? inv : 1.f;
+          }
+        }
+        const bool room = wait(&p_free[b], ((t >> 1) & 1u) ^ 1u, kStatusFullWaitTimeout, int(2 * t));
+        named_barrier(2, 32 * L::kSoftmaxWarps);
+        if (threadIdx.x == 0) KVB_TC_MARK(t, kTraceSmParams);
+        // P digits of this token: row 2c = low digit, 2c + 1 = high digit of
+        // u = rint(w vscale 2^sh), |u| < 2^14: the low byte of u, and
+        // (u + 128) >> 8. fma(wp, vs, 1.5 * 2^23) rounds the product to the
+        // nearest integer (ties to even) in the low mantissa bits, whose bits
+        // are 0x4B400000 + u.
+        // Groups of four columns: their parameters are loaded before any of
+        // the group's digit stores, so that the loads are not held behind
+        // stores the compiler cannot prove disjoint.
+        uint8_t* pt = smem + L::kOffP + b * L::kPBufBytes + (r / 16u) * (NPV * 16u) + (r & 15u);
+#pragma unroll
+        for (uint32_t j4 = 0; j4 < CH; j4 += 4) {
+          float4 cp[4];
+#pragma unroll
+          for (uint32_t i = 0; i < 4; ++i) cp[i] = colp[b * NC + cbase + j4 + i];
+          int ub[4];
+#pragma unroll
+          for (uint32_t i = 0; i < 4; ++i) {
+            const float wp = fast_exp2(fmaf(x[j4 + i], cp[i].x, cp[i].y));  // w * 2^sh; 0 where x = -inf
+            lp[j4 + i] = fmaf(wp, cp[i].z, lp[j4 + i] * cp[i].w);
+            ub[i] = int(__float_as_uint(fmaf(wp, vs, 12582912.0f)));  // 0x4B400000 + u
+          }
           if (room) {
-            pt[(2 * c) * 16u] = uint8_t(u);
-            pt[(2 * c + 1) * 16u] = uint8_t((u + 128) >> 8);
-            if (r == c) {
-              st[2 * c] = alpha;
-              st[2 * c + 1] = bound > 0.f ? inv : 1.f;
-              m_cur[c] = mnew;
+#pragma unroll
+            for (uint32_t i = 0; i < 4; ++i) {
+              const uint32_t c = cbase + j4 + i;
+              pt[(2 * c) * 16u] = uint8_t(ub[i]);
+              pt[(2 * c + 1) * 16u] = uint8_t((ub[i] - int(0x4B400000u) + 128) >> 8);
             }
           }
         }
+        if (threadIdx.x == 0) KVB_TC_MARK(t, kTraceSmStored);
         tc::fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(&p_ready[b]);
+        if (threadIdx.x == 0) KVB_TC_MARK(t, kTraceSoftmaxOut);
       }
       // l over the 128 tokens (the four quadrant warps of the half), then one
       // (m, l) per query column.
@@ -519,14 +667,14 @@ __global__ void __maxnreg__((TcSmem<D, P, NC, SLOTS, NH>::kMaxRegs))
 #pragma unroll
       for (uint32_t j = 0; j < CH; ++j) {
         const float sum = warp_sum(lp[j]);
-        if (lane == 0) rw[warp * L::kRedStride + j] = sum;
+        if (lane == 0) rw[warp * 32 + j] = sum;
       }
       named_barrier(2, 32 * L::kSoftmaxWarps);
       if (qd == 0 && lane < CH && cbase + lane < cols) {
         const uint32_t j = lane, c = cbase + lane;
         float lsum = 0.f;
 #pragma unroll
-        for (uint32_t w = 0; w < 4; ++w) lsum += rw[(4 * hh + w) * L::kRedStride + j];
+        for (uint32_t w = 0; w < 4; ++w) lsum += rw[(4 * hh + w) * 32 + j];
         const float mr = col_m[((ntiles + 1) & 1u) * NC + c];  // written in the last tile
         const uint32_t row = c / p.group, gq = c % p.group;
         const size_t rh = size_t(row) * p.q_heads + size_t(pc.h) * p.group + gq;
@@ -535,8 +683,9 @@ __global__ void __maxnreg__((TcSmem<D, P, NC, SLOTS, NH>::kMaxRegs))
         out[1] = lsum;
       }
     } else {
-      // ---- fold: warp 4 NH + w = lane quadrant w % 4 (dims d = 32 (w % 4) +
-      // lane, + 128 h) x column half w / 4.
+      // ---- fold: warp 4 NH + w = lane quadrant w % 4 (TMEM lane dl = 32
+      // (w % 4) + lane: dims 2 dl + h with dim-paired pages, else 128 h + dl)
+      // x column half w / 4.
       const uint32_t fw = warp - L::kSoftmaxWarps;
       const uint32_t qd = fw & 3u, hh = fw >> 2;
       const uint32_t dl = 32 * qd + lane;
@@ -552,6 +701,7 @@ __global__ void __maxnreg__((TcSmem<D, P, NC, SLOTS, NH>::kMaxRegs))
         if (!wait(o_ready, t & 1u, kStatusFullWaitTimeout, int(2 * t)) ||
             !wait(&p_ready[b], (t >> 1) & 1u, kStatusFullWaitTimeout, int(2 * t)))
           break;
+        if (fw == 0 && lane == 0) KVB_TC_MARK(t, kTraceFoldIn);
         tc::fence_after_sync();
         const float* st = stats + b * NC * 2;
 #pragma unroll
@@ -574,6 +724,7 @@ __global__ void __maxnreg__((TcSmem<D, P, NC, SLOTS, NH>::kMaxRegs))
         if (lane == 0) {
           mbar_arrive(o_free);
           mbar_arrive(&stats_free[b]);
+          if (fw == 0) KVB_TC_MARK(t, kTraceFoldOut);
         }
       }
 #pragma unroll
@@ -584,7 +735,7 @@ __global__ void __maxnreg__((TcSmem<D, P, NC, SLOTS, NH>::kMaxRegs))
           const size_t rh = size_t(row) * p.q_heads + size_t(pc.h) * p.group + gq;
           float* out = p.part + (rh * p.split_stride + pc.slot) * (D + 2) + 2;
 #pragma unroll
-          for (uint32_t h = 0; h < D / 128; ++h) out[h * 128 + dl] = acc[h][j];
+          for (uint32_t h = 0; h < D / 128; ++h) out[L::kVPair ? 2 * dl + h : h * 128 + dl] = acc[h][j];
         }
       }
     }
