@@ -53,6 +53,9 @@ from pathlib import Path
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
+# Steps per group in the end-to-end leg: the call stream waits on the copy
+# streams once per group instead of once per step.
+E2E_GROUP = 50
 METRIC = "µs/decode-attention call and effective KV GB/s (% of HBM peak) at 64K ctx, 1–8 B200"
 WORKLOAD = dict(
     workload="cfg2: single-layer decode attention, 65,536 ctx",
@@ -514,12 +517,17 @@ def main():
     # ---- end to end through the public API: per step, one H2D copy of the
     # step's query, query positions and page table (packed in one pinned
     # host buffer, as a caller stages a step's inputs) into a device staging
-    # buffer, the call on those device copies, and one D2H read of the fp16
-    # output. As a serving loop would, the copies run on their own streams
-    # with two staging and two output buffers, so that step i's input copy
-    # and step i-1's output copy overlap the kernels of the neighbouring
-    # steps; events order every copy against the calls that use its buffer.
-    # All copies of the timed steps are inside the timed region (the streams
+    # buffer of its own, the call on those device copies, and one D2H read of
+    # the step's fp16 output. As a serving loop would, the copies run on
+    # their own streams and overlap the kernels: steps go in groups of
+    # E2E_GROUP, the inputs of group g+1 are copied while group g computes,
+    # and each step's output is read back as soon as its call is done. The
+    # call stream waits on the copy streams once per group (for that group's
+    # inputs, and for the read-back of the group that last used its output
+    # buffers), because each cross-stream wait in front of a call costs
+    # about 4 us on B200: it stops the next call's kernel from starting
+    # under the previous call's merge (programmatic dependent launch). All
+    # copies of the timed steps are inside the timed region (the streams
     # join before each stop event). Captured as graphs like the device run.
     q_bytes = layers[0].q.numel() * 4
     qpos_off = q_bytes
@@ -532,14 +540,18 @@ def main():
         buf[qpos_off:qpos_off + c.q_positions.numel() * 8].copy_(c.q_positions.cpu().view(torch.uint8))
         buf[table_off:].copy_(c.page_table.cpu().view(torch.uint8))
         host_in.append(buf)
-    staging = [torch.empty(packed_bytes, dtype=torch.uint8, device=device) for _ in range(2)]
-    staged_inputs = [[kvb.DeviceInput(st.data_ptr(), st.data_ptr() + qpos_off, c.k_positions,
-                                      st.data_ptr() + table_off, c.k, c.v, c.k_scales, c.v_scales)
-                      for c in layers] for st in staging]
-    dev_out = [torch.empty_like(out) for _ in range(2)]
-    host_out = [torch.empty(out.numel(), dtype=torch.float16).pin_memory() for _ in range(2)]
+    group = min(E2E_GROUP, bench.block)
+    # Two groups of per-step staging and output buffers, used alternately.
+    staging = [[torch.empty(packed_bytes, dtype=torch.uint8, device=device) for _ in range(group)]
+               for _ in range(2)]
+    staged_inputs = [[[kvb.DeviceInput(st.data_ptr(), st.data_ptr() + qpos_off, c.k_positions,
+                                       st.data_ptr() + table_off, c.k, c.v, c.k_scales, c.v_scales)
+                       for c in layers] for st in half] for half in staging]
+    dev_out = [[torch.empty_like(out) for _ in range(group)] for _ in range(2)]
+    host_out = [[torch.empty(out.numel(), dtype=torch.float16).pin_memory() for _ in range(group)]
+                for _ in range(2)]
     h2d_bytes = packed_bytes
-    d2h_bytes = host_out[0].numel() * 2
+    d2h_bytes = out.numel() * 2
     s_in = torch.cuda.Stream(device=device)
     s_out = torch.cuda.Stream(device=device)
     stream = bench.stream
@@ -548,28 +560,45 @@ def main():
         """Enqueue `count` pipelined steps from `stream` and join back to it."""
         s_in.wait_stream(stream)
         s_out.wait_stream(stream)
-        ev_in, ev_call, ev_out = [], [], []
-        for i in range(count):
-            b, j = i % 2, i % len(layers)
+        groups = (count + group - 1) // group
+        ev_in, ev_done, ev_read = [None] * groups, [None] * groups, [None] * groups
+
+        def steps_of(g):
+            return range(g * group, min(count, (g + 1) * group))
+
+        def copy_in(g):
             with torch.cuda.stream(s_in):
-                if i >= 2:
-                    s_in.wait_event(ev_call[i - 2])  # the call that read staging[b] is done
-                staging[b].copy_(host_in[j], non_blocking=True)
-                ev_in.append(torch.cuda.Event())
-                ev_in[i].record(s_in)
+                if g >= 2:
+                    s_in.wait_event(ev_done[g - 2])  # group g-2's calls have read staging[g % 2]
+                for i in steps_of(g):
+                    staging[g % 2][i - g * group].copy_(host_in[i % len(layers)], non_blocking=True)
+                ev_in[g] = torch.cuda.Event()
+                ev_in[g].record(s_in)
+
+        copy_in(0)
+        for g in range(groups):
+            if g + 1 < groups:
+                copy_in(g + 1)
+            half = g % 2
+            ev_call = []
             with torch.cuda.stream(stream):
-                stream.wait_event(ev_in[i])
-                if i >= 2:
-                    stream.wait_event(ev_out[i - 2])  # dev_out[b] has been read back
-                kvb.launch_attention_ex(shape, staged_inputs[b][j], scratch, m, l, n,
-                                        partitions=args.partitions, out_f16=dev_out[b])
-                ev_call.append(torch.cuda.Event())
-                ev_call[i].record(stream)
+                stream.wait_event(ev_in[g])
+                if g >= 2:
+                    stream.wait_event(ev_read[g - 2])  # dev_out[half] has been read back
+                for i in steps_of(g):
+                    k = i - g * group
+                    kvb.launch_attention_ex(shape, staged_inputs[half][k][i % len(layers)], scratch, m, l, n,
+                                            partitions=args.partitions, out_f16=dev_out[half][k])
+                    ev_call.append(torch.cuda.Event())
+                    ev_call[-1].record(stream)
+                ev_done[g] = ev_call[-1]
             with torch.cuda.stream(s_out):
-                s_out.wait_event(ev_call[i])
-                host_out[b].copy_(dev_out[b], non_blocking=True)
-                ev_out.append(torch.cuda.Event())
-                ev_out[i].record(s_out)
+                for i, ev in zip(steps_of(g), ev_call):
+                    k = i - g * group
+                    s_out.wait_event(ev)
+                    host_out[half][k].copy_(dev_out[half][k], non_blocking=True)
+                ev_read[g] = torch.cuda.Event()
+                ev_read[g].record(s_out)
         stream.wait_stream(s_in)
         stream.wait_stream(s_out)
 
@@ -579,7 +608,8 @@ def main():
     e2e = bench.timed(g_e2e.replay, bench.block)
     # The host copy of the last step's output must be that layer's result.
     last = bench.block - 1
-    e2e_out = host_out[last % 2].clone()
+    last_group = last // group
+    e2e_out = host_out[last_group % 2][last - last_group * group].clone()
     with torch.cuda.stream(stream):
         call(last % len(layers))
     torch.cuda.synchronize()
@@ -658,10 +688,11 @@ def main():
             "d2h_bytes_per_step": d2h_bytes,
             "us_per_call": round(e2e["per_call_ms"] * 1e3, 3),
             "how": "public API launch_attention_ex; every step one H2D copy of that step's Q, q_positions and page "
-                   "table (packed in one pinned host buffer) and one D2H copy of the fp16 output, on two copy "
-                   "streams with double-buffered staging and outputs so that they overlap the neighbouring steps' "
-                   "kernels (all inside the timed region), CUDA-graph replayed; the KV cache is resident device "
-                   "state; per GPU at N > 1",
+                   "table (packed in one pinned host buffer) into a staging buffer of its own and one D2H copy of "
+                   f"its fp16 output, on two copy streams that overlap the kernels: steps in groups of {group}, "
+                   "inputs of the next group copied while a group computes, each output read back when its call "
+                   "is done, one cross-stream wait per group on the call stream (all inside the timed region), "
+                   "CUDA-graph replayed; the KV cache is resident device state; per GPU at N > 1",
         },
         "gpu_launches": 2 * head["calls"],
         "clocks": {k: clocks[k] for k in ("sm_mhz", "sm_max_mhz", "reasons", "samples")},
