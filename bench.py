@@ -664,14 +664,16 @@ def main():
                       f"({q_local} query heads each), no collective" if world > 1 else "single GPU"),
             launch="CUDA-graph replay of launch_attention_ex (partial kernel, then LSE merge kernel with the fp16 "
                    "epilogue; programmatic dependent launch between them)",
-            compute="QK: int8 mma.sync m16n8k32 on raw K codes x 3 int8 limbs of Q (exact s32); "
-                    "PV: int8 mma.sync m16n8k32 on raw V codes x 2 int8 limbs of 14-bit fixed-point "
-                    "P = softmax weight x V scale (exact s32), fp32 accumulation",
+            compute="QK: int8 mma.sync m16n8k32 on raw K codes x 3 int8 digits of 22-bit fixed-point Q "
+                    "(exact s32); PV: int8 mma.sync m16n8k32 on raw V codes x 3 int8 digits of 22-bit "
+                    "fixed-point P = softmax weight x V scale (exact s32), fp32 accumulation; the 4 query "
+                    "columns of a KV head in lane pairs that split the digits (one m-tile each)",
         ),
         "roofline": {
             "bound": "hbm",
-            "kernel": ("kvb::decode_partial_tc_kernel<128,64,8,6> (tcgen05, TMEM accumulators)"
-                       if args.kernel == "tcgen05" else "kvb::decode_partial_kernel<128,1,6,false,false>"),
+            "kernel": ("kvb::decode_partial_tc_kernel<128,64,8,6,1> (tcgen05, TMEM accumulators)"
+                       if args.kernel == "tcgen05" else "kvb::decode_partial_kernel<128,0,6,false,false> "
+                       "(warp-level int8 MMA, four-column layout)"),
             "achieved": round(achieved, 2),
             "peak": peak,
             "unit": "GB/s",

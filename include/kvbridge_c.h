@@ -201,6 +201,13 @@ int kvb_decode_kernel(void);
  * and clears them. Other builds return KVB_EINVAL. */
 int kvb_debug_read_tc_trace(unsigned long long* out, size_t count);
 
+/* Per-CTA timeline of the warp-level partial kernels, in libraries built
+ * with the trace flag: copies up to `count` stamps [1024 CTAs][16 events]
+ * of the latest launches (entry and exit on the global timer in ns, the
+ * rest SM clock stamps; the event list is in decode_tma.cuh, CtaTraceEvent)
+ * and clears them. Other builds return KVB_EINVAL. */
+int kvb_debug_read_cta_trace(unsigned long long* out, size_t count);
+
 /* Decode call that allocates nothing. It has no counterpart in the
  * reference. kvb_launch_attention_ex needs a caller-provided scratch buffer
  * of scratch_elements(shape) floats; callers that cannot call cudaMalloc

@@ -163,15 +163,21 @@ FastVariant make_variant(bool small_pages) {
 FastVariant fast_variant(uint32_t dim, uint32_t nt, uint32_t page_tokens, bool batched) {
   const bool small = page_tokens < kvb::kStageTokens;
   if (batched) {
+    if (dim == 128 && nt == 0) return make_variant<128, 0, 5, true>(small);
     if (dim == 128 && nt == 1) return make_variant<128, 1, 5, true>(small);
     if (dim == 128 && nt == 2) return make_variant<128, 2, 4, true>(small);
+    if (dim == 64 && nt == 0) return make_variant<64, 0, 8, true>(small);
     if (dim == 64 && nt == 1) return make_variant<64, 1, 8, true>(small);
     if (dim == 64 && nt == 2) return make_variant<64, 2, 7, true>(small);
+    if (dim == 256 && nt == 0) return make_variant<256, 0, 4, true>(small);
     if (dim == 256 && nt == 1) return make_variant<256, 1, 4, true>(small);
     return FastVariant{};
   }
+  if (dim == 128 && nt == 0) return make_variant<128, 0, 6, false>(small);
   if (dim == 128 && nt == 1) return make_variant<128, 1, 6, false>(small);
+  if (dim == 64 && nt == 0) return make_variant<64, 0, 8, false>(small);
   if (dim == 64 && nt == 1) return make_variant<64, 1, 8, false>(small);
+  if (dim == 256 && nt == 0) return make_variant<256, 0, 6, false>(small);
   if (dim == 256 && nt == 1) return make_variant<256, 1, 6, false>(small);
   return FastVariant{};
 }
@@ -256,19 +262,28 @@ std::atomic<int> g_decode_kernel{0};
 
 uint32_t query_rows(const Shape& s) { return s.rows * (s.q_heads / s.kv_heads); }
 
-// Single sequence: a CTA takes 8 query columns of one KV head (nt = 1);
-// more columns (rows x group up to 64, e.g. the reference's native 8 rows x
-// group 6) are cut into column groups, one CTA per group and KV range, whose
-// repeated page reads hit L2. Measured at 64K tokens with 16 columns, two
-// 8-column groups (51.8 us) beat one 16-column CTA (69.3 us), whose PV
-// accumulators spill. (The batched path, without column groups, still takes
-// up to 16 columns in one CTA.)
+// Single sequence: a CTA takes 8 query columns of one KV head (nt = 1), or at
+// most 4 in the four-column layout (nt = 0: one query row of a 32/8-head
+// model, as at BASELINE cfg1/cfg2); more columns (rows x group up to 64,
+// e.g. the reference's native 8 rows x group 6) are cut into column groups,
+// one CTA per group and KV range, whose repeated page reads hit L2. Measured
+// at 64K tokens with 16 columns, two 8-column groups (51.8 us) beat one
+// 16-column CTA (69.3 us), whose PV accumulators spill. (The batched path,
+// without column groups, still takes up to 16 columns in one CTA.)
 struct ColumnPlan {
   uint32_t nt, groups;
 };
 constexpr uint32_t kMaxQueryColumns = 64;
 
-ColumnPlan column_plan(uint32_t /*dim*/, uint32_t qrows) { return ColumnPlan{1, (qrows + 7) / 8}; }
+ColumnPlan column_plan(uint32_t /*dim*/, uint32_t qrows) {
+  return qrows <= 4 ? ColumnPlan{0, 1} : ColumnPlan{1, (qrows + 7) / 8};
+}
+
+// Query columns of a CTA for `nt` (decode_tma.cuh, cta_cols).
+uint32_t columns_of(uint32_t nt) { return nt == 0 ? 4u : 8u * nt; }
+
+// Batched: one CTA takes a sequence's whole query group (at most 16).
+uint32_t batched_nt(uint32_t group) { return group <= 4 ? 0u : (group + 7) / 8; }
 
 // Tensor-core geometry. `max_rows`: query columns per KV head the caller can
 // cut into column groups (single sequence), or one group's worth (batched).
@@ -544,7 +559,7 @@ kvb::DecodeParamsGather single_params(const Shape& s, const DeviceInput& in, uin
   prm.max_tokens = s.tokens;
   const ColumnPlan plan = column_plan(s.dim, query_rows(s));
   prm.col_groups = plan.groups;
-  prm.group_cols = 8 * plan.nt;
+  prm.group_cols = columns_of(plan.nt);
   prm.ctas = parts * s.kv_heads * plan.groups;
   prm.total_stages = uint64_t(prm.seg_stages) * s.kv_heads;
   prm.score_scale = s.scale;
@@ -601,7 +616,7 @@ void launch_single_partials(const Shape& s, const DeviceInput& in, uint32_t part
       return;
     }
   }
-  fast_variant(s.dim, prm.group_cols / 8, s.page_tokens, false).launch(prm, stream);
+  fast_variant(s.dim, prm.group_cols == 4 ? 0 : prm.group_cols / 8, s.page_tokens, false).launch(prm, stream);
 }
 
 }  // namespace
@@ -716,7 +731,7 @@ const char* batch_shape_error(const BatchShape& s) noexcept {
 size_t batch_workspace_bytes(const BatchShape& s) {
   if (const char* e = batch_shape_error(s)) throw std::invalid_argument(e);
   const uint32_t group = s.q_heads / s.kv_heads;
-  const FastVariant v = fast_variant(s.dim, (group + 7) / 8, s.page_tokens, true);
+  const FastVariant v = fast_variant(s.dim, batched_nt(group), s.page_tokens, true);
   const uint64_t slots = uint64_t(batched_ctas(v)) + uint64_t(s.batch) * s.kv_heads;
   return size_t(slots * group * (s.dim + 2) * sizeof(float));
 }
@@ -740,7 +755,7 @@ void launch_attention_batched(const BatchShape& s, const BatchInput& in, void* w
   if (workspace_bytes < batch_workspace_bytes(s))
     throw std::invalid_argument("workspace smaller than batch_workspace_bytes(shape)");
   const uint32_t group = s.q_heads / s.kv_heads;
-  const FastVariant v = fast_variant(s.dim, (group + 7) / 8, s.page_tokens, true);
+  const FastVariant v = fast_variant(s.dim, batched_nt(group), s.page_tokens, true);
   kvb::DecodeParamsGather prm{};
   prm.q = in.q;
   prm.table = in.block_table;
@@ -763,7 +778,7 @@ void launch_attention_batched(const BatchShape& s, const BatchInput& in, void* w
   prm.max_tokens = s.max_tokens;
   prm.ctas = batched_ctas(v);
   prm.col_groups = 1;
-  prm.group_cols = 8 * ((group + 7) / 8);
+  prm.group_cols = columns_of(batched_nt(group));
   prm.score_scale = s.scale;
   prm.wait_limit_ns = wait_limit_ns();
   prm.fault_stage = take_skip_stage();
@@ -901,6 +916,22 @@ cudaError_t read_tc_trace(unsigned long long* out, size_t count, bool* available
   if (code != cudaSuccess) return code;
   static const unsigned long long zeros[kvb::kTraceCtas][kvb::kTraceTiles][kvb::kTraceEvents] = {};
   return cudaMemcpyToSymbol(kvb::g_tc_trace, zeros, sizeof(zeros));
+#else
+  (void)out;
+  (void)count;
+  *available = false;
+  return cudaSuccess;
+#endif
+}
+
+cudaError_t read_cta_trace(unsigned long long* out, size_t count, bool* available) noexcept {
+#ifdef KVB_TC_TRACE
+  *available = true;
+  const size_t all = size_t(kvb::kCtaTraceCtas) * kvb::kCtaTraceEvents;
+  cudaError_t code = cudaMemcpyFromSymbol(out, kvb::g_cta_trace, std::min(count, all) * sizeof(unsigned long long));
+  if (code != cudaSuccess) return code;
+  static const unsigned long long zeros[kvb::kCtaTraceCtas][kvb::kCtaTraceEvents] = {};
+  return cudaMemcpyToSymbol(kvb::g_cta_trace, zeros, sizeof(zeros));
 #else
   (void)out;
   (void)count;

@@ -100,6 +100,45 @@ struct DecodeParamsGather : DecodeParams {
 template <bool SMALL_PAGES>
 using KernelParams = typename std::conditional<SMALL_PAGES, DecodeParamsGather, DecodeParams>::type;
 
+// Per-CTA timeline of these kernels (trace builds only, -DKVB_TC_TRACE): for
+// the first kCtaTraceCtas CTAs of the latest launch, g_cta_trace[cta][event]
+// with the events below. Entry and exit also carry the global timer (ns), so
+// that CTAs on different SMs share one time axis; the other events are SM
+// clock stamps (clock64), exact within a CTA.
+constexpr int kCtaTraceCtas = 1024;
+constexpr int kCtaTraceEvents = 16;
+enum CtaTraceEvent : int {
+  kCtaEntryNs = 0,      // thread 0 entered (global timer)
+  kCtaEntryClk = 1,     // thread 0 entered (clock64)
+  kCtaSm = 2,           // SM id
+  kCtaDepWaitDone = 3,  // consumer warp 0 passed the dependency wait on the preceding grid
+  kCtaFirstCopy = 4,    // producer armed its first stage (copies issued right after)
+  kCtaLastCopy = 5,     // producer armed its last stage
+  kCtaFirstStage = 6,   // the CTA's first stage had landed (its consumer's wait returned)
+  kCtaWarpDone = 7,     // + w: consumer warp w finished its last stage (w < 4)
+  kCtaPartialDone = 11, // partials written, the consumers' exit (clock64)
+  kCtaExitNs = 12,      // the same moment on the global timer
+  kCtaStages = 13,      // stages the producer issued
+  kCtaLastStage = 14,   // the CTA's last stage had landed (its consumer's wait returned)
+};
+#ifdef KVB_TC_TRACE
+__device__ unsigned long long g_cta_trace[kCtaTraceCtas][kCtaTraceEvents];
+#define KVB_CTA_MARK(event, value)                                          \
+  do {                                                                      \
+    if (blockIdx.x < kCtaTraceCtas) g_cta_trace[blockIdx.x][(event)] = (value); \
+  } while (0)
+#else
+#define KVB_CTA_MARK(event, value) \
+  do {                             \
+  } while (0)
+#endif
+
+__device__ __forceinline__ unsigned long long sm_id() {
+  uint32_t id;
+  asm volatile("mov.u32 %0, %%smid;" : "=r"(id));
+  return id;
+}
+
 constexpr int kConsumerWarps = 4;
 constexpr int kProducerWarp = kConsumerWarps;
 constexpr int kDecodeThreads = 32 * (kConsumerWarps + 1);
@@ -131,10 +170,22 @@ __device__ __forceinline__ uint32_t v_page_pitch(uint32_t dim, uint32_t page_tok
 // landed and every stage has been read (the consumers meet at a barrier
 // first); the freed shared memory holds one more stage. A batched CTA may
 // already be loading its next piece and keeps a buffer of its own.
+// Query columns of a CTA. NT >= 1: 8 NT columns, column grp + 8 nt of a
+// warp's MMA fragments in lane (grp, tig). NT = 0: the four-column layout of
+// query groups of at most 4 columns (one query row of a 32/8- or 64/16-head
+// model): column grp & 3 in lanes grp and grp + 4, which split the int8
+// digits of its query and probability rows between them, so that QK needs
+// one m-tile instead of two and P carries three digits instead of two.
+template <int NT>
+constexpr int cta_cols() { return NT == 0 ? 4 : 8 * NT; }
+// Column slots of the per-thread state arrays (one in the four-column layout).
+template <int NT>
+constexpr int nt_slots() { return NT == 0 ? 1 : NT; }
+
 template <int D, int NT, int STAGES, bool RING_COMBINE>
 struct DecodeSmem {
   static constexpr uint32_t kRing = STAGES * StageLayout<D>::kBytes;
-  static constexpr uint32_t kCols = 8 * NT;
+  static constexpr uint32_t kCols = 8 * nt_slots<NT>();  // four-column layout: 4 of 8 used
   static constexpr uint32_t kPitch = D + 4;  // floats; breaks bank aliasing of columns
   static constexpr uint32_t kCombine = kConsumerWarps * kCols * kPitch * 4;
   static_assert(!RING_COMBINE || kCombine <= kRing, "combine buffer larger than the ring");
@@ -339,7 +390,7 @@ __device__ void prefetch_query_lines(const DecodeParams& p, const Piece& pc) {
   const uint32_t lane = threadIdx.x & 31;
   if (pc.j1 <= pc.j0) return;
   constexpr uint32_t kLines = D * 4 / 128;  // 128-byte lines of one fp32 query row
-  for (uint32_t i = lane; i < 8u * NT * kLines; i += 32) {
+  for (uint32_t i = lane; i < uint32_t(cta_cols<NT>()) * kLines; i += 32) {
     const uint32_t col = pc.col0 + i / kLines;
     if (col >= p.qr) break;
     const uint32_t r = col / p.group, g = col % p.group;
@@ -474,6 +525,8 @@ __device__ void produce_small_pages(const DecodeParamsGather& p, const Piece& on
         // Tag protocol as in produce().
         tags[slot] = g;
         mbar_arrive_expect_tx(&full[slot], okpages * kv_bytes);
+        if (g == 0) KVB_CTA_MARK(kCtaFirstCopy, clock64());
+        KVB_CTA_MARK(kCtaLastCopy, clock64());
       }
       __syncwarp();
       if (gather) {
@@ -520,6 +573,7 @@ __device__ void produce_small_pages(const DecodeParamsGather& p, const Piece& on
     x = piece_end_stage(p, pc, x);
   }
   if (!BATCHED && !failed) mark_empty_splits<D>(p, only);
+  if (lane == 0) KVB_CTA_MARK(kCtaStages, g);
   drain_copies<STAGES>(full, g, p.wait_limit_ns);
 }
 
@@ -618,6 +672,8 @@ __device__ void produce(const DecodeParams& p, const Piece& only, uint8_t* ring,
           tags[slot] = g;
           const uint32_t stage_lanes = (pps == 4 ? 0xffffu : (1u << (4 * pps)) - 1u) << (4 * pps * sb);
           mbar_arrive_expect_tx(&full[slot], __popc(okmask & stage_lanes) * page_bytes);
+          if (g == 0) KVB_CTA_MARK(kCtaFirstCopy, clock64());
+          KVB_CTA_MARK(kCtaLastCopy, clock64());
         }
         __syncwarp();
         if (ok && lane_stage == sb)
@@ -629,6 +685,7 @@ __device__ void produce(const DecodeParams& p, const Piece& only, uint8_t* ring,
     x = piece_end_stage(p, pc, x);
   }
   if (!BATCHED && !failed) mark_empty_splits<D>(p, only);
+  if (lane == 0) KVB_CTA_MARK(kCtaStages, g);
   drain_copies<STAGES>(full, g, p.wait_limit_ns);
 }
 
@@ -637,17 +694,21 @@ __device__ void produce(const DecodeParams& p, const Piece& only, uint8_t* ring,
 
 template <int D, int NT>
 struct WarpState {
-  float acc[D / 8][NT][2];  // O fragments: column grp + 8 nt, dims 8 dn + 2 tig + e
-  float m[NT];              // running max (log2 units) of column grp + 8 nt
-  float l[NT];              // thread-partial denominator of that column
+  // O fragments: column grp + 8 nt, dims 8 dn + 2 tig + e. Four-column
+  // layout: lanes grp and grp + 4 each hold a part of column grp & 3 (their
+  // digit rows' sums), added together when the warp flushes.
+  float acc[D / 8][nt_slots<NT>()][2];
+  float m[nt_slots<NT>()];  // running max (log2 units) of the column
+  float l[nt_slots<NT>()];  // thread-partial denominator of that column
 };
 
 // QK m-tiles: rows (column c, limb k) are numbered 3 c + k (c < 8 NT taken
 // as 8 nt + row-in-group), eight to a half-tile: m-tile mt holds row sets
 // 2 mt (rows 0-7) and 2 mt + 1 (rows 8-15). With NT = 1 the last half-tile
-// is zero.
+// is zero. Four-column layout: one m-tile, rows grp < 4 limb 0 of column
+// grp, rows 8 + grp limb 1, rows 4 + c limb 2 of column c, rows 12-15 zero.
 template <int NT>
-constexpr int qk_tiles() { return (3 * NT + 1) / 2; }
+constexpr int qk_tiles() { return NT == 0 ? 1 : (3 * NT + 1) / 2; }
 
 // Per-piece query operands of one warp: the A fragments of the QK MMA for
 // every k-step (k-step j covers dims 64*(j/2) + 16*tig + 8*(j%2) + [0,8) for
@@ -656,8 +717,8 @@ constexpr int qk_tiles() { return (3 * NT + 1) / 2; }
 template <int D, int NT>
 struct QueryFrags {
   uint32_t a[qk_tiles<NT>()][D / 32][4];
-  float cf[NT];      // score factor of column grp + 8 nt (log2 units)
-  int64_t qpos[NT];  // query position of that column
+  float cf[nt_slots<NT>()];      // score factor of the thread's column (log2 units)
+  int64_t qpos[nt_slots<NT>()];  // query position of that column
 };
 
 // Loads the piece's query operands and, for a single sequence, returns
@@ -669,19 +730,20 @@ struct QueryFrags {
 template <int D, int NT, bool BATCHED>
 __device__ __forceinline__ bool load_query(const DecodeParams& p, const Piece& pc,
                                            uint32_t last_token, QueryFrags<D, NT>& qf) {
+  constexpr int kNt = nt_slots<NT>();
   const uint32_t lane = threadIdx.x & 31, grp = lane >> 2, tig = lane & 3;
-  // Visibility: lane j < 8 * NT checks the row of column col0 + j.
+  // Visibility: lane j < cta_cols checks the row of column col0 + j.
   int64_t kp_last = 0, qp_own = INT64_MAX;
   if (!BATCHED) {
     kp_last = __ldg(p.k_positions + last_token);
     const uint32_t ocol = pc.col0 + lane;
-    if (lane < 8u * NT && ocol < p.qr) qp_own = __ldg(p.q_positions + ocol / p.group);
+    if (lane < uint32_t(cta_cols<NT>()) && ocol < p.qr) qp_own = __ldg(p.q_positions + ocol / p.group);
   }
-  float vals[NT][D / 64][16];
-  int64_t qp[NT];
+  float vals[kNt][D / 64][16];
+  int64_t qp[kNt];
 #pragma unroll
-  for (int nt = 0; nt < NT; ++nt) {
-    const uint32_t col = pc.col0 + 8 * nt + grp;
+  for (int nt = 0; nt < kNt; ++nt) {
+    const uint32_t col = pc.col0 + (NT == 0 ? (grp & 3u) : 8 * nt + grp);
     const bool valid = col < p.qr;
     const uint32_t r = valid ? col / p.group : 0, g = valid ? col % p.group : 0;
     const uint32_t row = !BATCHED ? r : pc.b;
@@ -701,7 +763,7 @@ __device__ __forceinline__ bool load_query(const DecodeParams& p, const Piece& p
     qp[nt] = (!BATCHED && valid) ? __ldg(p.q_positions + r) : INT64_MAX;
   }
 #pragma unroll
-  for (int nt = 0; nt < NT; ++nt) {
+  for (int nt = 0; nt < kNt; ++nt) {
     float amax = 0.f;
 #pragma unroll
     for (int c = 0; c < D / 64; ++c)
@@ -738,12 +800,20 @@ __device__ __forceinline__ bool load_query(const DecodeParams& p, const Piece& p
           const uint32_t limb[3] = {__byte_perm(a, b, 0x5410) ^ 0x80808080u,
                                     __byte_perm(a, b, 0x7632) ^ 0x80808080u,
                                     __byte_perm(c2, d2, 0x5410) ^ 0x80808080u};
-          // Row set 3 nt + k of the A fragment: a0/a2 (rows 0-7, k-lo/hi),
-          // a1/a3 (rows 8-15).
+          if constexpr (NT == 0) {
+            // a0/a2 (row grp): limb 0, or limb 2 in lanes grp >= 4; a1/a3
+            // (row grp + 8): limb 1, or zero.
+            const bool upper = grp >= 4;
+            qf.a[0][2 * c + jj][2 * half] = upper ? limb[2] : limb[0];
+            qf.a[0][2 * c + jj][1 + 2 * half] = upper ? 0u : limb[1];
+          } else {
+            // Row set 3 nt + k of the A fragment: a0/a2 (rows 0-7, k-lo/hi),
+            // a1/a3 (rows 8-15).
 #pragma unroll
-          for (int k = 0; k < 3; ++k) {
-            const int rs = 3 * nt + k;
-            qf.a[rs / 2][2 * c + jj][(rs % 2) + 2 * half] = limb[k];
+            for (int k = 0; k < 3; ++k) {
+              const int rs = 3 * nt + k;
+              qf.a[rs / 2][2 * c + jj][(rs % 2) + 2 * half] = limb[k];
+            }
           }
         }
       }
@@ -751,7 +821,7 @@ __device__ __forceinline__ bool load_query(const DecodeParams& p, const Piece& p
     qf.cf[nt] = p.score_scale * kLog2e * __uint_as_float(uint32_t(127 + e - 22) << 23);
     qf.qpos[nt] = qp[nt];
   }
-  if (3 * NT % 2 == 1) {
+  if constexpr (NT != 0 && 3 * NT % 2 == 1) {
 #pragma unroll
     for (int j = 0; j < D / 32; ++j) {
       qf.a[qk_tiles<NT>() - 1][j][1] = 0u;
@@ -770,6 +840,7 @@ __device__ __forceinline__ void consume_stage(const DecodeParams& p, const uint8
                                               bool all_visible, const QueryFrags<D, NT>& qf,
                                               WarpState<D, NT>& ws) {
   constexpr int kQk = qk_tiles<NT>();
+  constexpr int kNt = nt_slots<NT>();
   const uint32_t lane = threadIdx.x & 31, grp = lane >> 2, tig = lane & 3;
   const uint8_t* sk = st + StageLayout<D>::kK;
   const uint8_t* sv = st + StageLayout<D>::kV;
@@ -779,7 +850,7 @@ __device__ __forceinline__ void consume_stage(const DecodeParams& p, const uint8
   // ---- S = Q K^T. N-tile j holds tokens 16*(n/2) + 2j + n%2 (n = 0..7): the
   //      thread supplies the K row of token n = grp and gets back columns
   //      n = 2 tig + e, i.e. tokens 16 tig + 2 j + e (t = 2 j + e).
-  float sc[NT][16];
+  float sc[kNt][16];
   // K rows are read one n-tile ahead of the MMAs that use them; the compiler
   // fence after each read keeps it from hoisting further (register pressure).
   uint4 kw[2][D / 64];
@@ -811,18 +882,32 @@ __device__ __forceinline__ void consume_stage(const DecodeParams& p, const uint8
         imma_16832(acc[mt], a1[0], a1[1], a1[2], a1[3], k4.z, k4.w);
       }
     }
-    // Limb k of column grp + 8 nt is row set 3 nt + k: C rows 0-7 (c0, c1) or
-    // 8-15 (c2, c3) of m-tile (3 nt + k) / 2. Limb dots are exact integers
-    // (|dot| < 2^21); combine in fp32.
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt)
+    if constexpr (NT == 0) {
+      // Rows grp (c0, c1) and grp + 8 (c2, c3): limbs 0 and 1 of the column
+      // in lanes grp < 4 (l0 + 256 l1, exact in s32: |dot| <= 2^22 at dim
+      // 256), limb 2 in lanes grp >= 4 (its second row is zero). The lane
+      // pair adds the two parts (the same sum in both lanes: fp32 addition
+      // is commutative).
+      const float wgt = grp >= 4 ? 65536.f : 1.f;
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
-        const int r0 = 3 * nt, r1 = 3 * nt + 1, r2 = 3 * nt + 2;
-        const int d0 = acc[r0 / 2][2 * (r0 % 2) + e], d1 = acc[r1 / 2][2 * (r1 % 2) + e];
-        const int d2 = acc[r2 / 2][2 * (r2 % 2) + e];
-        sc[nt][2 * j + e] = fmaf(float(d2), 65536.f, fmaf(float(d1), 256.f, float(d0)));
+        const float part = float(acc[0][e] + 256 * acc[0][2 + e]) * wgt;
+        sc[0][2 * j + e] = part + __shfl_xor_sync(0xffffffffu, part, 16);
       }
+    } else {
+      // Limb k of column grp + 8 nt is row set 3 nt + k: C rows 0-7 (c0, c1)
+      // or 8-15 (c2, c3) of m-tile (3 nt + k) / 2. Limb dots are exact
+      // integers (|dot| < 2^21); combine in fp32.
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int r0 = 3 * nt, r1 = 3 * nt + 1, r2 = 3 * nt + 2;
+          const int d0 = acc[r0 / 2][2 * (r0 % 2) + e], d1 = acc[r1 / 2][2 * (r1 % 2) + e];
+          const int d2 = acc[r2 / 2][2 * (r2 % 2) + e];
+          sc[nt][2 * j + e] = fmaf(float(d2), 65536.f, fmaf(float(d1), 256.f, float(d0)));
+        }
+    }
   }
 
   // ---- scores in log2 units, masking.
@@ -839,7 +924,7 @@ __device__ __forceinline__ void consume_stage(const DecodeParams& p, const uint8
       ks[4 * i + 3] = f.w;
     }
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt)
+    for (int nt = 0; nt < kNt; ++nt)
 #pragma unroll
       for (int t = 0; t < 16; ++t) sc[nt][t] *= ks[t] * qf.cf[nt];
   }
@@ -849,7 +934,7 @@ __device__ __forceinline__ void consume_stage(const DecodeParams& p, const uint8
       const bool in = t0 + t >= lo && t0 + t < hi;
       const int64_t kp = (in && !all_visible) ? __ldg(p.k_positions + t0 + t) : 0;
 #pragma unroll
-      for (int nt = 0; nt < NT; ++nt)
+      for (int nt = 0; nt < kNt; ++nt)
         if (!in || (!all_visible && kp > qf.qpos[nt])) sc[nt][t] = -INFINITY;
     }
   }
@@ -858,9 +943,9 @@ __device__ __forceinline__ void consume_stage(const DecodeParams& p, const uint8
   //      lanes of the thread's quad).
   {
     bool rescale = false;
-    float fac[NT];
+    float fac[kNt];
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
+    for (int nt = 0; nt < kNt; ++nt) {
       float cm = sc[nt][0];
 #pragma unroll
       for (int t = 1; t < 16; ++t) cm = fmaxf(cm, sc[nt][t]);
@@ -885,7 +970,7 @@ __device__ __forceinline__ void consume_stage(const DecodeParams& p, const uint8
 #pragma unroll
       for (int dn = 0; dn < D / 8; ++dn)
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt) {
+        for (int nt = 0; nt < kNt; ++nt) {
           ws.acc[dn][nt][0] *= fac[nt];
           ws.acc[dn][nt][1] *= fac[nt];
         }
@@ -894,9 +979,10 @@ __device__ __forceinline__ void consume_stage(const DecodeParams& p, const uint8
 
   // ---- P = w * vscale in fp32 (tokens outside [lo, hi) take vscale 0: their
   //      slots may hold anything), and per column the power of two that puts
-  //      the stage's largest |P| in [2^13, 2^14): pscale scales P into the
-  //      fixed point below, inv_pscale scales the exact sums back.
-  float pscale[NT], inv_pscale[NT];
+  //      the stage's largest |P| in [2^13, 2^14) (four-column layout: in
+  //      [2^21, 2^22), for three digits): pscale scales P into the fixed
+  //      point below, inv_pscale scales the exact sums back.
+  float pscale[kNt], inv_pscale[kNt];
   {
     float vs[16];
 #pragma unroll
@@ -913,7 +999,7 @@ __device__ __forceinline__ void consume_stage(const DecodeParams& p, const uint8
         if (!(t0 + t >= lo && t0 + t < hi)) vs[t] = 0.f;
     }
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
+    for (int nt = 0; nt < kNt; ++nt) {
       float pm = 0.f;
 #pragma unroll
       for (int t = 0; t < 16; ++t) {
@@ -922,10 +1008,11 @@ __device__ __forceinline__ void consume_stage(const DecodeParams& p, const uint8
       }
       pm = fmaxf(pm, __shfl_xor_sync(0xffffffffu, pm, 1));
       pm = fmaxf(pm, __shfl_xor_sync(0xffffffffu, pm, 2));
-      // pm < 2^(x - 126) for biased exponent x; pscale = 2^(140 - x), kept
-      // a normal float (stages with |P| below ~2^-113 lose precision).
+      // pm < 2^(x - 126) for biased exponent x; pscale = 2^(140 - x) (2^(148
+      // - x) for three digits), kept a normal float (stages with |P| below
+      // ~2^-113 lose precision).
       const int x = int((__float_as_uint(pm) >> 23) & 0xffu);
-      const int sh = max(-126, min(126, 140 - x));
+      const int sh = max(-126, min(126, (NT == 0 ? 148 : 140) - x));
       pscale[nt] = pm > 0.f ? __uint_as_float(uint32_t(127 + sh) << 23) : 1.f;
       inv_pscale[nt] = pm > 0.f ? __uint_as_float(uint32_t(127 - sh) << 23) : 1.f;
     }
@@ -939,11 +1026,15 @@ __device__ __forceinline__ void consume_stage(const DecodeParams& p, const uint8
   //      in its two low bytes. The PV A fragment of k-step kb is rows
   //      (column, lo) and (column, hi) over tokens 8 kb + [0, 8) of the
   //      thread: a0 / a2 = lo of tokens +0..3 / +4..7, a1 / a3 = hi.
+  //      Four-column layout: |u| <= 2^22 in three digits u = d0 + 256 d1 +
+  //      65536 d2 (the query's split); lanes grp < 4 supply rows (column,
+  //      d0) and (column, d1), lanes grp >= 4 rows (column, d2) and zero.
   constexpr float kRoundInt = 12582912.0f;  // 1.5 * 2^23
-  constexpr uint32_t kBias = 0x8080u - 0x4B400000u;
-  uint32_t pa[NT][2][4];
+  constexpr uint32_t kBias = (NT == 0 ? 0x808080u : 0x8080u) - 0x4B400000u;
+  const bool upper = NT == 0 && grp >= 4;
+  uint32_t pa[kNt][2][4];
 #pragma unroll
-  for (int nt = 0; nt < NT; ++nt)
+  for (int nt = 0; nt < kNt; ++nt)
 #pragma unroll
     for (int kb = 0; kb < 2; ++kb)
 #pragma unroll
@@ -953,8 +1044,17 @@ __device__ __forceinline__ void consume_stage(const DecodeParams& p, const uint8
         for (int i = 0; i < 4; ++i)
           w[i] = __float_as_uint(fmaf(sc[nt][8 * kb + 4 * half + i], pscale[nt], kRoundInt)) + kBias;
         const uint32_t t01 = __byte_perm(w[0], w[1], 0x5140), t23 = __byte_perm(w[2], w[3], 0x5140);
-        pa[nt][kb][2 * half + 0] = __byte_perm(t01, t23, 0x5410) ^ 0x80808080u;
-        pa[nt][kb][2 * half + 1] = __byte_perm(t01, t23, 0x7632) ^ 0x80808080u;
+        const uint32_t d0 = __byte_perm(t01, t23, 0x5410) ^ 0x80808080u;
+        const uint32_t d1 = __byte_perm(t01, t23, 0x7632) ^ 0x80808080u;
+        if constexpr (NT == 0) {
+          const uint32_t c2 = __byte_perm(w[0], w[1], 0x0062), e2 = __byte_perm(w[2], w[3], 0x0062);
+          const uint32_t d2 = __byte_perm(c2, e2, 0x5410) ^ 0x80808080u;
+          pa[nt][kb][2 * half + 0] = upper ? d2 : d0;
+          pa[nt][kb][2 * half + 1] = upper ? 0u : d1;
+        } else {
+          pa[nt][kb][2 * half + 0] = d0;
+          pa[nt][kb][2 * half + 1] = d1;
+        }
       }
 
   // ---- O += P V on the int8 MMA (exact s32). k-step kb covers the thread's
@@ -973,16 +1073,18 @@ __device__ __forceinline__ void consume_stage(const DecodeParams& p, const uint8
     if (dn % 2 == 0) asm volatile("" ::: "memory");
     const uint4 v4 = vw[dn & 1];
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
+    for (int nt = 0; nt < kNt; ++nt) {
       int c4[4] = {0, 0, 0, 0};
       imma_16832(c4, pa[nt][0][0], pa[nt][0][1], pa[nt][0][2], pa[nt][0][3], v4.x, v4.y);
       imma_16832(c4, pa[nt][1][0], pa[nt][1][1], pa[nt][1][2], pa[nt][1][3], v4.z, v4.w);
-      // c0, c1: lo-limb sums of dims 8 dn + 2 tig + e; c2, c3: hi-limb sums.
-      // |lo sum| <= 64 * 128 * 128 and |hi sum| <= 64 * 128 * 64, so
-      // hi * 256 + lo (< 2^28) is exact in s32.
+      // c0, c1: lo-digit sums of dims 8 dn + 2 tig + e; c2, c3: hi-digit
+      // sums (four-column layout, lanes grp >= 4: d2 sums and zero, weight
+      // 65536). |digit sums| <= 64 * 128 * 128, so hi * 256 + lo (< 2^29)
+      // is exact in s32.
 #pragma unroll
       for (int e = 0; e < 2; ++e)
-        ws.acc[dn][nt][e] = fmaf(float(c4[2 + e] * 256 + c4[e]), inv_pscale[nt], ws.acc[dn][nt][e]);
+        ws.acc[dn][nt][e] = fmaf(float(c4[2 + e] * 256 + c4[e]), upper ? inv_pscale[nt] * 65536.f : inv_pscale[nt],
+                                 ws.acc[dn][nt][e]);
     }
   }
 }
@@ -1002,12 +1104,13 @@ __device__ __forceinline__ void consume_stage(const DecodeParams& p, const uint8
 // spills). At dim 256 one CTA has the SM to itself: 216 (2 x 27 + 10).
 template <int D, int NT, bool BATCHED>
 constexpr int decode_max_regs() {
-  return D == 256 ? 216 : (D == 128 && NT == 1) ? 144 : 168;
+  return D == 256 ? 216 : (D == 128 && NT <= 1) ? 144 : 168;
 }
 
 template <int D, int NT, int STAGES, bool SMALL_PAGES, bool BATCHED>
 __device__ __forceinline__ void decode_partial_body(const KernelParams<SMALL_PAGES>& p) {
   using L = DecodeSmem<D, NT, STAGES, !BATCHED>;
+  constexpr int kNt = nt_slots<NT>();
   extern __shared__ __align__(128) uint8_t smem[];
   uint8_t* ring = smem;
   float* combine = reinterpret_cast<float*>(smem + L::kOffCombine);
@@ -1019,6 +1122,9 @@ __device__ __forceinline__ void decode_partial_body(const KernelParams<SMALL_PAG
 
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
+    KVB_CTA_MARK(kCtaEntryNs, global_ns());
+    KVB_CTA_MARK(kCtaEntryClk, clock64());
+    KVB_CTA_MARK(kCtaSm, sm_id());
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
@@ -1043,6 +1149,7 @@ __device__ __forceinline__ void decode_partial_body(const KernelParams<SMALL_PAG
   }
   if (warp == 0 && !BATCHED && p.prefetch_stages != 0) prefetch_query_lines<D, NT>(p, only);
   grid_dependency_wait();
+  if (threadIdx.x == 0) KVB_CTA_MARK(kCtaDepWaitDone, clock64());
   uint64_t total, x0, x1;
   cta_stage_range<BATCHED>(p, only, total, x0, x1);
 
@@ -1058,9 +1165,9 @@ __device__ __forceinline__ void decode_partial_body(const KernelParams<SMALL_PAG
 #pragma unroll
     for (int dn = 0; dn < D / 8; ++dn)
 #pragma unroll
-      for (int nt = 0; nt < NT; ++nt) ws.acc[dn][nt][0] = ws.acc[dn][nt][1] = 0.f;
+      for (int nt = 0; nt < kNt; ++nt) ws.acc[dn][nt][0] = ws.acc[dn][nt][1] = 0.f;
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
+    for (int nt = 0; nt < kNt; ++nt) {
       ws.m[nt] = -INFINITY;
       ws.l[nt] = 0.f;
     }
@@ -1080,6 +1187,8 @@ __device__ __forceinline__ void decode_partial_body(const KernelParams<SMALL_PAG
                            p.wait_limit_ns) == kWaitOk)
         mbar_wait_bounded(&full[slot], (g / STAGES) & 1u, abort_flag, kStatusFullWaitTimeout,
                           int(g), p.wait_limit_ns);
+      if (g == 0 && lane == 0) KVB_CTA_MARK(kCtaFirstStage, clock64());
+      if (i + 1 == n && x + n >= x1 && lane == 0) KVB_CTA_MARK(kCtaLastStage, clock64());
       const uint32_t tb = (first_stage + pc.j0 + i) * kStageTokens;
       consume_stage<D, NT, SMALL_PAGES>(p, ring + size_t(slot) * StageLayout<D>::kBytes, tb, pc.lo, pc.hi,
                            all_visible, qf, ws);
@@ -1087,12 +1196,20 @@ __device__ __forceinline__ void decode_partial_body(const KernelParams<SMALL_PAG
       if (lane == 0) mbar_arrive(&empty[slot]);
     }
     g_base += n;
+    if (lane == 0) KVB_CTA_MARK(kCtaWarpDone + int(warp), clock64());
 
     // ---- flush this warp's state.
     float* cw = combine + size_t(warp) * L::kCols * L::kPitch;
-    float lsums[NT];
+    if constexpr (NT == 0) {
+      // Lanes grp and grp + 4 hold the two digit parts of one column.
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
+      for (int dn = 0; dn < D / 8; ++dn)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) ws.acc[dn][0][e] += __shfl_xor_sync(0xffffffffu, ws.acc[dn][0][e], 16);
+    }
+    float lsums[kNt];
+#pragma unroll
+    for (int nt = 0; nt < kNt; ++nt) {
       float lsum = ws.l[nt];
       lsum += __shfl_xor_sync(0xffffffffu, lsum, 1);
       lsum += __shfl_xor_sync(0xffffffffu, lsum, 2);
@@ -1100,17 +1217,20 @@ __device__ __forceinline__ void decode_partial_body(const KernelParams<SMALL_PAG
     }
     // The combine buffer overlays ring slots that other warps may still read.
     if (!BATCHED) named_barrier(1, 32 * kConsumerWarps);
+    const bool writer = NT != 0 || grp < 4;
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
+    for (int nt = 0; nt < kNt; ++nt) {
       const uint32_t col = 8 * nt + grp;
-      if (tig == 0) {
+      if (tig == 0 && writer) {
         stats[(warp * L::kCols + col) * 2 + 0] = ws.m[nt];
         stats[(warp * L::kCols + col) * 2 + 1] = lsums[nt];
       }
+      if (writer) {
 #pragma unroll
-      for (int dn = 0; dn < D / 8; ++dn)
-        *reinterpret_cast<float2*>(cw + col * L::kPitch + 8 * dn + 2 * tig) =
-            make_float2(ws.acc[dn][nt][0], ws.acc[dn][nt][1]);
+        for (int dn = 0; dn < D / 8; ++dn)
+          *reinterpret_cast<float2*>(cw + col * L::kPitch + 8 * dn + 2 * tig) =
+              make_float2(ws.acc[dn][nt][0], ws.acc[dn][nt][1]);
+      }
     }
     if (x + n >= x1) grid_launch_dependents();
     named_barrier(1, 32 * kConsumerWarps);
@@ -1161,6 +1281,10 @@ __device__ __forceinline__ void decode_partial_body(const KernelParams<SMALL_PAG
     }
     named_barrier(1, 32 * kConsumerWarps);
     x += n;
+  }
+  if (threadIdx.x == 0) {
+    KVB_CTA_MARK(kCtaPartialDone, clock64());
+    KVB_CTA_MARK(kCtaExitNs, global_ns());
   }
 }
 

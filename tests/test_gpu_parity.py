@@ -97,6 +97,33 @@ def test_geometries(cuda_device, rows, q_heads, kv_heads, dim, qpos, partitions)
                          f"{rows}x{q_heads}/{kv_heads}d{dim}/P{partitions}")
 
 
+@pytest.mark.parametrize(
+    "rows,q_heads,kv_heads,dim,page_tokens",
+    [
+        (1, 8, 8, 128, 64),   # 1 query column per KV head
+        (1, 16, 8, 256, 32),  # 2 columns, dim 256
+        (3, 8, 8, 64, 16),    # 3 causal rows of group 1, dim 64, Page16
+        (2, 16, 8, 256, 64),  # 4 columns: 2 rows x group 2, dim 256
+        (4, 4, 4, 128, 32),   # 4 causal rows of group 1
+        (1, 32, 8, 128, 16),  # cfg2 geometry on 16-token pages
+    ],
+)
+def test_four_column_layout(cuda_device, rows, q_heads, kv_heads, dim, page_tokens):
+    """At most 4 query columns per KV head take the four-column layout
+    (lane pairs splitting the Q and P digits, three P digits): every column
+    count 1-4, every dim and page size, causal rows whose visible ranges end
+    inside a stage."""
+    tokens = 2500
+    qpos = [tokens - 37 * (rows - r) for r in range(rows)] if rows > 1 else None
+    case = make(cuda_device, rows=rows, q_heads=q_heads, kv_heads=kv_heads, dim=dim, page_tokens=page_tokens,
+                tokens=tokens, seed=rows * 1000 + dim + page_tokens, q_positions=qpos)
+    assert kvb.attention_b200_supported(case.shape, case.device_input())
+    for partitions in (0, 5):
+        res = run_single(case, partitions=partitions)
+        check_against_oracle(res, case.shape, oracle.reference_case(case, threads=8),
+                             f"{rows}x{q_heads}/{kv_heads}d{dim}P{page_tokens}/{partitions}")
+
+
 def test_outlier_scales_page16_gqa8(cuda_device):
     """cfg4 flavour: GQA 8, Page16, 1% of tokens with 10x scales."""
     case = make(cuda_device, rows=1, q_heads=64, kv_heads=8, dim=128, page_tokens=16, tokens=4096,
@@ -281,6 +308,8 @@ def test_invalid_arguments_raise_before_launch(cuda_device):
         (32, 8, 128, 64, 0.0),   # cfg3 flavour
         (64, 8, 128, 16, 0.01),  # cfg4 flavour: GQA 8, Page16 (four-page gather loads), outliers
         (16, 2, 64, 16, 0.0),    # dim 64, Page16
+        (24, 8, 256, 32, 0.0),   # group 3 (four-column layout), dim 256
+        (8, 8, 128, 64, 0.01),   # group 1 (four-column layout), outliers
     ],
 )
 def test_batched_ragged(cuda_device, q_heads, kv_heads, dim, page_tokens, outliers):
