@@ -202,11 +202,18 @@ int kvb_decode_kernel(void);
 int kvb_debug_read_tc_trace(unsigned long long* out, size_t count);
 
 /* Per-CTA timeline of the warp-level partial kernels, in libraries built
- * with the trace flag: copies up to `count` stamps [1024 CTAs][16 events]
+ * with the trace flag: copies up to `count` stamps [1024 CTAs][18 events]
  * of the latest launches (entry and exit on the global timer in ns, the
- * rest SM clock stamps; the event list is in decode_tma.cuh, CtaTraceEvent)
+ * rest SM clock stamps; events 16-17 are kept from the first launch after
+ * the previous read; the event list is in decode_tma.cuh, CtaTraceEvent)
  * and clears them. Other builds return KVB_EINVAL. */
 int kvb_debug_read_cta_trace(unsigned long long* out, size_t count);
+
+/* Merge timeline in trace builds: [1024 CTAs][5] global-timer stamps (ns) -
+ * entry, dependency wait passed, exit, first loads used, warps folded - of
+ * the first merge launch after the previous read, then clears them. Other
+ * builds return KVB_EINVAL. */
+int kvb_debug_read_merge_trace(unsigned long long* out, size_t count);
 
 /* Decode call that allocates nothing. It has no counterpart in the
  * reference. kvb_launch_attention_ex needs a caller-provided scratch buffer

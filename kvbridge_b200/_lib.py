@@ -190,6 +190,7 @@ SIGNATURES = {
     "kvb_set_decode_kernel": (c_int, [c_int]),
     "kvb_debug_read_tc_trace": (c_int, [POINTER(ctypes.c_ulonglong), c_size_t]),
     "kvb_debug_read_cta_trace": (c_int, [POINTER(ctypes.c_ulonglong), c_size_t]),
+    "kvb_debug_read_merge_trace": (c_int, [POINTER(ctypes.c_ulonglong), c_size_t]),
     "kvb_decode_kernel": (c_int, []),
     "kvb_read_device_status": (c_int, [POINTER(c_int)]),
     "kvb_read_wait_failure": (c_int, [POINTER(ctypes.c_longlong)]),

@@ -480,8 +480,11 @@ cudaError_t preload_attention_kernels() {
 
 namespace {
 
-// Stages per CTA prefetched into L2 while the preceding grid finishes.
-constexpr uint32_t kPrefetchStages = 4;
+// Stages per CTA prefetched into L2 while the preceding grid finishes. At
+// cfg2 (28 stages a CTA) 0, 2, 4, 5 and 6 stages gave 26.7, 24.9, 23.7,
+// 23.6 and 23.7 us a call: the prefetch fills the HBM time the previous
+// call's drain and merge leave idle; more of it competes with that call.
+constexpr uint32_t kPrefetchStages = 5;
 
 // cuTensorMapEncodeTiled through the runtime's driver entry point (the
 // library does not link libcuda); null when the driver does not offer it.
@@ -932,6 +935,23 @@ cudaError_t read_cta_trace(unsigned long long* out, size_t count, bool* availabl
   if (code != cudaSuccess) return code;
   static const unsigned long long zeros[kvb::kCtaTraceCtas][kvb::kCtaTraceEvents] = {};
   return cudaMemcpyToSymbol(kvb::g_cta_trace, zeros, sizeof(zeros));
+#else
+  (void)out;
+  (void)count;
+  *available = false;
+  return cudaSuccess;
+#endif
+}
+
+cudaError_t read_merge_trace(unsigned long long* out, size_t count, bool* available) noexcept {
+#ifdef KVB_TC_TRACE
+  *available = true;
+  const size_t all = size_t(kvb::kMergeTraceCtas) * kvb::kMergeTraceEvents;
+  cudaError_t code =
+      cudaMemcpyFromSymbol(out, kvb::g_merge_trace, std::min(count, all) * sizeof(unsigned long long));
+  if (code != cudaSuccess) return code;
+  static const unsigned long long zeros[kvb::kMergeTraceCtas][kvb::kMergeTraceEvents] = {};
+  return cudaMemcpyToSymbol(kvb::g_merge_trace, zeros, sizeof(zeros));
 #else
   (void)out;
   (void)count;

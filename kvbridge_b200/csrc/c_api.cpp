@@ -16,6 +16,7 @@
 namespace kvbridge::detail {
 cudaError_t read_tc_trace(unsigned long long* out, size_t count, bool* available) noexcept;
 cudaError_t read_cta_trace(unsigned long long* out, size_t count, bool* available) noexcept;
+cudaError_t read_merge_trace(unsigned long long* out, size_t count, bool* available) noexcept;
 void launch_attention_noalloc(const Shape&, const DeviceInput&, unsigned partitions, float* m,
                               float* l, float* n, void* out_f16, cudaStream_t);
 }  // namespace kvbridge::detail
@@ -328,6 +329,17 @@ int kvb_debug_read_cta_trace(unsigned long long* out, size_t count) {
     if (out == nullptr) throw std::invalid_argument("output pointer is null");
     bool available = false;
     const cudaError_t code = kvbridge::detail::read_cta_trace(out, count, &available);
+    if (!available)
+      throw std::invalid_argument("this library was built without the event trace (KVB_TC_TRACE)");
+    if (code != cudaSuccess) throw std::runtime_error(std::string("trace read: ") + cudaGetErrorString(code));
+  });
+}
+
+int kvb_debug_read_merge_trace(unsigned long long* out, size_t count) {
+  return guarded([&] {
+    if (out == nullptr) throw std::invalid_argument("output pointer is null");
+    bool available = false;
+    const cudaError_t code = kvbridge::detail::read_merge_trace(out, count, &available);
     if (!available)
       throw std::invalid_argument("this library was built without the event trace (KVB_TC_TRACE)");
     if (code != cudaSuccess) throw std::runtime_error(std::string("trace read: ") + cudaGetErrorString(code));

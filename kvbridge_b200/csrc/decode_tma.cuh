@@ -106,7 +106,7 @@ using KernelParams = typename std::conditional<SMALL_PAGES, DecodeParamsGather, 
 // that CTAs on different SMs share one time axis; the other events are SM
 // clock stamps (clock64), exact within a CTA.
 constexpr int kCtaTraceCtas = 1024;
-constexpr int kCtaTraceEvents = 16;
+constexpr int kCtaTraceEvents = 18;
 enum CtaTraceEvent : int {
   kCtaEntryNs = 0,      // thread 0 entered (global timer)
   kCtaEntryClk = 1,     // thread 0 entered (clock64)
@@ -120,6 +120,11 @@ enum CtaTraceEvent : int {
   kCtaExitNs = 12,      // the same moment on the global timer
   kCtaStages = 13,      // stages the producer issued
   kCtaLastStage = 14,   // the CTA's last stage had landed (its consumer's wait returned)
+  // Kept from the first launch after the trace was cleared (later launches
+  // leave them alone), so that two traced calls show call 1's exit beside
+  // call 2's events:
+  kCtaFirstEntryNs = 16,  // entry (global timer)
+  kCtaFirstExitNs = 17,   // consumers' exit (global timer)
 };
 #ifdef KVB_TC_TRACE
 __device__ unsigned long long g_cta_trace[kCtaTraceCtas][kCtaTraceEvents];
@@ -127,9 +132,17 @@ __device__ unsigned long long g_cta_trace[kCtaTraceCtas][kCtaTraceEvents];
   do {                                                                      \
     if (blockIdx.x < kCtaTraceCtas) g_cta_trace[blockIdx.x][(event)] = (value); \
   } while (0)
+#define KVB_CTA_MARK_FIRST(event, value)                                                     \
+  do {                                                                                       \
+    if (blockIdx.x < kCtaTraceCtas && g_cta_trace[blockIdx.x][(event)] == 0ull)                \
+      g_cta_trace[blockIdx.x][(event)] = (value);                                            \
+  } while (0)
 #else
 #define KVB_CTA_MARK(event, value) \
   do {                             \
+  } while (0)
+#define KVB_CTA_MARK_FIRST(event, value) \
+  do {                                   \
   } while (0)
 #endif
 
@@ -1122,6 +1135,7 @@ __device__ __forceinline__ void decode_partial_body(const KernelParams<SMALL_PAG
 
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
+    KVB_CTA_MARK_FIRST(kCtaFirstEntryNs, global_ns());
     KVB_CTA_MARK(kCtaEntryNs, global_ns());
     KVB_CTA_MARK(kCtaEntryClk, clock64());
     KVB_CTA_MARK(kCtaSm, sm_id());
@@ -1285,6 +1299,7 @@ __device__ __forceinline__ void decode_partial_body(const KernelParams<SMALL_PAG
   if (threadIdx.x == 0) {
     KVB_CTA_MARK(kCtaPartialDone, clock64());
     KVB_CTA_MARK(kCtaExitNs, global_ns());
+    KVB_CTA_MARK_FIRST(kCtaFirstExitNs, global_ns());
   }
 }
 

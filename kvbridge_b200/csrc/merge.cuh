@@ -43,6 +43,25 @@ struct MergeParams {
   uint32_t batch, q_heads, kv_heads, group, max_tokens, ctas;
 };
 
+// Merge timeline (trace builds only, -DKVB_TC_TRACE): per CTA of the first
+// merge launch after the trace was cleared, the global timer (ns) at entry
+// (0), after the dependency wait on the partial kernel (1), at exit (2),
+// after the first chunk's loads were used (3) and after the warps' fold (4).
+constexpr int kMergeTraceCtas = 1024;
+constexpr int kMergeTraceEvents = 5;
+#ifdef KVB_TC_TRACE
+__device__ unsigned long long g_merge_trace[kMergeTraceCtas][kMergeTraceEvents];
+#define KVB_MERGE_MARK(event)                                                                 \
+  do {                                                                                        \
+    if (threadIdx.x == 0 && blockIdx.x < kMergeTraceCtas && g_merge_trace[blockIdx.x][(event)] == 0ull) \
+      g_merge_trace[blockIdx.x][(event)] = global_ns();                                       \
+  } while (0)
+#else
+#define KVB_MERGE_MARK(event) \
+  do {                        \
+  } while (0)
+#endif
+
 // Four warps per CTA with at most 80 registers a thread, so that a merge CTA
 // fits on an SM beside two partial-kernel CTAs: with programmatic dependent
 // launch it becomes resident early without holding back a partial CTA.
@@ -87,8 +106,10 @@ __global__ void __launch_bounds__(32 * kMergeWarps, 6) merge_kernel(MergeParams 
   __shared__ float red_n[kMergeWarps][256];
   // The next kernel on the stream may start its prologue now; its own
   // dependency wait still waits for this grid to finish.
+  KVB_MERGE_MARK(0);
   grid_launch_dependents();
   grid_dependency_wait();
+  KVB_MERGE_MARK(1);
   const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const uint32_t rh = blockIdx.x;
   const uint32_t D = p.dim;
@@ -158,6 +179,7 @@ __global__ void __launch_bounds__(32 * kMergeWarps, 6) merge_kernel(MergeParams 
       if (lv[j] > 0.f) cm = fmaxf(cm, mv[j]);
     if (lane == 0) red_m[warp] = cm;
     __syncthreads();
+    KVB_MERGE_MARK(3);
     float mnew = M;
 #pragma unroll
     for (int w = 0; w < kMergeWarps; ++w) mnew = fmaxf(mnew, red_m[w]);
@@ -187,6 +209,7 @@ __global__ void __launch_bounds__(32 * kMergeWarps, 6) merge_kernel(MergeParams 
     if (d < D) red_n[warp][d] = acc[k];
   }
   __syncthreads();
+  KVB_MERGE_MARK(4);
   float L = 0.f;
 #pragma unroll
   for (int w = 0; w < kMergeWarps; ++w) L += red_l[w];
@@ -211,6 +234,7 @@ __global__ void __launch_bounds__(32 * kMergeWarps, 6) merge_kernel(MergeParams 
       row[size_t(i) * (D + 2) + 1] = 0.f;
     }
   }
+  KVB_MERGE_MARK(2);
 }
 
 }  // namespace kvb

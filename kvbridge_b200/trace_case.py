@@ -23,8 +23,9 @@ them:
 
 ``--kernel warp`` prints instead the per-CTA timeline of the warp-level
 partial kernel (decode_tma.cuh, CtaTraceEvent) for the last of
-``--back-to-back`` calls issued without a host sync between them, as in a
-decode loop: every traced CTA's events on one time axis (the global timer
+``--back-to-back`` calls (default 2) replayed from one CUDA graph, as in
+bench.py, and the chain from the first call's partial
+kernel through its merge to the second call's dependency wait: every traced CTA's events on one time axis (the global timer
 at entry and exit aligns CTAs of different SMs; SM clock stamps place the
 events in between, converted at the clock rate each CTA's own entry/exit
 pair implies), the distribution over CTAs of each event and of the spans
@@ -46,9 +47,10 @@ NAMES = ["start", "qk", "sm_in", "sm_out", "pv", "f_in", "f_out", "copy", "sm_ld
 
 
 # CtaTraceEvent of decode_tma.cuh.
-CTA_MAX, CTA_EVENTS = 1024, 16
+CTA_MAX, CTA_EVENTS, MERGE_MAX, MERGE_EVENTS = 1024, 18, 1024, 5
 (E_ENTRY_NS, E_ENTRY_CLK, E_SM, E_DEP, E_FIRST_COPY, E_LAST_COPY, E_FIRST_STAGE, E_WARP0,
- E_PARTIAL, E_EXIT_NS, E_STAGES, E_LAST_STAGE) = 0, 1, 2, 3, 4, 5, 6, 7, 11, 12, 13, 14
+ E_PARTIAL, E_EXIT_NS, E_STAGES, E_LAST_STAGE, E_FIRST_ENTRY_NS, E_FIRST_EXIT_NS) = (
+    0, 1, 2, 3, 4, 5, 6, 7, 11, 12, 13, 14, 16, 17)
 
 
 def _pct(vals, q):
@@ -62,14 +64,28 @@ def cta_timeline(args, torch, _lib, api, profile_case) -> int:
     call = profile_case.make_call(args.case, torch.device("cuda", 0))
     n = CTA_MAX * CTA_EVENTS
     buf = (ctypes.c_ulonglong * n)()
-    for _ in range(args.warmup):
-        call()
+    mbuf = (ctypes.c_ulonglong * (MERGE_MAX * MERGE_EVENTS))()
+    # The traced calls replay from a CUDA graph, as in bench.py, so that the
+    # host's launch rate does not set the gaps between them.
+    stream = torch.cuda.Stream()
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            call()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for _ in range(args.back_to_back):
+            call()
+    with torch.cuda.stream(stream):
+        graph.replay()
     torch.cuda.synchronize()
     _lib.check(lib.kvb_debug_read_cta_trace(buf, n))  # clears
-    for _ in range(args.back_to_back):
-        call()
+    _lib.check(lib.kvb_debug_read_merge_trace(mbuf, MERGE_MAX * MERGE_EVENTS))
+    with torch.cuda.stream(stream):
+        graph.replay()
     torch.cuda.synchronize()
     _lib.check(lib.kvb_debug_read_cta_trace(buf, n))
+    _lib.check(lib.kvb_debug_read_merge_trace(mbuf, MERGE_MAX * MERGE_EVENTS))
     if api.read_device_status() != 0:
         print("device status nonzero:", api.read_wait_failure(), file=sys.stderr)
         return 1
@@ -131,6 +147,29 @@ def cta_timeline(args, torch, _lib, api, profile_case) -> int:
     for x in exits:
         hist[int(x) - lo] += 1
     print("CTA exits per microsecond: " + ", ".join(f"{lo + i}: {c}" for i, c in enumerate(hist) if c))
+
+    # The chain between calls: the first call's partial kernel, its merge, and
+    # the next call's partial kernel, on the global timer.
+    merges = [[mbuf[c * MERGE_EVENTS + e] for e in range(MERGE_EVENTS)] for c in range(MERGE_MAX)]
+    merges = [m for m in merges if all(m)]
+    first_exits = [r[E_FIRST_EXIT_NS] for r in rows if r[E_FIRST_EXIT_NS]]
+    if args.back_to_back >= 2 and merges and first_exits:
+        z = max(first_exits)
+
+        def span_us(vals):
+            return f"{(min(vals) - z) / 1e3:7.2f} .. {(max(vals) - z) / 1e3:7.2f}"
+
+        deps = [t0 + at(r, E_DEP) * 1e3 for r in rows if r[E_DEP]]
+        print("call 1 -> its merge -> call 2 (global timer, microseconds after call 1's last partial CTA exit):")
+        print(f"  call 1 partial CTAs exited       {span_us(first_exits)}")
+        print(f"  call 1 merge CTAs entered        {span_us([m[0] for m in merges])}")
+        print(f"  call 1 merge dependency passed   {span_us([m[1] for m in merges])}")
+        print(f"  call 1 merge first loads used    {span_us([m[3] for m in merges])}")
+        print(f"  call 1 merge warps folded        {span_us([m[4] for m in merges])}")
+        print(f"  call 1 merge CTAs exited         {span_us([m[2] for m in merges])}")
+        if args.back_to_back == 2:
+            print(f"  call 2 partial CTAs entered      {span_us([r[E_ENTRY_NS] for r in rows])}")
+            print(f"  call 2 dependency wait passed    {span_us(deps)}")
     return 0
 
 
@@ -139,7 +178,7 @@ def main(argv=None) -> int:
     ap.add_argument("--case", default="native")
     ap.add_argument("--kernel", choices=["tcgen05", "warp"], default="tcgen05")
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--back-to-back", type=int, default=5, help="warp: calls issued before the read")
+    ap.add_argument("--back-to-back", type=int, default=2, help="warp: calls issued before the read")
     ap.add_argument("--mhz", type=float, default=1965.0, help="tcgen05: SM clock used to convert cycles to microseconds")
     args = ap.parse_args(argv)
     os.environ["KVB_TRACE_LIBRARY"] = "1"
