@@ -417,9 +417,14 @@ unsigned attention_partitions(const Shape& s, unsigned requested) {
     } else {
       const ColumnPlan plan = column_plan(s.dim, query_rows(s));
       const FastVariant v = fast_variant(s.dim, plan.nt, s.page_tokens, false);
-      const uint32_t wave =
-          v.fn ? uint32_t(current_device_facts().sms) * uint32_t(resident_ctas(v)) : 1u;
-      parts = std::max(1u, wave / (s.kv_heads * plan.groups));
+      const uint32_t sms = uint32_t(current_device_facts().sms);
+      const uint32_t wave = v.fn ? sms * uint32_t(resident_ctas(v)) : 1u;
+      // One wave of CTAs, but at most one partition per SM for a KV head:
+      // with fewer KV heads (one per GPU when cfg2's 8 are split over 8)
+      // the merge's rounds over the partials cost more than the extra CTAs
+      // stream (one KV head, 65,536 tokens: 256 partitions 15.2 us a call,
+      // 148 12.4 us, 96 12.5 us, 64 13.3 us).
+      parts = std::max(1u, std::min(wave / (s.kv_heads * plan.groups), sms));
     }
   }
   parts = std::min(parts, stages);
