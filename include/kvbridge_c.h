@@ -202,7 +202,7 @@ int kvb_decode_kernel(void);
 int kvb_debug_read_tc_trace(unsigned long long* out, size_t count);
 
 /* Per-CTA timeline of the warp-level partial kernels, in libraries built
- * with the trace flag: copies up to `count` stamps [1024 CTAs][18 events]
+ * with the trace flag: copies up to `count` stamps [1024 CTAs][20 events]
  * of the latest launches (entry and exit on the global timer in ns, the
  * rest SM clock stamps; events 16-17 are kept from the first launch after
  * the previous read; the event list is in decode_tma.cuh, CtaTraceEvent)

@@ -106,7 +106,7 @@ using KernelParams = typename std::conditional<SMALL_PAGES, DecodeParamsGather, 
 // that CTAs on different SMs share one time axis; the other events are SM
 // clock stamps (clock64), exact within a CTA.
 constexpr int kCtaTraceCtas = 1024;
-constexpr int kCtaTraceEvents = 18;
+constexpr int kCtaTraceEvents = 20;
 enum CtaTraceEvent : int {
   kCtaEntryNs = 0,      // thread 0 entered (global timer)
   kCtaEntryClk = 1,     // thread 0 entered (clock64)
@@ -125,7 +125,20 @@ enum CtaTraceEvent : int {
   // call 2's events:
   kCtaFirstEntryNs = 16,  // entry (global timer)
   kCtaFirstExitNs = 17,   // consumers' exit (global timer)
+  kCtaProducerWait = 18,  // SM cycles the producer spent waiting for free ring slots
+  kCtaConsumerWait = 19,  // SM cycles consumer warp 0 spent waiting for its stages to land
 };
+#ifdef KVB_TC_TRACE
+#define KVB_WAIT_CLOCK_BEGIN() const long long kvb_wait_t0 = clock64()
+#define KVB_WAIT_CLOCK_END(acc) (acc) += static_cast<unsigned long long>(clock64() - kvb_wait_t0)
+#else
+#define KVB_WAIT_CLOCK_BEGIN() \
+  do {                         \
+  } while (0)
+#define KVB_WAIT_CLOCK_END(acc) \
+  do {                          \
+  } while (0)
+#endif
 #ifdef KVB_TC_TRACE
 __device__ unsigned long long g_cta_trace[kCtaTraceCtas][kCtaTraceEvents];
 #define KVB_CTA_MARK(event, value)                                          \
@@ -463,7 +476,7 @@ __device__ void mark_empty_splits(const DecodeParams& p, const Piece& pc) {
 // scales for l < 16, V scales above) with a plain load and stores them to the
 // stage before the barrier is armed, and the lane holding a page's first
 // four tokens starts the bulk copy of that page's K (l < 16) or V (l >= 16).
-// A lane's table entries and scales are fetched 8 and 3 stages ahead in
+// A lane's table entries and scales are fetched 8 and 5 stages ahead in
 // registers that take turns (no register copies, which would wait for the
 // loads). With 64-token pages the extra per-stage work costs more than the
 // two copies it saves, so produce() keeps those.
@@ -488,6 +501,8 @@ __device__ void produce_small_pages(const DecodeParamsGather& p, const Piece& on
   cta_stage_range<BATCHED>(p, only, total, x0, x1);
   uint32_t g = 0;  // stages issued so far (CTA stage sequence number)
   bool failed = false;
+  unsigned long long empty_wait = 0;  // trace builds only
+  (void)empty_wait;
   for (uint64_t x = x0; x < x1 && !failed;) {
     const Piece pc = locate_piece<BATCHED>(p, only, x, x1, total, blockIdx.x);
     const uint32_t first_stage = pc.lo / kStageTokens;
@@ -519,9 +534,11 @@ __device__ void produce_small_pages(const DecodeParamsGather& p, const Piece& on
       const bool gather = pps == 4 && p.gather_kv != 0 && __all_sync(0xffffffffu, ok);
       const int32_t unit32 = int32_t(uint32_t(ok ? t : 0u) * p.kv_heads + pc.h);
       const uint32_t slot = g % STAGES;
+      KVB_WAIT_CLOCK_BEGIN();
       if (mbar_wait_bounded(&empty[slot], ((g / STAGES) & 1u) ^ 1u, abort_flag,
                             kStatusEmptyWaitTimeout, int(g), p.wait_limit_ns) != kWaitOk)
         return false;
+      KVB_WAIT_CLOCK_END(empty_wait);
       if (g == p.fault_stage && blockIdx.x == 0) {
         // Test hook: the stage is never published (no tag) and loads nothing;
         // its barrier phase completes with zero bytes so that the ring, and
@@ -564,19 +581,22 @@ __device__ void produce_small_pages(const DecodeParamsGather& p, const Piece& on
       ++g;
       return true;
     };
+    // Table entries 8 stages ahead, scales 5 (their loads go to DRAM under a
+    // streaming HBM; at cfg4 a lead of 3 was 1.5 % slower, and 7 leaves the
+    // table entry too little time before its scale load needs it).
     uint32_t t[8];
     bool mine[8];
-    float4 sc[4];
+    float4 sc[8];
 #pragma unroll
     for (int u = 0; u < 8; ++u) table_load(pc.j0 + u, t[u], mine[u]);
 #pragma unroll
-    for (int u = 0; u < 3; ++u) scale_load(t[u], mine[u], sc[u]);
+    for (int u = 0; u < 5; ++u) scale_load(t[u], mine[u], sc[u]);
     for (uint32_t jb = pc.j0; jb < pc.j1 && !failed; jb += 8) {
 #pragma unroll
       for (int u = 0; u < 8; ++u) {
         if (jb + u >= pc.j1) break;
-        scale_load(t[(u + 3) & 7], mine[(u + 3) & 7], sc[(u + 3) & 3]);
-        if (!issue_stage(t[u], mine[u], sc[u & 3])) {
+        scale_load(t[(u + 5) & 7], mine[(u + 5) & 7], sc[(u + 5) & 7]);
+        if (!issue_stage(t[u], mine[u], sc[u & 7])) {
           failed = true;
           break;
         }
@@ -586,7 +606,10 @@ __device__ void produce_small_pages(const DecodeParamsGather& p, const Piece& on
     x = piece_end_stage(p, pc, x);
   }
   if (!BATCHED && !failed) mark_empty_splits<D>(p, only);
-  if (lane == 0) KVB_CTA_MARK(kCtaStages, g);
+  if (lane == 0) {
+    KVB_CTA_MARK(kCtaStages, g);
+    KVB_CTA_MARK(kCtaProducerWait, empty_wait);
+  }
   drain_copies<STAGES>(full, g, p.wait_limit_ns);
 }
 
@@ -625,6 +648,8 @@ __device__ void produce(const DecodeParams& p, const Piece& only, uint8_t* ring,
   cta_stage_range<BATCHED>(p, only, total, x0, x1);
   uint32_t g = 0;  // stages issued so far (CTA stage sequence number)
   bool failed = false;
+  unsigned long long empty_wait = 0;  // trace builds only
+  (void)empty_wait;
   for (uint64_t x = x0; x < x1 && !failed;) {
     const Piece pc = locate_piece<BATCHED>(p, only, x, x1, total, blockIdx.x);
     const uint32_t first_stage = pc.lo / kStageTokens;
@@ -665,11 +690,13 @@ __device__ void produce(const DecodeParams& p, const Piece& only, uint8_t* ring,
       for (uint32_t sb = 0; sb < nstages; ++sb) {
         const uint32_t slot = g % STAGES;
         const uint32_t use = g / STAGES;
+        KVB_WAIT_CLOCK_BEGIN();
         if (mbar_wait_bounded(&empty[slot], (use & 1u) ^ 1u, abort_flag, kStatusEmptyWaitTimeout,
                               int(g), p.wait_limit_ns) != kWaitOk) {
           failed = true;
           break;
         }
+        KVB_WAIT_CLOCK_END(empty_wait);
         if (g == p.fault_stage && blockIdx.x == 0) {
           // Test hook: the stage is never published (no tag) and loads
           // nothing; its barrier phase completes with zero bytes so that the
@@ -698,7 +725,10 @@ __device__ void produce(const DecodeParams& p, const Piece& only, uint8_t* ring,
     x = piece_end_stage(p, pc, x);
   }
   if (!BATCHED && !failed) mark_empty_splits<D>(p, only);
-  if (lane == 0) KVB_CTA_MARK(kCtaStages, g);
+  if (lane == 0) {
+    KVB_CTA_MARK(kCtaStages, g);
+    KVB_CTA_MARK(kCtaProducerWait, empty_wait);
+  }
   drain_copies<STAGES>(full, g, p.wait_limit_ns);
 }
 
@@ -1169,6 +1199,8 @@ __device__ __forceinline__ void decode_partial_body(const KernelParams<SMALL_PAG
 
   const uint32_t grp = lane >> 2, tig = lane & 3;
   uint32_t g_base = 0;  // CTA stage sequence number of the piece's first stage
+  unsigned long long full_wait = 0;  // trace builds only
+  (void)full_wait;
   for (uint64_t x = x0; x < x1;) {
     const Piece pc = locate_piece<BATCHED>(p, only, x, x1, total, blockIdx.x);
     const uint32_t first_stage = pc.lo / kStageTokens;
@@ -1197,10 +1229,12 @@ __device__ __forceinline__ void decode_partial_body(const KernelParams<SMALL_PAG
       // would mistake that phase for this one. Wait for the producer to tag
       // the slot with g first; from then on the barrier is in the phase of
       // stage g or past it, and the parity test is exact.
+      KVB_WAIT_CLOCK_BEGIN();
       if (wait_tag_bounded(&tags[slot], g, abort_flag, kStatusFullWaitTimeout, int(g),
                            p.wait_limit_ns) == kWaitOk)
         mbar_wait_bounded(&full[slot], (g / STAGES) & 1u, abort_flag, kStatusFullWaitTimeout,
                           int(g), p.wait_limit_ns);
+      KVB_WAIT_CLOCK_END(full_wait);
       if (g == 0 && lane == 0) KVB_CTA_MARK(kCtaFirstStage, clock64());
       if (i + 1 == n && x + n >= x1 && lane == 0) KVB_CTA_MARK(kCtaLastStage, clock64());
       const uint32_t tb = (first_stage + pc.j0 + i) * kStageTokens;
@@ -1297,6 +1331,7 @@ __device__ __forceinline__ void decode_partial_body(const KernelParams<SMALL_PAG
     x += n;
   }
   if (threadIdx.x == 0) {
+    KVB_CTA_MARK(kCtaConsumerWait, full_wait);
     KVB_CTA_MARK(kCtaPartialDone, clock64());
     KVB_CTA_MARK(kCtaExitNs, global_ns());
     KVB_CTA_MARK_FIRST(kCtaFirstExitNs, global_ns());

@@ -9,6 +9,7 @@ profiler's replay passes):
   cfg2            B1, 65,536 ctx, 32/8 heads, dim 128, Page64 shuffled
   cfg3-slice      batch 8 of the cfg3 ragged lengths, Page64 shared pool
   cfg4-slice      batch 8 x 16,384, 64/8 heads, Page16, 1 % 10x outliers
+  cfg4-slice-p64  the same on 64-token pages (the page size's own cost)
   cfg5-slice      batch 4 x 131,072 tokens (one eighth of each cfg5 sequence)
   native          the reference's native shape: rows 8, 24/4 heads, dim 256,
                   Page32, 32,768 ctx
@@ -23,7 +24,7 @@ import torch
 
 from . import api, build, synth
 
-CASES = ("cfg1", "cfg2", "cfg3-slice", "cfg4-slice", "cfg5-slice", "native")
+CASES = ("cfg1", "cfg2", "cfg3-slice", "cfg4-slice", "cfg4-slice-p64", "cfg5-slice", "native")
 
 
 def _single(case: synth.SingleCase, partitions: int):
@@ -69,8 +70,9 @@ def make_call(name: str, device):
     if name == "cfg3-slice":
         lens = synth.ragged_lengths(32, 1024, 32768, seed=seed + 3)[:8]
         return _batched(synth.make_batched(32, 8, 128, 64, lens, seed + 3, device))
-    if name == "cfg4-slice":
-        return _batched(synth.make_batched(64, 8, 128, 16, [16384] * 8, seed + 4, device, outlier_frac=0.01))
+    if name in ("cfg4-slice", "cfg4-slice-p64"):
+        page = 16 if name == "cfg4-slice" else 64
+        return _batched(synth.make_batched(64, 8, 128, page, [16384] * 8, seed + 4, device, outlier_frac=0.01))
     if name == "cfg5-slice":
         return _batched(synth.make_batched(32, 8, 128, 64, [131072] * 4, seed + 5, device))
     if name == "native":

@@ -47,10 +47,10 @@ NAMES = ["start", "qk", "sm_in", "sm_out", "pv", "f_in", "f_out", "copy", "sm_ld
 
 
 # CtaTraceEvent of decode_tma.cuh.
-CTA_MAX, CTA_EVENTS, MERGE_MAX, MERGE_EVENTS = 1024, 18, 1024, 5
+CTA_MAX, CTA_EVENTS, MERGE_MAX, MERGE_EVENTS = 1024, 20, 1024, 5
 (E_ENTRY_NS, E_ENTRY_CLK, E_SM, E_DEP, E_FIRST_COPY, E_LAST_COPY, E_FIRST_STAGE, E_WARP0,
- E_PARTIAL, E_EXIT_NS, E_STAGES, E_LAST_STAGE, E_FIRST_ENTRY_NS, E_FIRST_EXIT_NS) = (
-    0, 1, 2, 3, 4, 5, 6, 7, 11, 12, 13, 14, 16, 17)
+ E_PARTIAL, E_EXIT_NS, E_STAGES, E_LAST_STAGE, E_FIRST_ENTRY_NS, E_FIRST_EXIT_NS, E_PROD_WAIT,
+ E_CONS_WAIT) = (0, 1, 2, 3, 4, 5, 6, 7, 11, 12, 13, 14, 16, 17, 18, 19)
 
 
 def _pct(vals, q):
@@ -141,6 +141,13 @@ def cta_timeline(args, torch, _lib, api, profile_case) -> int:
     print(f"{'span (per CTA)':32s} {'min':>7s} {'median':>7s} {'p90':>7s} {'max':>7s}")
     for name, vals in spans:
         print(f"{name:32s} " + " ".join(f"{_pct(vals, q):7.2f}" for q in (0, 0.5, 0.9, 1.0)))
+    life = [(r[E_PARTIAL] - r[E_ENTRY_CLK]) for r in rows]
+    pw = [r[E_PROD_WAIT] / max(1, x) for r, x in zip(rows, life)]
+    cw = [r[E_CONS_WAIT] / max(1, x) for r, x in zip(rows, life)]
+    print(f"producer waiting for free slots: median {100 * statistics.median(pw):.0f} % of the CTA's "
+          f"lifetime (p10 {100 * _pct(pw, 0.1):.0f}, p90 {100 * _pct(pw, 0.9):.0f}); consumer warp 0 "
+          f"waiting for data: median {100 * statistics.median(cw):.0f} % (p10 {100 * _pct(cw, 0.1):.0f}, "
+          f"p90 {100 * _pct(cw, 0.9):.0f})")
     exits = [at(r, E_PARTIAL) for r in rows]
     lo = int(min(exits))
     hist = [0] * (int(max(exits)) - lo + 1)
