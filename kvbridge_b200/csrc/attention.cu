@@ -316,12 +316,21 @@ const void* merge_fn(int mode, uint32_t dim) {
   return dim <= 64 ? merge_fn_kd<2>(mode) : dim <= 128 ? merge_fn_kd<4>(mode) : merge_fn_kd<8>(mode);
 }
 
+// Merges of more than kMergeWideAbove partials per row-head (reference
+// scratch or shard layout): one CTA per 32 dims of a row-head.
+const void* merge_wide_fn(int mode) {
+  return mode == kvb::kMergeScratch ? reinterpret_cast<const void*>(&kvb::merge_wide_kernel<kvb::kMergeScratch>)
+                                    : reinterpret_cast<const void*>(&kvb::merge_wide_kernel<kvb::kMergeShards>);
+}
+
 void launch_merge(int mode, const kvb::MergeParams& prm, cudaStream_t stream) {
-  const uint32_t blocks = prm.row_heads;  // one CTA per row-head
-  if (blocks == 0) return;
+  if (prm.row_heads == 0) return;
+  const bool wide = mode != kvb::kMergeBatched && prm.np > kvb::kMergeWideAbove;
+  // One CTA per row-head, or per 32 dims of one.
+  const uint32_t blocks = wide ? prm.row_heads * ((prm.dim + 31) / 32) : prm.row_heads;
   kvb::MergeParams copy = prm;
   void* args[] = {&copy};
-  const void* fn = merge_fn(mode, prm.dim);
+  const void* fn = wide ? merge_wide_fn(mode) : merge_fn(mode, prm.dim);
   cuda_ok(prefer_max_shared(fn), "merge kernel carveout");
   launch_pdl(fn, dim3(blocks), dim3(32 * kvb::kMergeWarps), 0, stream, args,
              "attention merge launch");
@@ -444,7 +453,8 @@ cudaError_t preload_attention_reference_kernels() {
       merge_fn(kvb::kMergeScratch, 256), merge_fn(kvb::kMergeBatched, 64),
       merge_fn(kvb::kMergeBatched, 128), merge_fn(kvb::kMergeBatched, 256),
       merge_fn(kvb::kMergeShards, 64),   merge_fn(kvb::kMergeShards, 128),
-      merge_fn(kvb::kMergeShards, 256),
+      merge_fn(kvb::kMergeShards, 256),  merge_wide_fn(kvb::kMergeScratch),
+      merge_wide_fn(kvb::kMergeShards),
   };
   for (const void* fn : fns) {
     cudaError_t code = cudaFuncGetAttributes(&a, fn);

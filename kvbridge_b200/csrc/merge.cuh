@@ -237,4 +237,117 @@ __global__ void __launch_bounds__(32 * kMergeWarps, 6) merge_kernel(MergeParams 
   KVB_MERGE_MARK(2);
 }
 
+// Number of partials above which a row-head's merge takes merge_wide_kernel:
+// merge_kernel reads at most kMergeWarps * 10 partials a round at dim 128.
+constexpr uint32_t kMergeWideAbove = 40;
+
+// Merge of many partials per row-head (kScratch, kShards): CTA c merges dims
+// [32 s, 32 s + 32) of row-head c / S, S = ceil(dim / 32), so that the S
+// slices of a row-head read its partials on S SMs. Partials go in rounds of
+// 32 a warp (128 a CTA): lane j loads m and l of the warp's partial j, and
+// every lane loads each of those 32 partials' n at its own dim, all before
+// any is used; the partials' weights reach the lanes by shuffles. With 148
+// partials per row-head (one KV head of cfg2 per GPU) that is two rounds
+// where merge_kernel takes four.
+template <int MODE>
+__global__ void __launch_bounds__(32 * kMergeWarps, 6) merge_wide_kernel(MergeParams p) {
+  static_assert(MODE != kMergeBatched, "the batched layout takes merge_kernel");
+  __shared__ float red_m[kMergeWarps];
+  __shared__ float red_l[kMergeWarps];
+  __shared__ float red_n[kMergeWarps][32];
+  KVB_MERGE_MARK(0);
+  grid_launch_dependents();
+  grid_dependency_wait();
+  KVB_MERGE_MARK(1);
+  const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const uint32_t D = p.dim, slices = (D + 31) / 32;
+  const uint32_t rh = blockIdx.x / slices, slice = blockIdx.x % slices;
+  const uint32_t d = 32 * slice + lane;
+  const bool has_d = d < D;
+  const uint32_t np = p.np;
+
+  const float *mb, *lb, *nb;
+  size_t ms, ls, ns;
+  if (MODE == kMergeScratch) {
+    mb = p.part + size_t(rh) * p.split_stride * (D + 2);
+    lb = mb + 1;
+    nb = mb + 2;
+    ms = ls = ns = D + 2;
+  } else {
+    mb = p.m_parts + rh;
+    lb = p.l_parts + rh;
+    nb = p.n_parts + size_t(rh) * D;
+    ms = ls = p.shard_stride ? p.shard_stride : p.row_heads;
+    ns = p.shard_stride ? p.shard_stride : size_t(p.row_heads) * D;
+  }
+
+  float acc = 0.f, M = -INFINITY, Lw = 0.f;  // Lw: this lane's partials' share of L
+  for (uint32_t base = 0; base < np; base += 32 * kMergeWarps) {
+    const uint32_t first = base + 32 * warp;
+    const uint32_t i = first + lane;  // this lane's partial
+    const bool ok = i < np;
+    const float lv = ok ? lb[i * ls] : 0.f;
+    const float mv = ok ? mb[i * ms] : -INFINITY;
+    const uint32_t okmask = __ballot_sync(0xffffffffu, ok);
+    float nv[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      nv[j] = (((okmask >> j) & 1u) != 0u && has_d) ? nb[size_t(first + j) * ns + d] : 0.f;
+    const float cm = warp_max(lv > 0.f ? mv : -INFINITY);
+    if (lane == 0) red_m[warp] = cm;
+    __syncthreads();
+    KVB_MERGE_MARK(3);
+    float mnew = M;
+#pragma unroll
+    for (int w = 0; w < kMergeWarps; ++w) mnew = fmaxf(mnew, red_m[w]);
+    __syncthreads();
+    if (mnew == -INFINITY) continue;
+    const float alpha = M == -INFINITY ? 0.f : expf(M - mnew);
+    Lw *= alpha;
+    acc *= alpha;
+    // A partial with l = 0 contributes nothing (an empty-split marker leaves
+    // its n undefined).
+    const bool live = lv > 0.f;
+    const float e = live ? expf(mv - mnew) : 0.f;
+    Lw = fmaf(e, lv, Lw);
+    const uint32_t livemask = __ballot_sync(0xffffffffu, live);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const float ej = __shfl_sync(0xffffffffu, e, j);
+      acc = ((livemask >> j) & 1u) != 0u ? fmaf(ej, nv[j], acc) : acc;
+    }
+    M = mnew;
+  }
+  Lw = warp_sum(Lw);
+  if (lane == 0) red_l[warp] = Lw;
+  red_n[warp][lane] = acc;
+  __syncthreads();
+  KVB_MERGE_MARK(4);
+  float L = 0.f;
+#pragma unroll
+  for (int w = 0; w < kMergeWarps; ++w) L += red_l[w];
+  if (threadIdx.x == 0 && slice == 0) {
+    p.m[rh] = L > 0.f ? M : -INFINITY;
+    p.l[rh] = L;
+  }
+  if (warp == 0 && has_d) {
+    float v = 0.f;
+#pragma unroll
+    for (int w = 0; w < kMergeWarps; ++w) v += red_n[w][lane];
+    v = L > 0.f ? v : 0.f;
+    const float inv = L > 0.f ? 1.f / L : 0.f;
+    p.n[size_t(rh) * D + d] = v;
+    if (p.out != nullptr) p.out[size_t(rh) * D + d] = __float2half_rn(v * inv);
+    if (p.out_bf16 != nullptr) p.out_bf16[size_t(rh) * D + d] = __float2bfloat16_rn(v * inv);
+  }
+  if (MODE == kMergeScratch && p.fill_empty && slice == 0) {
+    float* row = p.part + size_t(rh) * p.split_stride * (D + 2);
+    for (uint32_t j = np + threadIdx.x; j < p.split_stride; j += 32 * kMergeWarps) {
+      row[size_t(j) * (D + 2) + 0] = -INFINITY;
+      row[size_t(j) * (D + 2) + 1] = 0.f;
+    }
+  }
+  KVB_MERGE_MARK(2);
+}
+
 }  // namespace kvb

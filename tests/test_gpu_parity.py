@@ -124,6 +124,19 @@ def test_four_column_layout(cuda_device, rows, q_heads, kv_heads, dim, page_toke
                              f"{rows}x{q_heads}/{kv_heads}d{dim}P{page_tokens}/{partitions}")
 
 
+@pytest.mark.parametrize("kv_heads", [1, 2])
+@pytest.mark.parametrize("partitions", [0, 256])
+def test_few_kv_heads_many_partials(cuda_device, kv_heads, partitions):
+    """One rank's share of cfg2 split over 8 or 4 GPUs (1 or 2 KV heads, 65,536
+    tokens): 148 automatic partitions, or 256, per row-head, merged by the
+    many-partials merge (one CTA per 32 dims, rounds of 128 partials)."""
+    case = make(cuda_device, rows=1, q_heads=4 * kv_heads, kv_heads=kv_heads, dim=128, page_tokens=64,
+                tokens=65536, seed=900 + kv_heads)
+    assert kvb.attention_partitions(case.shape, partitions) > 40
+    res = run_single(case, partitions=partitions)
+    check_against_oracle(res, case.shape, oracle.reference_case(case, threads=8), f"kv{kv_heads}/P{partitions}")
+
+
 def test_outlier_scales_page16_gqa8(cuda_device):
     """cfg4 flavour: GQA 8, Page16, 1% of tokens with 10x scales."""
     case = make(cuda_device, rows=1, q_heads=64, kv_heads=8, dim=128, page_tokens=16, tokens=4096,
