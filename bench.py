@@ -750,9 +750,12 @@ def weak_replicated(args, bench, kvb, synth, world, rank, device):
 def cfg5_sequence_sharded(args, bench, kvb, synth, world, rank, device):
     """BASELINE cfg5, 4 x 1,048,576 tokens, split along the sequence: each
     rank decodes its page-aligned range of every sequence (one batched call
-    into a packed [m | l | n] buffer); at N > 1 the buffers are all-gathered
-    in one NCCL collective and merged with merge_attention_shards_ex, inside
-    the timed region. Steps are eager launches, timed in blocks of --steps."""
+    into a packed [m | l | n] buffer); at N > 1 the ranks' partials are
+    exchanged and merged inside the timed region, by one kernel that reads
+    the other ranks' buffers over NVLink (sharding.PeerExchange,
+    merge_attention_peers; the value reported), and for comparison by one
+    NCCL all-gather followed by merge_attention_shards_ex. Steps are eager
+    launches, timed in blocks of --steps."""
     import torch
 
     from kvbridge_b200 import sharding
@@ -775,11 +778,20 @@ def cfg5_sequence_sharded(args, bench, kvb, synth, world, rank, device):
     def local_step():
         kvb.launch_attention_batched(bc.shape, binp, ws, ws_bytes, pm, pl, pn, out if world == 1 else None)
 
-    def full_step():
+    def nccl_step():
         local_step()
-        if world > 1:
-            gathered = sharding.all_gather_packed(packed)
-            merge(gathered)
+        gathered = sharding.all_gather_packed(packed)
+        merge(gathered)
+
+    ex = sharding.PeerExchange(rh, D) if world > 1 else None
+    mo = torch.empty(rh, device=device)
+    lo = torch.empty(rh, device=device)
+    no = torch.empty(rh * D, device=device)
+
+    def peer_step():
+        sm, sl, sn = ex.slot()
+        kvb.launch_attention_batched(bc.shape, binp, ws, ws_bytes, sm, sl, sn, None)
+        ex.merge(mo, lo, no, out)
 
     def block(fn):
         def run():
@@ -787,9 +799,14 @@ def cfg5_sequence_sharded(args, bench, kvb, synth, world, rank, device):
                 fn()
         return run
 
-    full = bench.timed(block(full_step), bench.steps)
+    full = bench.timed(block(peer_step if world > 1 else local_step), bench.steps)
+    nccl = bench.timed(block(nccl_step), bench.steps) if world > 1 else full
     loc = bench.timed(block(local_step), bench.steps) if world > 1 else full
     check_status(kvb, "cfg5")
+    if ex is not None:
+        torch.cuda.synchronize()
+        bench.barrier()  # every rank's kernels are done with every peer buffer
+        ex.close()
     total_bytes = batch * tokens * 8 * (2 * D + 8)
     value = total_bytes / (full["per_call_ms"] / 1e3) / 1e9
     del bc, ws
@@ -798,11 +815,15 @@ def cfg5_sequence_sharded(args, bench, kvb, synth, world, rank, device):
             "us_per_call": round(full["per_call_ms"] * 1e3, 3),
             "local_decode_us": round(loc["per_call_ms"] * 1e3, 3),
             "exchange_and_merge_us": round((full["per_call_ms"] - loc["per_call_ms"]) * 1e3, 3),
+            "nccl_all_gather_and_merge": ({"us_per_call": round(nccl["per_call_ms"] * 1e3, 3),
+                                           "exchange_and_merge_us": round((nccl["per_call_ms"] - loc["per_call_ms"])
+                                                                          * 1e3, 3)} if world > 1 else None),
             "kv_bytes_per_step": total_bytes, "calls": full["calls"],
             "pct_of_measured_hbm_per_gpu": round(100 * value / world / measured_peak()[0], 2),
             "config": f"4 x 1,048,576 ctx, 32/8 heads, dim 128, Page64; {local} tokens of each sequence per GPU"
-                      + ("; one NCCL all-gather of the packed (m, l, n) partials + merge_attention_shards_ex"
-                         if world > 1 else "")}
+                      + ("; the partials exchanged and merged by one kernel over NVLink peer memory "
+                         "(merge_attention_peers); nccl_all_gather_and_merge: the same step with one NCCL "
+                         "all-gather + merge_attention_shards_ex" if world > 1 else "")}
 
 
 # ---------------------------------------------------------------------------

@@ -109,6 +109,30 @@ void merge_attention_shards_ex(unsigned shards, unsigned row_heads, unsigned dim
                                size_t shard_stride, float* m, float* l, float* n, void* out_f16,
                                void* out_bf16, cudaStream_t);
 
+// Cross-GPU merge of sequence shards over NVLink peer memory, in place of an
+// all-gather followed by merge_attention_shards_ex: one kernel exchanges and
+// merges. Each of the `world` ranks (one process per GPU, at most 8) owns a
+// peer buffer of peer_buffer_bytes(row_heads, dim) bytes from
+// peer_buffer_alloc, exported to the other ranks by its 64-byte CUDA IPC
+// handle and mapped there with peer_buffer_open. Call number `epoch` (1, 2,
+// ... counted by each rank alike) writes the rank's partials (m, l, n as in
+// the packed layout above) into peer_slot(own buffer, epoch, ...) and then
+// calls merge_attention_peers with every rank's buffer base (its own at
+// [rank]) on the same stream: the kernel publishes the slot to every rank,
+// waits (up to the wait limit, status 7 when it runs out) until every rank
+// has published this epoch, reads their slots over NVLink and writes the
+// merged m, l, n (and fp16 / bf16 outputs) of all row_heads. A rank must
+// not start call epoch + 2 before its call epoch + 1 returned on the stream.
+size_t peer_buffer_bytes(unsigned row_heads, unsigned dim);
+float* peer_slot(void* buffer, unsigned epoch, unsigned row_heads, unsigned dim);
+void peer_buffer_alloc(size_t bytes, void** buffer, unsigned char handle[64]);
+void peer_buffer_open(const unsigned char handle[64], void** peer_buffer);
+void peer_buffer_close(void* peer_buffer);
+void peer_buffer_free(void* buffer);
+void merge_attention_peers(const void* const* buffers, unsigned world, unsigned rank, unsigned epoch,
+                           unsigned row_heads, unsigned dim, float* m, float* l, float* n, void* out_f16,
+                           void* out_bf16, cudaStream_t);
+
 // Paged KV append (the step before decode; no counterpart in the reference,
 // whose fixtures write codes and scales directly): quantises new K and V rows
 // with the symmetric per-(token, kv-head) absmax rule -- scale = max|x| / 127,

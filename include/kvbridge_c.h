@@ -160,6 +160,36 @@ int kvb_merge_attention_shards_ex(unsigned shards, unsigned row_heads, unsigned 
                                   const float* m_parts, const float* l_parts,
                                   const float* n_parts, size_t shard_stride, float* m, float* l,
                                   float* n, void* out_f16, void* out_bf16, void* stream);
+/* Cross-GPU merge of sequence shards over NVLink peer memory, in place of an
+ * all-gather followed by kvb_merge_attention_shards_ex (one kernel exchanges
+ * and merges). Each rank (one process per GPU, at most 8) allocates a peer
+ * buffer of kvb_peer_buffer_bytes(row_heads, dim) bytes with
+ * kvb_peer_buffer_alloc, which also returns its 64-byte CUDA IPC handle; the
+ * ranks exchange handles (any host channel) and map each other's buffers
+ * with kvb_peer_buffer_open. Call number `epoch` (1, 2, ..., counted alike on
+ * every rank) writes the rank's partials into kvb_peer_slot(own buffer,
+ * epoch, row_heads, dim) - packed [m | l | n]: m at 0, l at row_heads, n at
+ * 2 * row_heads floats - and then calls kvb_merge_attention_peers on the same
+ * stream with every rank's buffer ([rank] = its own). The kernel publishes
+ * the slot to every rank, waits until every rank published this epoch (up
+ * to the wait limit; status 7 and no output when it runs out), reads their
+ * slots over NVLink and writes the merged m, l, n and optional fp16 / bf16
+ * outputs. A rank starts call epoch + 2 only after its call epoch + 1 has
+ * returned on its stream (the two slots alternate). kvb_peer_buffer_close
+ * unmaps a peer's buffer and kvb_peer_buffer_free releases one's own.
+ * kvb_peer_buffer_bytes returns 0 for an invalid shape. */
+size_t kvb_peer_buffer_bytes(unsigned row_heads, unsigned dim);
+float* kvb_peer_slot(void* buffer, unsigned epoch, unsigned row_heads, unsigned dim);
+int kvb_peer_buffer_alloc(size_t bytes, void** buffer, unsigned char* handle64);
+int kvb_peer_buffer_open(const unsigned char* handle64, void** peer_buffer);
+int kvb_peer_buffer_close(void* peer_buffer);
+int kvb_peer_buffer_free(void* buffer);
+int kvb_merge_attention_peers(const void* const* buffers, unsigned world, unsigned rank, unsigned epoch,
+                              unsigned row_heads, unsigned dim, float* m, float* l, float* n, void* out_f16,
+                              void* out_bf16, void* stream);
+/* Test hook: copies `bytes` from host memory to a device address (for
+ * instance a peer buffer's flag or slot, which no tensor library wraps). */
+int kvb_debug_copy_to_device(void* dst, const void* src, size_t bytes);
 /* Reads and clears the kernels' device status word (0 = ok). Returns the
  * cudaError_t of the read. */
 int kvb_read_device_status(int* status);

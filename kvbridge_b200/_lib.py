@@ -183,6 +183,18 @@ SIGNATURES = {
         c_int,
         [ctypes.c_uint, ctypes.c_uint, ctypes.c_uint, c_void_p, c_void_p, c_void_p, c_size_t] + [c_void_p] * 6,
     ),
+    "kvb_peer_buffer_bytes": (c_size_t, [ctypes.c_uint, ctypes.c_uint]),
+    "kvb_peer_slot": (c_void_p, [c_void_p, ctypes.c_uint, ctypes.c_uint, ctypes.c_uint]),
+    "kvb_peer_buffer_alloc": (c_int, [c_size_t, POINTER(c_void_p), POINTER(ctypes.c_ubyte)]),
+    "kvb_peer_buffer_open": (c_int, [POINTER(ctypes.c_ubyte), POINTER(c_void_p)]),
+    "kvb_peer_buffer_close": (c_int, [c_void_p]),
+    "kvb_peer_buffer_free": (c_int, [c_void_p]),
+    "kvb_merge_attention_peers": (
+        c_int,
+        [POINTER(c_void_p), ctypes.c_uint, ctypes.c_uint, ctypes.c_uint, ctypes.c_uint, ctypes.c_uint]
+        + [c_void_p] * 6,
+    ),
+    "kvb_debug_copy_to_device": (c_int, [c_void_p, c_void_p, c_size_t]),
     "kvb_set_wait_limit_ns": (None, [ctypes.c_ulonglong]),
     "kvb_wait_limit_ns": (ctypes.c_ulonglong, []),
     "kvb_debug_fail_launch": (c_int, [ctypes.c_uint, c_int]),

@@ -342,6 +342,67 @@ def merge_attention_shards_ex(
     )
 
 
+def peer_buffer_bytes(row_heads: int, dim: int) -> int:
+    """Bytes of one rank's peer buffer for merge_attention_peers."""
+    n = int(_lib.load().kvb_peer_buffer_bytes(row_heads, dim))
+    if n == 0:
+        raise ValueError("row_heads must be positive and dim in [1, 256]")
+    return n
+
+
+def peer_slot(buffer: int, epoch: int, row_heads: int, dim: int) -> int:
+    """Device address of the slot call ``epoch`` writes its partials into
+    (packed [m | l | n] floats)."""
+    return int(_lib.load().kvb_peer_slot(buffer, epoch, row_heads, dim))
+
+
+def peer_buffer_alloc(nbytes: int) -> tuple[int, bytes]:
+    """Allocates (cudaMalloc, zeroed) and exports a peer buffer: returns its
+    device address and its 64-byte CUDA IPC handle."""
+    ptr = ctypes.c_void_p()
+    handle = (ctypes.c_ubyte * 64)()
+    check(_lib.load().kvb_peer_buffer_alloc(nbytes, ctypes.byref(ptr), handle))
+    return int(ptr.value), bytes(handle)
+
+
+def peer_buffer_open(handle: bytes) -> int:
+    """Maps another rank's peer buffer from its IPC handle; returns the address."""
+    if len(handle) != 64:
+        raise ValueError("a CUDA IPC handle is 64 bytes")
+    h = (ctypes.c_ubyte * 64).from_buffer_copy(handle)
+    ptr = ctypes.c_void_p()
+    check(_lib.load().kvb_peer_buffer_open(h, ctypes.byref(ptr)))
+    return int(ptr.value)
+
+
+def peer_buffer_close(peer_buffer: int) -> None:
+    check(_lib.load().kvb_peer_buffer_close(peer_buffer))
+
+
+def peer_buffer_free(buffer: int) -> None:
+    check(_lib.load().kvb_peer_buffer_free(buffer))
+
+
+def merge_attention_peers(buffers, rank: int, epoch: int, row_heads: int, dim: int, m, l, n,
+                          out_f16=None, out_bf16=None, stream=None) -> None:
+    """Exchange and merge of the ranks' shard partials over NVLink peer
+    memory (see include/kvbridge_c.h): ``buffers`` holds every rank's peer
+    buffer address, this rank's own at ``rank``."""
+    arr = (ctypes.c_void_p * len(buffers))(*[int(b) for b in buffers])
+    check(
+        _lib.load().kvb_merge_attention_peers(
+            arr, len(buffers), rank, epoch, row_heads, dim, _ptr(m), _ptr(l), _ptr(n), _ptr(out_f16),
+            _ptr(out_bf16), _stream(stream),
+        )
+    )
+
+
+def debug_copy_to_device(dst: int, data: bytes) -> None:
+    """Test hook: copies host bytes to a device address."""
+    buf = ctypes.create_string_buffer(data, len(data))
+    check(_lib.load().kvb_debug_copy_to_device(dst, buf, len(data)))
+
+
 def set_wait_limit_ns(ns: int) -> None:
     """Bound of any single pipeline wait in later launches (0 = default 2 s)."""
     _lib.load().kvb_set_wait_limit_ns(int(ns))

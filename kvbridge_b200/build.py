@@ -30,6 +30,7 @@ HEADERS = [
     "decode_tc.cuh",
     "decode_simt.cuh",
     "merge.cuh",
+    "peer_merge.cuh",
     "append_kv.cuh",
     "launch_checks.h",
 ]

@@ -23,6 +23,7 @@
 #include "decode_tma.cuh"
 #include "decode_tc.cuh"
 #include "merge.cuh"
+#include "peer_merge.cuh"
 #include "append_kv.cuh"
 
 namespace kvbridge {
@@ -853,6 +854,90 @@ void merge_attention_shards(unsigned shards, unsigned row_heads, unsigned dim,
                             float* m, float* l, float* n, void* out_f16, cudaStream_t stream) {
   merge_attention_shards_ex(shards, row_heads, dim, m_parts, l_parts, n_parts, 0, m, l, n, out_f16,
                             nullptr, stream);
+}
+
+// ---------------------------------------------------------------------------
+// Cross-GPU merge over NVLink peer memory (peer_merge.cuh).
+
+size_t peer_buffer_bytes(unsigned row_heads, unsigned dim) {
+  if (row_heads == 0 || dim == 0 || dim > 256)
+    throw std::invalid_argument("row_heads must be positive and dim in [1,256]");
+  return kvb::kPeerFlagBytes + 2 * kvb::peer_slot_floats(row_heads, dim) * sizeof(float);
+}
+
+float* peer_slot(void* buffer, unsigned epoch, unsigned row_heads, unsigned dim) {
+  if (buffer == nullptr) throw std::invalid_argument("peer buffer is null");
+  return reinterpret_cast<float*>(static_cast<char*>(buffer) + kvb::kPeerFlagBytes) +
+         (epoch & 1u) * kvb::peer_slot_floats(row_heads, dim);
+}
+
+void peer_buffer_alloc(size_t bytes, void** buffer, unsigned char handle[64]) {
+  static_assert(sizeof(cudaIpcMemHandle_t) == 64, "CUDA IPC handles are 64 bytes");
+  if (buffer == nullptr || handle == nullptr) throw std::invalid_argument("output pointers are null");
+  if (bytes < kvb::kPeerFlagBytes) throw std::invalid_argument("peer buffer smaller than its flag block");
+  void* p = nullptr;
+  cuda_ok(cudaMalloc(&p, bytes), "peer buffer cudaMalloc");
+  // Flags start at 0 (epochs count from 1).
+  cudaError_t code = cudaMemset(p, 0, bytes);
+  cudaIpcMemHandle_t h{};
+  if (code == cudaSuccess) code = cudaIpcGetMemHandle(&h, p);
+  if (code != cudaSuccess) {
+    cudaFree(p);
+    cuda_ok(code, "peer buffer export");
+  }
+  std::memcpy(handle, &h, sizeof(h));
+  *buffer = p;
+}
+
+void peer_buffer_open(const unsigned char handle[64], void** peer_buffer) {
+  if (handle == nullptr || peer_buffer == nullptr) throw std::invalid_argument("handle or output is null");
+  cudaIpcMemHandle_t h{};
+  std::memcpy(&h, handle, sizeof(h));
+  cuda_ok(cudaIpcOpenMemHandle(peer_buffer, h, cudaIpcMemLazyEnablePeerAccess), "peer buffer open");
+}
+
+void peer_buffer_close(void* peer_buffer) {
+  if (peer_buffer != nullptr) cuda_ok(cudaIpcCloseMemHandle(peer_buffer), "peer buffer close");
+}
+
+void peer_buffer_free(void* buffer) {
+  if (buffer != nullptr) cuda_ok(cudaFree(buffer), "peer buffer free");
+}
+
+void merge_attention_peers(const void* const* buffers, unsigned world, unsigned rank, unsigned epoch,
+                           unsigned row_heads, unsigned dim, float* m, float* l, float* n, void* out_f16,
+                           void* out_bf16, cudaStream_t stream) {
+  if (world == 0 || world > kvb::kMaxPeers || rank >= world)
+    throw std::invalid_argument("world must be in [1, 8] and rank below it");
+  if (epoch == 0) throw std::invalid_argument("epochs count from 1");
+  if (row_heads == 0 || dim == 0 || dim > 256)
+    throw std::invalid_argument("row_heads must be positive and dim in [1,256]");
+  if (buffers == nullptr || !m || !l || !n) throw std::invalid_argument("peer merge buffers must be non-null");
+  kvb::PeerMergeParams pp{};
+  for (unsigned i = 0; i < world; ++i) {
+    if (buffers[i] == nullptr || !aligned_to(buffers[i], 16))
+      throw std::invalid_argument("peer buffers must be non-null and 16-byte aligned");
+    pp.peers[i] = static_cast<const float*>(buffers[i]);
+  }
+  pp.world = world;
+  pp.rank = rank;
+  pp.epoch = epoch;
+  pp.row_heads = row_heads;
+  pp.dim = dim;
+  pp.m = m;
+  pp.l = l;
+  pp.n = n;
+  pp.out = static_cast<__half*>(out_f16);
+  pp.out_bf16 = static_cast<__nv_bfloat16*>(out_bf16);
+  pp.wait_limit_ns = wait_limit_ns();
+  const uint32_t kd = (dim + 31) / 32;
+  const void* fn = kd <= 1   ? reinterpret_cast<const void*>(&kvb::merge_peers_kernel<1>)
+                   : kd <= 2 ? reinterpret_cast<const void*>(&kvb::merge_peers_kernel<2>)
+                   : kd <= 4 ? reinterpret_cast<const void*>(&kvb::merge_peers_kernel<4>)
+                             : reinterpret_cast<const void*>(&kvb::merge_peers_kernel<8>);
+  void* args[] = {&pp};
+  launch_pdl(fn, dim3((row_heads + kvb::kPeerMergeWarps - 1) / kvb::kPeerMergeWarps),
+             dim3(32 * kvb::kPeerMergeWarps), 0, stream, args, "peer merge launch");
 }
 
 // ---------------------------------------------------------------------------

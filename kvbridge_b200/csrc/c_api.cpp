@@ -302,6 +302,51 @@ int kvb_merge_attention_shards_ex(unsigned shards, unsigned row_heads, unsigned 
   });
 }
 
+size_t kvb_peer_buffer_bytes(unsigned row_heads, unsigned dim) {
+  try {
+    return kvbridge::peer_buffer_bytes(row_heads, dim);
+  } catch (...) {
+    return 0;
+  }
+}
+
+float* kvb_peer_slot(void* buffer, unsigned epoch, unsigned row_heads, unsigned dim) {
+  return buffer == nullptr ? nullptr : kvbridge::peer_slot(buffer, epoch, row_heads, dim);
+}
+
+int kvb_peer_buffer_alloc(size_t bytes, void** buffer, unsigned char* handle64) {
+  return guarded([&] { kvbridge::peer_buffer_alloc(bytes, buffer, handle64); });
+}
+
+int kvb_peer_buffer_open(const unsigned char* handle64, void** peer_buffer) {
+  return guarded([&] { kvbridge::peer_buffer_open(handle64, peer_buffer); });
+}
+
+int kvb_peer_buffer_close(void* peer_buffer) {
+  return guarded([&] { kvbridge::peer_buffer_close(peer_buffer); });
+}
+
+int kvb_peer_buffer_free(void* buffer) {
+  return guarded([&] { kvbridge::peer_buffer_free(buffer); });
+}
+
+int kvb_merge_attention_peers(const void* const* buffers, unsigned world, unsigned rank, unsigned epoch,
+                              unsigned row_heads, unsigned dim, float* m, float* l, float* n, void* out_f16,
+                              void* out_bf16, void* stream) {
+  return guarded([&] {
+    kvbridge::merge_attention_peers(buffers, world, rank, epoch, row_heads, dim, m, l, n, out_f16, out_bf16,
+                                    as_stream(stream));
+  });
+}
+
+int kvb_debug_copy_to_device(void* dst, const void* src, size_t bytes) {
+  return guarded([&] {
+    if (dst == nullptr || src == nullptr) throw std::invalid_argument("null pointer");
+    const cudaError_t code = cudaMemcpy(dst, src, bytes, cudaMemcpyHostToDevice);
+    if (code != cudaSuccess) throw std::runtime_error(std::string("copy: ") + cudaGetErrorString(code));
+  });
+}
+
 int kvb_read_device_status(int* status) { return int(kvbridge::read_device_status(status)); }
 
 void kvb_set_wait_limit_ns(unsigned long long ns) { kvbridge::set_wait_limit_ns(ns); }

@@ -14,7 +14,10 @@ Two modes, one process per GPU over ``torch.distributed``:
   295-335) with one "split" per rank.
 
 The exchange and merge functions are parameters so the orchestration runs
-unchanged on CPU ``gloo`` ranks in the tests.
+unchanged on CPU ``gloo`` ranks in the tests. On GPUs that reach each other
+over NVLink, ``PeerExchange`` replaces the all-gather and the merge with one
+kernel that reads the other ranks' partials from their memory
+(merge_attention_peers).
 """
 from __future__ import annotations
 
@@ -149,3 +152,53 @@ def gpu_shard_merge(rh: int, dim: int, out_f16: bool = True):
         return m, l, n, out
 
     return merge
+
+
+class PeerExchange:
+    """Sequence-shard exchange over NVLink peer memory for one process group:
+    every rank allocates a peer buffer (``api.peer_buffer_alloc``), the CUDA IPC
+    handles are all-gathered once, and each rank maps the others' buffers.
+    Per call: ``slot()`` gives the address of this call's slot (packed
+    [m | l | n] floats) for the local decode to write its partials into, and
+    ``merge(...)`` launches the kernel that publishes the slot, waits for the
+    other ranks' and merges them all into m, l, n (and an fp16 / bf16 output).
+    Every rank must make the same sequence of calls; the epoch (call number)
+    advances in ``slot()``. ``close()`` unmaps and frees the buffers."""
+
+    def __init__(self, row_heads: int, dim: int, group=None):
+        import torch.distributed as dist
+
+        from . import api
+
+        self._api = api
+        self.row_heads, self.dim = row_heads, dim
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.own, handle = api.peer_buffer_alloc(api.peer_buffer_bytes(row_heads, dim))
+        handles: list = [None] * self.world
+        dist.all_gather_object(handles, handle, group=group)
+        self.buffers = [self.own if r == self.rank else api.peer_buffer_open(h) for r, h in enumerate(handles)]
+        # Every rank has mapped every buffer (and the zeroed flags are in
+        # place) before any rank publishes into another's.
+        dist.barrier(group=group)
+        self.epoch = 0
+
+    def slot(self):
+        """Starts the next call; returns (m, l, n) addresses of its slot."""
+        self.epoch += 1
+        base = self._api.peer_slot(self.own, self.epoch, self.row_heads, self.dim)
+        return base, base + 4 * self.row_heads, base + 8 * self.row_heads
+
+    def merge(self, m, l, n, out_f16=None, out_bf16=None, stream=None) -> None:
+        self._api.merge_attention_peers(self.buffers, self.rank, self.epoch, self.row_heads, self.dim, m, l, n,
+                                        out_f16, out_bf16, stream)
+
+    def close(self) -> None:
+        """Releases the mappings and the buffer; every rank's kernels that
+        read them must have finished (synchronize, then a barrier)."""
+        for r, b in enumerate(self.buffers):
+            if r != self.rank:
+                self._api.peer_buffer_close(b)
+        self._api.peer_buffer_free(self.own)
+        self.buffers = []
