@@ -799,6 +799,7 @@ void launch_attention_batched(const BatchShape& s, const BatchInput& in, void* w
   prm.col_groups = 1;
   prm.group_cols = columns_of(batched_nt(group));
   prm.score_scale = s.scale;
+  prm.prefetch_stages = kPrefetchStages;
   prm.wait_limit_ns = wait_limit_ns();
   prm.fault_stage = take_skip_stage();
   set_gather_maps(prm, s.dim, s.pages);

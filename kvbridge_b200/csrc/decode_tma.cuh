@@ -69,8 +69,8 @@ struct DecodeParams {
   uint32_t ctas;
   uint64_t total_stages;  // single sequence only (batched computes it)
   float score_scale;
-  // Single sequence: L2 prefetch of the CTA's first `prefetch_stages` stages
-  // before the dependency wait on the preceding grid (0 = none).
+  // L2 prefetch of the CTA's first `prefetch_stages` stages before the
+  // dependency wait on the preceding grid (0 = none).
   uint32_t prefetch_stages;
   // Single sequence: the query columns (rows * group per KV head) are cut
   // into col_groups groups of group_cols (= 8 * NT) columns; CTA c works on
@@ -237,18 +237,23 @@ struct Piece {
   uint32_t col0;       // first query column of the CTA's column group
 };
 
+// HINT: a read before the dependency wait on the preceding grid, through L2
+// only (ld.global.cg), so that no possibly stale copy stays in L1 for the
+// reads after the wait; such values only steer prefetches.
+template <bool HINT = false>
 __device__ __forceinline__ uint32_t clamped_len(const DecodeParams& p, uint32_t b) {
-  const uint32_t len = p.seq_lens[b];
+  const uint32_t len = HINT ? __ldcg(p.seq_lens + b) : p.seq_lens[b];
   return len > p.max_tokens ? p.max_tokens : len;
 }
 
 // Warp-cooperative: total stages of a batched call.
+template <bool HINT = false>
 __device__ __forceinline__ uint64_t batched_total(const DecodeParams& p) {
   const uint32_t lane = threadIdx.x & 31;
   uint64_t total = 0;
   for (uint32_t base = 0; base < p.batch; base += 32) {
     const uint32_t b = base + lane;
-    const uint32_t t = b < p.batch ? stages_of_range(0, clamped_len(p, b)) : 0;
+    const uint32_t t = b < p.batch ? stages_of_range(0, clamped_len<HINT>(p, b)) : 0;
     uint64_t s = t;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
@@ -259,13 +264,14 @@ __device__ __forceinline__ uint64_t batched_total(const DecodeParams& p) {
 
 // Warp-cooperative: sequence b whose segments hold global stage x, and the
 // number of stages of all earlier sequences (per KV head).
+template <bool HINT = false>
 __device__ __forceinline__ void batched_locate(const DecodeParams& p, uint64_t x, uint32_t& b_out,
                                                uint64_t& pref_out) {
   const uint32_t lane = threadIdx.x & 31;
   uint64_t pref = 0;
   for (uint32_t base = 0; base < p.batch; base += 32) {
     const uint32_t b = base + lane;
-    const uint64_t t = b < p.batch ? stages_of_range(0, clamped_len(p, b)) : 0;
+    const uint64_t t = b < p.batch ? stages_of_range(0, clamped_len<HINT>(p, b)) : 0;
     uint64_t incl = t;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
@@ -399,6 +405,47 @@ __device__ void prefetch_first_stages(const DecodeParams& p, const Piece& pc, ui
     const uint32_t phys = __ldcg(p.table + pg);
     if (phys >= p.pages) continue;
     const size_t unit = size_t(phys) * p.kv_heads + pc.h;
+    prefetch_l2(p.k + unit * P * D, P * D);
+    prefetch_l2(p.v + unit * D * P, D * P);
+    prefetch_l2(p.k_scales + unit * P, 4 * P);
+    prefetch_l2(p.v_scales + unit * P, 4 * P);
+  }
+}
+
+// Batched, before the dependency wait on the preceding grid: L2 prefetch of
+// the K/V pages and scales of the CTA's first `count` stages (within its
+// first piece). The preceding grid may still be writing seq_lens, the block
+// table or the pages, so everything here is read through L2 only and steers
+// prefetches alone (entries that point outside the pool are skipped); the
+// producer locates its pieces and reads the table again after the wait.
+template <int D>
+__device__ void prefetch_first_stages_batched(const DecodeParams& p, uint32_t count) {
+  const uint32_t lane = threadIdx.x & 31;
+  const uint64_t total = batched_total<true>(p);
+  const uint64_t x0 = cta_stage_begin(blockIdx.x, total, p.ctas);
+  const uint64_t x1 = cta_stage_begin(blockIdx.x + 1, total, p.ctas);
+  if (x0 >= x1) return;
+  uint32_t b;
+  uint64_t pref;
+  batched_locate<true>(p, x0, b, pref);
+  if (b >= p.batch) return;
+  const uint32_t len = clamped_len<true>(p, b);
+  const uint32_t t = stages_of_range(0, len);
+  if (t == 0) return;
+  const uint64_t seg_base = pref * p.kv_heads;
+  const uint32_t h = static_cast<uint32_t>((x0 - seg_base) / t);
+  if (h >= p.kv_heads) return;
+  const uint32_t j0 = static_cast<uint32_t>(x0 - seg_base - uint64_t(h) * t);
+  const uint32_t j1 = static_cast<uint32_t>(min(uint64_t(t), uint64_t(j0) + min(uint64_t(count), x1 - x0)));
+  const uint32_t tok_lo = j0 * kStageTokens, tok_hi = min(len, j1 * kStageTokens);
+  if (tok_hi <= tok_lo) return;
+  const uint32_t* trow = p.table + size_t(b) * p.table_stride;
+  const uint32_t P = p.page_tokens;
+  const uint32_t pg1 = (tok_hi - 1) >> p.log2_page;
+  for (uint32_t pg = (tok_lo >> p.log2_page) + lane; pg <= pg1; pg += 32) {
+    const uint32_t phys = __ldcg(trow + pg);
+    if (phys >= p.pages) continue;
+    const size_t unit = size_t(phys) * p.kv_heads + h;
     prefetch_l2(p.k + unit * P * D, P * D);
     prefetch_l2(p.v + unit * D * P, D * P);
     prefetch_l2(p.k_scales + unit * P, 4 * P);
@@ -1185,6 +1232,7 @@ __device__ __forceinline__ void decode_partial_body(const KernelParams<SMALL_PAG
   const Piece only = !BATCHED ? single_piece(p, blockIdx.x) : Piece{};
   if (warp == kProducerWarp) {
     if (!BATCHED && p.prefetch_stages != 0) prefetch_first_stages<D>(p, only, p.prefetch_stages);
+    if (BATCHED && p.prefetch_stages != 0) prefetch_first_stages_batched<D>(p, p.prefetch_stages);
     if constexpr (SMALL_PAGES)
       produce_small_pages<D, STAGES, BATCHED>(p, only, ring, full, empty, tags, abort_flag);
     else

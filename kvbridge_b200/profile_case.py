@@ -9,6 +9,7 @@ profiler's replay passes):
   cfg2            B1, 65,536 ctx, 32/8 heads, dim 128, Page64 shuffled
   cfg2-rank4      one rank's share of cfg2 split over 4 GPUs (8/2 heads)
   cfg2-rank8      one rank's share of cfg2 split over 8 GPUs (4/1 heads)
+  cfg3            the whole cfg3 batch: 32 ragged lengths U[1K, 32K], Page64 shared pool
   cfg3-slice      batch 8 of the cfg3 ragged lengths, Page64 shared pool
   cfg4-slice      batch 8 x 16,384, 64/8 heads, Page16, 1 % 10x outliers
   cfg4-slice-p64  the same on 64-token pages (the page size's own cost)
@@ -26,7 +27,7 @@ import torch
 
 from . import api, build, synth
 
-CASES = ("cfg1", "cfg2", "cfg2-rank4", "cfg2-rank8", "cfg3-slice", "cfg4-slice", "cfg4-slice-p64", "cfg5-slice", "native")
+CASES = ("cfg1", "cfg2", "cfg2-rank4", "cfg2-rank8", "cfg3", "cfg3-slice", "cfg4-slice", "cfg4-slice-p64", "cfg5-slice", "native")
 
 
 def _single(case: synth.SingleCase, partitions: int):
@@ -72,8 +73,9 @@ def make_call(name: str, device):
     if name in ("cfg2-rank4", "cfg2-rank8"):
         kv = 2 if name == "cfg2-rank4" else 1
         return _single(synth.make_single(1, 4 * kv, kv, 128, 64, 65536, seed + 2, device), 0)
-    if name == "cfg3-slice":
-        lens = synth.ragged_lengths(32, 1024, 32768, seed=seed + 3)[:8]
+    if name in ("cfg3", "cfg3-slice"):
+        lens = synth.ragged_lengths(32, 1024, 32768, seed=seed + 3)
+        lens = lens if name == "cfg3" else lens[:8]
         return _batched(synth.make_batched(32, 8, 128, 64, lens, seed + 3, device))
     if name in ("cfg4-slice", "cfg4-slice-p64"):
         page = 16 if name == "cfg4-slice" else 64
