@@ -10,8 +10,8 @@
 // `epoch` (1, 2, ...) of a rank writes its decode partials into slot
 // epoch % 2 of its own buffer; its merge kernel then
 //   1. waits for the decode (programmatic dependent launch),
-//   2. after a system-scope fence, stores `epoch` into its flag in every
-//      rank's buffer (flag word `rank`),
+//   2. stores `epoch` into its flag in every rank's buffer (flag word
+//      `rank`) with system-scope release stores,
 //   3. waits, bounded by wait_limit_ns, until its own flag block shows
 //      `epoch` from every rank,
 //   4. reads every rank's slot over NVLink and merges (one warp per
@@ -53,8 +53,8 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
   return v;
 }
 
-__device__ __forceinline__ void st_relaxed_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
 // KD = dims a lane holds (ceil(dim / 32)).
@@ -66,14 +66,15 @@ __global__ void __launch_bounds__(32 * kPeerMergeWarps) merge_peers_kernel(PeerM
   const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const uint32_t RH = p.row_heads, D = p.dim;
 
-  // 2. Publish this rank's slot to every rank. Every CTA stores the same
-  //    value, so that no CTA's wait below depends on another CTA of this grid.
+  // 2. Publish this rank's slot to every rank: release stores, ordering the
+  //    slot's writes (which the preceding grid completed) before the flag.
+  //    Every CTA stores the same value, so that no CTA's wait below depends
+  //    on another CTA of this grid.
   if (threadIdx.x < p.world) {
-    __threadfence_system();
-    uint32_t* flags = reinterpret_cast<uint32_t*>(const_cast<float*>(p.peers[threadIdx.x]));
-    st_relaxed_sys(flags + p.rank, p.epoch);
+    uint32_t* peer_flags = reinterpret_cast<uint32_t*>(const_cast<float*>(p.peers[threadIdx.x]));
+    st_release_sys(peer_flags + p.rank, p.epoch);
   }
-  // 3. Wait for every rank's slot of this epoch.
+  // 3. Wait for every rank's slot of this epoch (acquire loads).
   if (threadIdx.x == 0) {
     const uint32_t* flags = reinterpret_cast<const uint32_t*>(p.peers[p.rank]);
     const unsigned long long start = global_ns();

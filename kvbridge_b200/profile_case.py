@@ -16,6 +16,8 @@ profiler's replay passes):
   cfg5-slice      batch 4 x 131,072 tokens (one eighth of each cfg5 sequence)
   native          the reference's native shape: rows 8, 24/4 heads, dim 256,
                   Page32, 32,768 ctx
+  peer-merge      merge_attention_peers with one rank (cfg5's partial shape: 4 x
+                  32 row-heads, dim 128), the kernel's own work without NVLink
 ``--kernel warp|tcgen05`` forces the single-sequence partial kernel.
 """
 from __future__ import annotations
@@ -27,7 +29,7 @@ import torch
 
 from . import api, build, synth
 
-CASES = ("cfg1", "cfg2", "cfg2-rank4", "cfg2-rank8", "cfg3", "cfg3-slice", "cfg4-slice", "cfg4-slice-p64", "cfg5-slice", "native")
+CASES = ("peer-merge", "cfg1", "cfg2", "cfg2-rank4", "cfg2-rank8", "cfg3", "cfg3-slice", "cfg4-slice", "cfg4-slice-p64", "cfg5-slice", "native")
 
 
 def _single(case: synth.SingleCase, partitions: int):
@@ -64,8 +66,34 @@ def _batched(bc: synth.BatchCase):
     return call
 
 
+def _peer_merge(device):
+    import numpy as np
+
+    rh, dim = 4 * 32, 128
+    own, _ = api.peer_buffer_alloc(api.peer_buffer_bytes(rh, dim))
+    g = np.random.default_rng(7)
+    m = g.normal(0, 3, rh).astype(np.float32)
+    l = g.uniform(0.5, 40, rh).astype(np.float32)
+    n = g.normal(0, 5, rh * dim).astype(np.float32)
+    for epoch in (1, 2):
+        api.debug_copy_to_device(api.peer_slot(own, epoch, rh, dim), m.tobytes() + l.tobytes() + n.tobytes())
+    mo = torch.empty(rh, device=device)
+    lo = torch.empty(rh, device=device)
+    no = torch.empty(rh * dim, device=device)
+    out = torch.empty(rh * dim, dtype=torch.float16, device=device)
+    state = {"epoch": 0}
+
+    def call():
+        state["epoch"] += 1
+        api.merge_attention_peers([own], 0, state["epoch"], rh, dim, mo, lo, no, out)
+
+    return call
+
+
 def make_call(name: str, device):
     seed = 0xC0FFEE
+    if name == "peer-merge":
+        return _peer_merge(device)
     if name == "cfg1":
         return _single(synth.make_single(1, 32, 8, 128, 64, 4096, seed + 1, device), 8)
     if name == "cfg2":
