@@ -186,6 +186,8 @@ class PeerExchange:
 
     def slot(self):
         """Starts the next call; returns (m, l, n) addresses of its slot."""
+        if not self.buffers:
+            raise RuntimeError("the exchange is closed")
         self.epoch += 1
         base = self._api.peer_slot(self.own, self.epoch, self.row_heads, self.dim)
         return base, base + 4 * self.row_heads, base + 8 * self.row_heads
@@ -195,10 +197,14 @@ class PeerExchange:
                                         out_f16, out_bf16, stream)
 
     def close(self) -> None:
-        """Releases the mappings and the buffer; every rank's kernels that
-        read them must have finished (synchronize, then a barrier)."""
+        """Releases the mappings and the buffer (once; later calls do
+        nothing); every rank's kernels that read them must have finished
+        (synchronize, then a barrier)."""
+        if not self.buffers:
+            return
         for r, b in enumerate(self.buffers):
             if r != self.rank:
                 self._api.peer_buffer_close(b)
         self._api.peer_buffer_free(self.own)
         self.buffers = []
+        self.own = 0
