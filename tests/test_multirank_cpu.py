@@ -92,3 +92,61 @@ def test_range_planning():
     with pytest.raises(ValueError):
         sharding.kv_head_range(8, 3, 0)
     assert sharding.local_pages([(64, 200)], 0, 64) == (1, 4)
+
+
+def _peer_worker(rank, world, port, results):
+    """PeerExchange's host logic with the buffer calls faked (no GPU): each
+    rank 'allocates' a buffer at a rank-specific address with a rank-specific
+    handle, and the exchange must map exactly the other ranks' handles, count
+    epochs alike, address the alternating slots (the library's own
+    arithmetic) and release everything once."""
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    from datetime import timedelta
+
+    from kvbridge_b200 import api
+
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
+    try:
+        base = lambda r: 0x7F0000000000 + (r << 32)  # noqa: E731
+        handle = lambda r: bytes([r + 1]) * 64  # noqa: E731
+        opened, closed, freed = [], [], []
+        api.peer_buffer_alloc = lambda nbytes: (base(rank), handle(rank))
+        api.peer_buffer_open = lambda h: (opened.append(h), base(h[0] - 1))[1]
+        api.peer_buffer_close = lambda b: closed.append(b)
+        api.peer_buffer_free = lambda b: freed.append(b)
+        rh, dim = 96, 128
+        ex = sharding.PeerExchange(rh, dim)
+        ok = ex.buffers == [base(r) for r in range(world)]
+        ok = ok and sorted(opened) == sorted(handle(r) for r in range(world) if r != rank)
+        slot_bytes = rh * (dim + 2) * 4
+        for epoch in (1, 2, 3):
+            m, l, n = ex.slot()
+            want = base(rank) + 256 + (epoch & 1) * slot_bytes
+            ok = ok and ex.epoch == epoch and (m, l, n) == (want, want + 4 * rh, want + 8 * rh)
+        ex.close()
+        ex.close()
+        ok = ok and sorted(closed) == [base(r) for r in range(world) if r != rank] and freed == [base(rank)]
+        try:
+            ex.slot()
+            ok = False
+        except RuntimeError:
+            pass
+        results[rank] = bool(ok)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_peer_exchange_host_logic_gloo():
+    world = 3
+    ctx = mp.get_context("spawn")
+    manager = ctx.Manager()
+    results = manager.dict()
+    port = _free_port()
+    procs = [ctx.Process(target=_peer_worker, args=(r, world, port, results)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    assert all(results[r] for r in range(world))
