@@ -227,7 +227,7 @@ int kvb_decode_kernel(void);
 
 /* Event timeline of the tcgen05 partial kernel, in libraries built with the
  * trace flag (python -m kvbridge_b200.build --trace): copies up to `count`
- * SM clock stamps [16 CTAs][16 tiles][15 events] of the latest launches
+ * SM clock stamps [16 CTAs][16 tiles][18 events] of the latest launches
  * and clears them. Other builds return KVB_EINVAL. */
 int kvb_debug_read_tc_trace(unsigned long long* out, size_t count);
 

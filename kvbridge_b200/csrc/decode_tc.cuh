@@ -62,7 +62,7 @@ struct DecodeParamsTc : DecodeParams {
 // (clock64; one CTA runs on one SM, so differences within a CTA are exact) of
 // the first kTraceCtas CTAs and kTraceTiles tiles of the last launch, read by
 // the host with kvb_debug_read_tc_trace. Events per tile: see kTrace*.
-constexpr uint32_t kTraceCtas = 16, kTraceTiles = 16, kTraceEvents = 15;
+constexpr uint32_t kTraceCtas = 16, kTraceTiles = 16, kTraceEvents = 18;
 enum : uint32_t {
   kTraceStart = 0,       // tile 0 only: the CTA passed its setup barrier
   kTraceQkIssued = 1,    // MMA thread issued QK(t) (its stages had landed)
@@ -79,6 +79,7 @@ enum : uint32_t {
   kTraceOFreeSeen = 12,   // MMA thread first saw O^T released for PV(t)
   kTraceVSeen = 13,       // MMA thread first saw V(t) landed
   kTraceSmStored = 14,    // softmax warp 0 finished its P digit stores (before the proxy fence)
+  kTracePGroup = 15,      // + g (g < 3): softmax warp 0 finished the P digits of column group g (4 columns)
 };
 #ifdef KVB_TC_TRACE
 __device__ unsigned long long g_tc_trace[kTraceCtas][kTraceTiles][kTraceEvents];
@@ -653,6 +654,7 @@ __global__ void __maxnreg__((TcSmem<D, P, NC, SLOTS, NH>::kMaxRegs))
               pt[(2 * c + 1) * 16u] = uint8_t((ub[i] - int(0x4B400000u) + 128) >> 8);
             }
           }
+          if (threadIdx.x == 0 && j4 / 4 < 3) KVB_TC_MARK(t, kTracePGroup + j4 / 4);
         }
         if (threadIdx.x == 0) KVB_TC_MARK(t, kTraceSmStored);
         tc::fence_proxy_async_smem();

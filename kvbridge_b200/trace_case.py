@@ -20,6 +20,8 @@ them:
   o_seen MMA thread saw O^T released by the fold   (kTraceOFreeSeen)
   v_seen MMA thread saw the tile's V landed         (kTraceVSeen)
   sm_st  softmax warp 0 finished its P stores (before its proxy fence) (kTraceSmStored)
+  p_g0..p_g2  softmax warp 0 finished the P digits of its column group 0, 1, 2
+         (4 columns each; group 3 ends at sm_st) (kTracePGroup)
 
 ``--kernel warp`` prints instead the per-CTA timeline of the warp-level
 partial kernel (decode_tma.cuh, CtaTraceEvent) for the last of
@@ -42,8 +44,9 @@ import os
 import statistics
 import sys
 
-CTAS, TILES, EVENTS = 16, 16, 15
-NAMES = ["start", "qk", "sm_in", "sm_out", "pv", "f_in", "f_out", "copy", "sm_ld", "sm_red", "sm_par", "p_seen", "o_seen", "v_seen", "sm_st"]
+CTAS, TILES, EVENTS = 16, 16, 18
+NAMES = ["start", "qk", "sm_in", "sm_out", "pv", "f_in", "f_out", "copy", "sm_ld", "sm_red", "sm_par", "p_seen", "o_seen",
+         "v_seen", "sm_st", "p_g0", "p_g1", "p_g2"]
 
 
 # CtaTraceEvent of decode_tma.cuh.
