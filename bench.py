@@ -85,11 +85,13 @@ def parse_args():
     ap.add_argument("--block-calls", type=int, default=500, help="calls per CUDA graph (rounded to whole step blocks)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extra", action="store_true", help="skip the weak-scaling and cfg5 keys")
-    ap.add_argument("--config", choices=["cfg2", "cfg1", "cfg3", "cfg4", "cfg5", "native"], default="cfg2",
+    ap.add_argument("--config", choices=["cfg2", "cfg1", "cfg3", "cfg4", "cfg5", "native", "f32"], default="cfg2",
                     help="BASELINE workload; the headline line is cfg2, the others are informational "
-                         "(native: the reference MMA kernel's rows-8 / 24-4 heads / dim-256 / Page32 shape)")
-    ap.add_argument("--kernel", choices=["auto", "warp", "tcgen05"], default="auto",
-                    help="single-sequence partial kernel (auto = chosen by shape)")
+                         "(native: the reference MMA kernel's rows-8 / 24-4 heads / dim-256 / Page32 shape; "
+                         "f32: cfg2's geometry with fp32 KV)")
+    ap.add_argument("--kernel", choices=["auto", "warp", "tcgen05", "general"], default="auto",
+                    help="single-sequence partial kernel (auto = chosen by shape; general = the CUDA-core "
+                         "kernel for every call)")
     return ap.parse_args()
 
 
@@ -448,7 +450,7 @@ def main():
     if rc != 0:
         raise RuntimeError(f"preload_attention_kernels failed: cudaError {rc}")
     kvb.set_decode_kernel({"auto": kvb.KERNEL_AUTO, "warp": kvb.KERNEL_WARP_MMA,
-                           "tcgen05": kvb.KERNEL_TCGEN05}[args.kernel])
+                           "tcgen05": kvb.KERNEL_TCGEN05, "general": kvb.KERNEL_GENERAL}[args.kernel])
     if args.config != "cfg2":
         return run_other_config(args, world, rank, local_rank, device)
     if 8 % world:
@@ -893,6 +895,34 @@ def run_other_config(args, world, rank, local_rank, device):
             desc = dict(workload="native: rows 8 (causal), 24/4 heads, dim 256, Page32, 32,768 ctx, "
                                  "launch_attention_mma", scaling="weak",
                         kernel=args.kernel, partitions=kvb.attention_partitions(shape, 0))
+        elif cfg == "f32":
+            # cfg2's geometry with fp32 K/V ~N(0,1) (Shape.int8 = False):
+            # 65,536 tokens, 32/8 heads, dim 128, 64-token shuffled pages;
+            # two resident layers of 537 MB (each > 4x L2) alternate.
+            tokens = 65536
+            base = synth.make_single(rows=1, q_heads=32, kv_heads=8, dim=128, page_tokens=64, tokens=tokens,
+                                     seed=0xC0FFEE + 32 + rank, device=device)
+            shape = kvb.Shape(**{**base.shape.__dict__, "int8": False})
+            gen = torch.Generator(device=device)
+            gen.manual_seed(0xF32 + rank)
+            pools = [(torch.randn(shape.pages * 8 * 64 * 128, generator=gen, device=device),
+                      torch.randn(shape.pages * 8 * 128 * 64, generator=gen, device=device)) for _ in range(2)]
+            inps = [synth.SingleCase(shape, base.q, base.q_positions, base.k_positions, base.page_table,
+                                     k, v, None, None).device_input() for k, v in pools]
+            scratch = torch.empty(kvb.scratch_elements(shape), device=device)
+            m = torch.empty(32, device=device)
+            l = torch.empty(32, device=device)
+            n = torch.empty(32 * 128, device=device)
+            out = torch.empty(32 * 128, dtype=torch.float16, device=device)
+
+            def step(i):
+                kvb.launch_attention_ex(shape, inps[i % 2], scratch, m, l, n, partitions=args.partitions,
+                                        out_f16=out)
+
+            total_bytes = world * tokens * 8 * 2 * 128 * 4
+            desc = dict(workload="f32: cfg2 geometry with fp32 KV (B1, 65,536 ctx, 32/8 heads, dim 128, "
+                                 "Page64 shuffled)", scaling="weak", kernel=args.kernel,
+                        kv_bytes_per_token="8 KV heads x 2 x 128 x 4 B = 8,192 B")
         else:
             if cfg == "cfg3":
                 lens = synth.ragged_lengths(32, 1024, 32768, seed=0xC0FFEE + 3)
@@ -938,7 +968,7 @@ def run_other_config(args, world, rank, local_rank, device):
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(per, 6), "higher_is_better": True,
-        "scaling": desc.pop("scaling"), "vs_baseline": None, "dtype": "int8",
+        "scaling": desc.pop("scaling"), "vs_baseline": None, "dtype": "f32" if cfg == "f32" else "int8",
         "data": "synthetic (seeded; BASELINE value distributions)",
         "pct_of_hbm_peak_per_gpu": round(100 * value / world / peak, 2), "peak": f"{peak} GB/s ({peak_kind})",
         "config": dict(desc, kv_bytes_per_step=total_bytes, launch=timing),

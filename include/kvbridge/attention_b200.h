@@ -189,8 +189,11 @@ void fail_launch(unsigned nth, cudaError_t code) noexcept;
 void skip_stage(unsigned stage) noexcept;
 // Which single-sequence partial kernel later calls use (process-wide): 0 =
 // chosen by shape (default), 1 = the warp-level MMA kernel, 2 = the tcgen05
-// (TMEM accumulator) kernel wherever it has a variant for the shape. For
-// side-by-side measurements and tests; results agree within the tolerance.
+// (TMEM accumulator) kernel wherever it has a variant for the shape, 3 = the
+// general CUDA-core kernel for every launch_attention / launch_attention_ex
+// call (int8 or fp32 KV; the partials-only entry points keep the
+// tensor-core kernels). For side-by-side measurements and tests; results
+// agree within the tolerance.
 void set_decode_kernel(int choice) noexcept;
 int decode_kernel() noexcept;
 }  // namespace detail

@@ -216,12 +216,14 @@ int kvb_debug_skip_stage(unsigned stage);
 /* Which single-sequence partial kernel later calls use (process-wide):
  * KVB_KERNEL_AUTO chooses by shape, KVB_KERNEL_WARP_MMA the warp-level int8
  * MMA kernel, KVB_KERNEL_TCGEN05 the TMEM-accumulator tcgen05 kernel wherever
- * it has a variant for the shape (else the warp-level one). For side-by-side
- * measurements and tests; results agree within the path tolerance.
- * kvb_decode_kernel returns the current choice. */
+ * it has a variant for the shape (else the warp-level one), KVB_KERNEL_GENERAL
+ * the general CUDA-core kernel for every kvb_launch_attention(_ex) call, int8
+ * or fp32 KV. For side-by-side measurements and tests; results agree within
+ * the path tolerance. kvb_decode_kernel returns the current choice. */
 #define KVB_KERNEL_AUTO 0
 #define KVB_KERNEL_WARP_MMA 1
 #define KVB_KERNEL_TCGEN05 2
+#define KVB_KERNEL_GENERAL 3
 int kvb_set_decode_kernel(int choice);
 int kvb_decode_kernel(void);
 

@@ -424,12 +424,13 @@ def debug_skip_stage(stage: int) -> None:
     check(_lib.load().kvb_debug_skip_stage(stage))
 
 
-KERNEL_AUTO, KERNEL_WARP_MMA, KERNEL_TCGEN05 = 0, 1, 2
+KERNEL_AUTO, KERNEL_WARP_MMA, KERNEL_TCGEN05, KERNEL_GENERAL = 0, 1, 2, 3
 
 
 def set_decode_kernel(choice: int) -> None:
     """Which single-sequence partial kernel later calls use: KERNEL_AUTO (by
-    shape), KERNEL_WARP_MMA or KERNEL_TCGEN05 (where a variant exists)."""
+    shape), KERNEL_WARP_MMA or KERNEL_TCGEN05 (where a variant exists), or
+    KERNEL_GENERAL (the CUDA-core kernel for every launch_attention call)."""
     check(_lib.load().kvb_set_decode_kernel(int(choice)))
 
 

@@ -28,6 +28,7 @@ HEADERS = [
     "kvb_schedule.h",
     "decode_tma.cuh",
     "decode_tc.cuh",
+    "decode_f32.cuh",
     "decode_simt.cuh",
     "merge.cuh",
     "peer_merge.cuh",

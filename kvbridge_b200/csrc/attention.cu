@@ -22,6 +22,7 @@
 #include "decode_simt.cuh"
 #include "decode_tma.cuh"
 #include "decode_tc.cuh"
+#include "decode_f32.cuh"
 #include "merge.cuh"
 #include "peer_merge.cuh"
 #include "append_kv.cuh"
@@ -258,10 +259,15 @@ TcVariant tc_variant(uint32_t dim, uint32_t page_tokens, uint32_t qrows) {
 
 // Which single-sequence partial kernel runs: 0 = by shape (tcgen05 where it
 // was measured to win), 1 = the warp-level MMA kernel, 2 = tcgen05 wherever
-// a variant exists. Process-wide (detail::set_decode_kernel).
+// a variant exists, 3 = the general CUDA-core kernel (decode_simt.cuh) for
+// every launch_attention call, int8 or fp32 KV. Process-wide
+// (detail::set_decode_kernel).
 std::atomic<int> g_decode_kernel{0};
 
 uint32_t query_rows(const Shape& s) { return s.rows * (s.q_heads / s.kv_heads); }
+
+// Eager load of the fp32-KV partial kernels (defined with their launcher).
+cudaError_t preload_f32_kernels();
 
 // Single sequence: a CTA takes 8 query columns of one KV head (nt = 1), or at
 // most 4 in the four-column layout (nt = 0: one query row of a 32/8-head
@@ -490,8 +496,9 @@ cudaError_t preload_attention_mma_kernels() {
 }
 
 cudaError_t preload_attention_kernels() {
-  const cudaError_t code = preload_attention_reference_kernels();
-  return code == cudaSuccess ? preload_attention_mma_kernels() : code;
+  cudaError_t code = preload_attention_reference_kernels();
+  if (code == cudaSuccess) code = preload_attention_mma_kernels();
+  return code == cudaSuccess ? preload_f32_kernels() : code;
 }
 
 namespace {
@@ -638,10 +645,83 @@ void launch_single_partials(const Shape& s, const DeviceInput& in, uint32_t part
   fast_variant(s.dim, prm.group_cols == 4 ? 0 : prm.group_cols / 8, s.page_tokens, false).launch(prm, stream);
 }
 
+// ---------------------------------------------------------------------------
+// fp32 KV (Shape::int8 == false): the streaming kernel of decode_f32.cuh for
+// head dims 64 and 128, 16/32/64-token pages and up to 16 query columns per
+// KV head (4 a CTA; more columns run as column groups whose CTAs share the
+// pages in L2), with 16-byte aligned q, k and v. Every other fp32 shape runs
+// the general kernel. One CTA per SM (a ring of 3 stages of 64 KB at dim
+// 128, 6 of 32 KB at dim 64).
+
+constexpr uint32_t kF32MaxColumns = 16;
+
+struct F32Variant {
+  const void* fn = nullptr;
+  uint32_t smem = 0;
+};
+
+template <int D, int STAGES>
+F32Variant make_f32_variant() {
+  return F32Variant{reinterpret_cast<const void*>(&kvb::decode_partial_f32_kernel<D, STAGES>),
+                    kvb::F32Layout<D, STAGES>::kBytes};
+}
+
+F32Variant f32_variant(uint32_t dim) {
+  return dim == 64 ? make_f32_variant<64, 6>() : make_f32_variant<128, 3>();
+}
+
+bool f32_geometry(const Shape& s, const DeviceInput& in, const float* scratch) {
+  return !s.int8 && (s.dim == 64 || s.dim == 128) &&
+         (s.page_tokens == 16 || s.page_tokens == 32 || s.page_tokens == 64) &&
+         query_rows(s) >= 1 && query_rows(s) <= kF32MaxColumns && aligned_to(in.q, 16) &&
+         aligned_to(in.k, 16) && aligned_to(in.v, 16) && aligned_to(scratch, 8);
+}
+
+uint32_t f32_column_groups(const Shape& s) {
+  return (query_rows(s) + kvb::kF32Cols - 1) / kvb::kF32Cols;
+}
+
+// Partitions per KV head: one CTA per SM over all heads and column groups
+// unless the caller asked for a count; at most one per stage and split.
+uint32_t f32_partitions(const Shape& s, uint32_t requested) {
+  const uint32_t stages = kvb::stages_of_range(s.begin, s.end);
+  if (stages == 0) return 0;
+  const uint32_t sms = uint32_t(current_device_facts().sms);
+  uint32_t parts = requested != 0 ? requested : sms / (s.kv_heads * f32_column_groups(s));
+  parts = std::min(std::max(parts, 1u), std::min(stages, split_count(s)));
+  return parts;
+}
+
+void launch_f32_partials(const Shape& s, const DeviceInput& in, uint32_t parts, float* scratch,
+                         uint32_t split_stride, cudaStream_t stream) {
+  kvb::DecodeParams prm = single_params(s, in, parts, scratch, split_stride);
+  prm.group_cols = kvb::kF32Cols;
+  prm.col_groups = f32_column_groups(s);
+  prm.ctas = parts * s.kv_heads * prm.col_groups;
+  const F32Variant v = f32_variant(s.dim);
+  cuda_ok(cudaFuncSetAttribute(v.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(v.smem)),
+          "fp32 decode kernel shared-memory opt-in");
+  void* args[] = {&prm};
+  launch_pdl(v.fn, dim3(prm.ctas), dim3(kvb::kF32Threads), v.smem, stream, args,
+             "fp32 decode partial launch");
+}
+
+cudaError_t preload_f32_kernels() {
+  for (uint32_t dim : {64u, 128u}) {
+    const F32Variant v = f32_variant(dim);
+    cudaFuncAttributes a{};
+    cudaError_t code = cudaFuncGetAttributes(&a, v.fn);
+    if (code == cudaSuccess)
+      code = cudaFuncSetAttribute(v.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(v.smem));
+    if (code != cudaSuccess) return code;
+  }
+  return cudaSuccess;
+}
+
 }  // namespace
 
 namespace detail {
-void set_decode_kernel(int choice) noexcept { g_decode_kernel.store(choice < 0 || choice > 2 ? 0 : choice); }
+void set_decode_kernel(int choice) noexcept { g_decode_kernel.store(choice < 0 || choice > 3 ? 0 : choice); }
 int decode_kernel() noexcept { return g_decode_kernel.load(); }
 }  // namespace detail
 
@@ -680,7 +760,18 @@ void launch_attention_ex(const Shape& s, const DeviceInput& in, const LaunchOpti
                          float* scratch, float* m, float* l, float* n, cudaStream_t stream) {
   detail::check_inputs(s, in, scratch, m, l, n);
   const uint32_t splits = split_count(s);
-  if (!attention_b200_supported(s, in)) {
+  const bool general = g_decode_kernel.load() == 3;
+  if (!attention_b200_supported(s, in) || general) {
+    const uint32_t parts = !general && f32_geometry(s, in, scratch) ? f32_partitions(s, opt.partitions) : 0u;
+    if (parts != 0) {
+      launch_f32_partials(s, in, parts, scratch, splits, stream);
+      // The partial kernel has already marked splits [parts, splits) empty.
+      launch_merge(kvb::kMergeScratch,
+                   scratch_merge_params(s, scratch, parts, splits, false, m, l, n, opt.out_f16,
+                                        opt.out_bf16),
+                   stream);
+      return;
+    }
     launch_simt(s, in, scratch, splits, stream);
     launch_merge(kvb::kMergeScratch,
                  scratch_merge_params(s, scratch, splits, splits, false, m, l, n, opt.out_f16,

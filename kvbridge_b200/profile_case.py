@@ -16,9 +16,10 @@ profiler's replay passes):
   cfg5-slice      batch 4 x 131,072 tokens (one eighth of each cfg5 sequence)
   native          the reference's native shape: rows 8, 24/4 heads, dim 256,
                   Page32, 32,768 ctx
+  f32             cfg2's geometry with fp32 KV ~N(0,1) (537 MB of K/V)
   peer-merge      merge_attention_peers with one rank (cfg5's partial shape: 4 x
                   32 row-heads, dim 128), the kernel's own work without NVLink
-``--kernel warp|tcgen05`` forces the single-sequence partial kernel.
+``--kernel warp|tcgen05|general`` forces the single-sequence partial kernel.
 """
 from __future__ import annotations
 
@@ -29,7 +30,7 @@ import torch
 
 from . import api, build, synth
 
-CASES = ("peer-merge", "cfg1", "cfg2", "cfg2-rank4", "cfg2-rank8", "cfg3", "cfg3-slice", "cfg4-slice", "cfg4-slice-p64", "cfg5-slice", "native")
+CASES = ("peer-merge", "cfg1", "cfg2", "cfg2-rank4", "cfg2-rank8", "cfg3", "cfg3-slice", "cfg4-slice", "cfg4-slice-p64", "cfg5-slice", "native", "f32")
 
 
 def _single(case: synth.SingleCase, partitions: int):
@@ -115,6 +116,15 @@ def make_call(name: str, device):
         case = synth.make_single(rows, 24, 4, 256, 32, tokens, seed + 8, device,
                                  q_positions=[tokens - rows + r for r in range(rows)])
         return _single(case, 0)
+    if name == "f32":
+        base = synth.make_single(1, 32, 8, 128, 64, 65536, seed + 32, device)
+        shape = api.Shape(**{**base.shape.__dict__, "int8": False})
+        gen = torch.Generator(device=device)
+        gen.manual_seed(seed + 0xF32)
+        k = torch.randn(shape.pages * 8 * 64 * 128, generator=gen, device=device)
+        v = torch.randn(shape.pages * 8 * 128 * 64, generator=gen, device=device)
+        return _single(synth.SingleCase(shape, base.q, base.q_positions, base.k_positions, base.page_table,
+                                        k, v, None, None), 0)
     raise ValueError(f"unknown case {name!r}; one of {', '.join(CASES)}")
 
 
@@ -122,12 +132,12 @@ def main(argv=None) -> int:
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--case", choices=CASES, required=True)
     ap.add_argument("--calls", type=int, default=3)
-    ap.add_argument("--kernel", choices=["auto", "warp", "tcgen05"], default="auto")
+    ap.add_argument("--kernel", choices=["auto", "warp", "tcgen05", "general"], default="auto")
     args = ap.parse_args(argv)
     build.build()
     device = torch.device("cuda", 0)
     api.set_decode_kernel({"auto": api.KERNEL_AUTO, "warp": api.KERNEL_WARP_MMA,
-                           "tcgen05": api.KERNEL_TCGEN05}[args.kernel])
+                           "tcgen05": api.KERNEL_TCGEN05, "general": api.KERNEL_GENERAL}[args.kernel])
     call = make_call(args.case, device)
     torch.cuda.synchronize()
     for _ in range(args.calls):
