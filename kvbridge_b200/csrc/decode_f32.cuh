@@ -109,14 +109,15 @@ __device__ void produce_f32(const DecodeParams& p, const Piece& pc, uint8_t* rin
   bool failed = false;
   for (uint32_t j = pc.j0; j < pc.j1; ++j) {
     const uint32_t phys = t[0];
-    const bool ok = in[0] && phys < p.pages;
+    const bool mine = in[0];
+    const bool ok = mine && phys < p.pages;
     t[0] = t[1];
     in[0] = in[1];
     t[1] = t[2];
     in[1] = in[2];
     in[2] = lane_page(j + 3, pg);
     t[2] = in[2] ? __ldg(p.table + pg) : 0u;
-    if (__ballot_sync(0xffffffffu, in[0] && !ok) != 0u && lane == 0) atomicMax(&g_kvb_status, kStatusBadPage);
+    if (__ballot_sync(0xffffffffu, mine && !ok) != 0u && lane == 0) atomicMax(&g_kvb_status, kStatusBadPage);
     const uint32_t okk = __ballot_sync(0xffffffffu, ok && !is_v);  // bit 2k: page k copied
     uint32_t okpages = 0;
 #pragma unroll
