@@ -40,6 +40,9 @@ constexpr int kF32ConsumerWarps = 8;
 constexpr int kF32ProducerWarp = kF32ConsumerWarps;
 constexpr int kF32Threads = 32 * (kF32ConsumerWarps + 1);
 constexpr int kF32Cols = 4;  // query columns per CTA
+// Floats per column row of the P buffer: 64 tokens + 4, so that the four
+// columns' stores of one token land in different banks (16-byte aligned rows).
+constexpr int kF32PPitch = kStageTokens + 4;
 
 // a[i] for a lane-dependent i without indexing a register array (which
 // would put the array in local memory).
@@ -65,8 +68,8 @@ struct F32Smem {
 template <int D, int STAGES>
 struct F32Layout {
   static constexpr uint32_t kRing = STAGES * F32Smem<D>::kStage;
-  static constexpr uint32_t kOffP = kRing;                                   // P[col][64]
-  static constexpr uint32_t kOffWmax = kOffP + kF32Cols * kStageTokens * 4;  // [warp][col]
+  static constexpr uint32_t kOffP = kRing;                                 // P[col][kF32PPitch]
+  static constexpr uint32_t kOffWmax = kOffP + kF32Cols * kF32PPitch * 4;  // [warp][col]
   static constexpr uint32_t kOffLw = kOffWmax + kF32ConsumerWarps * kF32Cols * 4;
   static constexpr uint32_t kOffOk = kOffLw + kF32ConsumerWarps * kF32Cols * 4;  // [slot] page mask
   static constexpr uint32_t kOffBar = (kOffOk + 4 * STAGES + 7) / 8 * 8;
@@ -322,7 +325,7 @@ __global__ void __launch_bounds__(kF32Threads, 1) decode_partial_f32_kernel(Deco
 #pragma unroll
       for (int r = 0; r < 2; ++r) {
         ps[r] = xs[r] == -INFINITY ? 0.f : fast_exp2(xs[r] - mc);
-        Ps[my_col * kStageTokens + 8 * warp + 4 * r + (lane >> 3)] = ps[r];
+        Ps[my_col * kF32PPitch + 8 * warp + 4 * r + (lane >> 3)] = ps[r];
       }
       lpart = fmaf(lpart, pick_col(alpha, my_col), ps[0] + ps[1]);
     }
@@ -340,7 +343,7 @@ __global__ void __launch_bounds__(kF32Threads, 1) decode_partial_f32_kernel(Deco
       if (!full_stage && ((okp >> pg) & 1u) == 0u) continue;
       float4 pv[kF32Cols];
 #pragma unroll
-      for (int c = 0; c < kF32Cols; ++c) pv[c] = *reinterpret_cast<const float4*>(Ps + c * kStageTokens + t0);
+      for (int c = 0; c < kF32Cols; ++c) pv[c] = *reinterpret_cast<const float4*>(Ps + c * kF32PPitch + t0);
       const float* vrow = Vs + pg * vpitch_f + s0;
 #pragma unroll
       for (int dd = 0; dd < kDpl; ++dd) {
