@@ -439,8 +439,11 @@ unsigned attention_partitions(const Shape& s, unsigned requested) {
       // with fewer KV heads (one per GPU when cfg2's 8 are split over 8)
       // the merge's rounds over the partials cost more than the extra CTAs
       // stream (one KV head, 65,536 tokens: 256 partitions 15.2 us a call,
-      // 148 12.4 us, 96 12.5 us, 64 13.3 us).
-      parts = std::max(1u, std::min(wave / (s.kv_heads * plan.groups), sms));
+      // 148 12.4 us, 96 12.5 us, 64 13.3 us). And at most one round of the
+      // many-partials merge (kMergeWideRound partials): one KV head of
+      // cfg2, 148 partitions 9.33 us, 136 9.51, 128 9.16, 120 9.74; two
+      // KV heads, 148 11.11 us, 128 10.43.
+      parts = std::max(1u, std::min({wave / (s.kv_heads * plan.groups), sms, kvb::kMergeWideRound}));
     }
   }
   parts = std::min(parts, stages);

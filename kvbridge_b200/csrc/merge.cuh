@@ -241,6 +241,9 @@ __global__ void __launch_bounds__(32 * kMergeWarps, 6) merge_kernel(MergeParams 
 // merge_kernel reads at most kMergeWarps * 10 partials a round at dim 128.
 constexpr uint32_t kMergeWideAbove = 40;
 
+// Partials a CTA of merge_wide_kernel folds per round (32 a warp).
+constexpr uint32_t kMergeWideRound = 32 * kMergeWarps;
+
 // Merge of many partials per row-head (kScratch, kShards): CTA c merges dims
 // [32 s, 32 s + 32) of row-head c / S, S = ceil(dim / 32), so that the S
 // slices of a row-head read its partials on S SMs. Partials go in rounds of
