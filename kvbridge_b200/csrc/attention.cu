@@ -435,15 +435,15 @@ unsigned attention_partitions(const Shape& s, unsigned requested) {
       const FastVariant v = fast_variant(s.dim, plan.nt, s.page_tokens, false);
       const uint32_t sms = uint32_t(current_device_facts().sms);
       const uint32_t wave = v.fn ? sms * uint32_t(resident_ctas(v)) : 1u;
-      // One wave of CTAs, but at most one partition per SM for a KV head:
-      // with fewer KV heads (one per GPU when cfg2's 8 are split over 8)
-      // the merge's rounds over the partials cost more than the extra CTAs
-      // stream (one KV head, 65,536 tokens: 256 partitions 15.2 us a call,
-      // 148 12.4 us, 96 12.5 us, 64 13.3 us). And at most one round of the
-      // many-partials merge (kMergeWideRound partials): one KV head of
-      // cfg2, 148 partitions 9.33 us, 136 9.51, 128 9.16, 120 9.74; two
-      // KV heads, 148 11.11 us, 128 10.43.
-      parts = std::max(1u, std::min({wave / (s.kv_heads * plan.groups), sms, kvb::kMergeWideRound}));
+      // One wave of CTAs; above one round of the many-partials merge
+      // (kMergeWideRound partials per row-head) a whole number of its rounds,
+      // because a partly filled round costs nearly a full one. Measured on
+      // cfg2's share of one rank (65,536 tokens): one KV head, 296 slots ->
+      // 256 partitions 8.81 us a call (224: 9.01, 192: 9.35, 148: 9.33,
+      // 136: 9.51, 128: 9.14, 120: 9.74); two KV heads, 148 slots -> 128
+      // partitions 10.34 us (148: 11.11, 256 in two waves: 15.49).
+      parts = std::max(1u, wave / (s.kv_heads * plan.groups));
+      if (parts > kvb::kMergeWideRound) parts -= parts % kvb::kMergeWideRound;
     }
   }
   parts = std::min(parts, stages);

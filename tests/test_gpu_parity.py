@@ -128,9 +128,10 @@ def test_four_column_layout(cuda_device, rows, q_heads, kv_heads, dim, page_toke
 @pytest.mark.parametrize("partitions", [0, 148, 256])
 def test_few_kv_heads_many_partials(cuda_device, kv_heads, partitions):
     """One rank's share of cfg2 split over 8 or 4 GPUs (1 or 2 KV heads, 65,536
-    tokens): 128 automatic partitions per row-head (one merge round), 148 (a
-    full and a partial round) or 256 (two rounds), merged by the
-    many-partials merge (one CTA per 32 dims, rounds of 128 partials)."""
+    tokens): automatic partitions (256 at one KV head, 128 at two: whole
+    merge rounds), 148 (a full and a partial round) or 256 per row-head,
+    merged by the many-partials merge (one CTA per 32 dims, rounds of 128
+    partials)."""
     case = make(cuda_device, rows=1, q_heads=4 * kv_heads, kv_heads=kv_heads, dim=128, page_tokens=64,
                 tokens=65536, seed=900 + kv_heads)
     assert kvb.attention_partitions(case.shape, partitions) > 40
