@@ -339,7 +339,7 @@ void launch_merge(int mode, const kvb::MergeParams& prm, cudaStream_t stream) {
   void* args[] = {&copy};
   const void* fn = wide ? merge_wide_fn(mode) : merge_fn(mode, prm.dim);
   cuda_ok(prefer_max_shared(fn), "merge kernel carveout");
-  launch_pdl(fn, dim3(blocks), dim3(32 * kvb::kMergeWarps), 0, stream, args,
+  launch_pdl(fn, dim3(blocks), dim3(32 * (wide ? kvb::kMergeWideWarps : kvb::kMergeWarps)), 0, stream, args,
              "attention merge launch");
 }
 
@@ -412,6 +412,9 @@ TcVariant chosen_tc_variant(const Shape& s) {
 // ---------------------------------------------------------------------------
 // B200 predicates and planning.
 
+// Granularity of automatic partition counts above it (attention_partitions).
+constexpr uint32_t kPartitionQuantum = 128;
+
 bool attention_b200_supported(const Shape& s, const DeviceInput& in) noexcept {
   if (!attention_shape_valid(s) || !s.int8) return false;
   if (!fast_geometry(s.dim, s.page_tokens, query_rows(s), kMaxQueryColumns)) return false;
@@ -435,15 +438,18 @@ unsigned attention_partitions(const Shape& s, unsigned requested) {
       const FastVariant v = fast_variant(s.dim, plan.nt, s.page_tokens, false);
       const uint32_t sms = uint32_t(current_device_facts().sms);
       const uint32_t wave = v.fn ? sms * uint32_t(resident_ctas(v)) : 1u;
-      // One wave of CTAs; above one round of the many-partials merge
-      // (kMergeWideRound partials per row-head) a whole number of its rounds,
-      // because a partly filled round costs nearly a full one. Measured on
-      // cfg2's share of one rank (65,536 tokens): one KV head, 296 slots ->
-      // 256 partitions 8.81 us a call (224: 9.01, 192: 9.35, 148: 9.33,
-      // 136: 9.51, 128: 9.14, 120: 9.74); two KV heads, 148 slots -> 128
-      // partitions 10.34 us (148: 11.11, 256 in two waves: 15.49).
+      // One wave of CTAs; above kPartitionQuantum partitions per KV head
+      // (few KV heads per GPU, where the many-partials merge runs) a
+      // multiple of it, which leaves some SMs' second slot free, so the
+      // merge's CTAs are resident before the partial grid ends. Measured
+      // on cfg2's share of one rank (65,536 tokens; 4-warp merge): one KV
+      // head, 296 slots -> 256 partitions 8.81 us a call (224: 9.01, 192:
+      // 9.35, 148: 9.33, 128: 9.14); two KV heads, 148 slots -> 128
+      // partitions 10.34 us (148: 11.11). With the 8-warp merge (one round
+      // of 256 partials): one KV head 256 -> 8.37 us (192: 8.90, 128:
+      // 9.10); two KV heads 128 -> 10.42 us, 148 -> 11.72 us.
       parts = std::max(1u, wave / (s.kv_heads * plan.groups));
-      if (parts > kvb::kMergeWideRound) parts -= parts % kvb::kMergeWideRound;
+      if (parts > kPartitionQuantum) parts -= parts % kPartitionQuantum;
     }
   }
   parts = std::min(parts, stages);

@@ -241,23 +241,26 @@ __global__ void __launch_bounds__(32 * kMergeWarps, 6) merge_kernel(MergeParams 
 // merge_kernel reads at most kMergeWarps * 10 partials a round at dim 128.
 constexpr uint32_t kMergeWideAbove = 40;
 
-// Partials a CTA of merge_wide_kernel folds per round (32 a warp).
-constexpr uint32_t kMergeWideRound = 32 * kMergeWarps;
+// Warps of a merge_wide_kernel CTA, and the partials it folds per round
+// (32 a warp).
+constexpr int kMergeWideWarps = 8;
+constexpr uint32_t kMergeWideRound = 32 * kMergeWideWarps;
 
 // Merge of many partials per row-head (kScratch, kShards): CTA c merges dims
 // [32 s, 32 s + 32) of row-head c / S, S = ceil(dim / 32), so that the S
 // slices of a row-head read its partials on S SMs. Partials go in rounds of
-// 32 a warp (128 a CTA): lane j loads m and l of the warp's partial j, and
+// 32 a warp (256 a CTA): lane j loads m and l of the warp's partial j, and
 // every lane loads each of those 32 partials' n at its own dim, all before
-// any is used; the partials' weights reach the lanes by shuffles. With 148
-// partials per row-head (one KV head of cfg2 per GPU) that is two rounds
-// where merge_kernel takes four.
+// any is used; the partials' weights reach the lanes by shuffles. With up to
+// 256 partials per row-head (one KV head of cfg2 per GPU) that is one round,
+// each round costing one memory round trip (with 4 warps, 128 a round, one
+// KV head of cfg2 at 256 partitions took 8.84 us a call).
 template <int MODE>
-__global__ void __launch_bounds__(32 * kMergeWarps, 6) merge_wide_kernel(MergeParams p) {
+__global__ void __launch_bounds__(32 * kMergeWideWarps, 3) merge_wide_kernel(MergeParams p) {
   static_assert(MODE != kMergeBatched, "the batched layout takes merge_kernel");
-  __shared__ float red_m[kMergeWarps];
-  __shared__ float red_l[kMergeWarps];
-  __shared__ float red_n[kMergeWarps][32];
+  __shared__ float red_m[kMergeWideWarps];
+  __shared__ float red_l[kMergeWideWarps];
+  __shared__ float red_n[kMergeWideWarps][32];
   KVB_MERGE_MARK(0);
   grid_launch_dependents();
   grid_dependency_wait();
@@ -285,7 +288,7 @@ __global__ void __launch_bounds__(32 * kMergeWarps, 6) merge_wide_kernel(MergePa
   }
 
   float acc = 0.f, M = -INFINITY, Lw = 0.f;  // Lw: this lane's partials' share of L
-  for (uint32_t base = 0; base < np; base += 32 * kMergeWarps) {
+  for (uint32_t base = 0; base < np; base += 32 * kMergeWideWarps) {
     const uint32_t first = base + 32 * warp;
     const uint32_t i = first + lane;  // this lane's partial
     const bool ok = i < np;
@@ -302,7 +305,7 @@ __global__ void __launch_bounds__(32 * kMergeWarps, 6) merge_wide_kernel(MergePa
     KVB_MERGE_MARK(3);
     float mnew = M;
 #pragma unroll
-    for (int w = 0; w < kMergeWarps; ++w) mnew = fmaxf(mnew, red_m[w]);
+    for (int w = 0; w < kMergeWideWarps; ++w) mnew = fmaxf(mnew, red_m[w]);
     __syncthreads();
     if (mnew == -INFINITY) continue;
     const float alpha = M == -INFINITY ? 0.f : expf(M - mnew);
@@ -328,7 +331,7 @@ __global__ void __launch_bounds__(32 * kMergeWarps, 6) merge_wide_kernel(MergePa
   KVB_MERGE_MARK(4);
   float L = 0.f;
 #pragma unroll
-  for (int w = 0; w < kMergeWarps; ++w) L += red_l[w];
+  for (int w = 0; w < kMergeWideWarps; ++w) L += red_l[w];
   if (threadIdx.x == 0 && slice == 0) {
     p.m[rh] = L > 0.f ? M : -INFINITY;
     p.l[rh] = L;
@@ -336,7 +339,7 @@ __global__ void __launch_bounds__(32 * kMergeWarps, 6) merge_wide_kernel(MergePa
   if (warp == 0 && has_d) {
     float v = 0.f;
 #pragma unroll
-    for (int w = 0; w < kMergeWarps; ++w) v += red_n[w][lane];
+    for (int w = 0; w < kMergeWideWarps; ++w) v += red_n[w][lane];
     v = L > 0.f ? v : 0.f;
     const float inv = L > 0.f ? 1.f / L : 0.f;
     p.n[size_t(rh) * D + d] = v;
@@ -345,7 +348,7 @@ __global__ void __launch_bounds__(32 * kMergeWarps, 6) merge_wide_kernel(MergePa
   }
   if (MODE == kMergeScratch && p.fill_empty && slice == 0) {
     float* row = p.part + size_t(rh) * p.split_stride * (D + 2);
-    for (uint32_t j = np + threadIdx.x; j < p.split_stride; j += 32 * kMergeWarps) {
+    for (uint32_t j = np + threadIdx.x; j < p.split_stride; j += 32 * kMergeWideWarps) {
       row[size_t(j) * (D + 2) + 0] = -INFINITY;
       row[size_t(j) * (D + 2) + 1] = 0.f;
     }
