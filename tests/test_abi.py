@@ -136,6 +136,20 @@ def test_wait_limit_setting(kvb_lib):
     assert kvb.wait_limit_ns() == 2_000_000_000
 
 
+def test_decode_kernel_switch(kvb_lib):
+    """The process-wide kernel choice (auto, warp-level MMA, tcgen05, general
+    CUDA-core kernel) round-trips through the C ABI; unknown values fall back
+    to auto. Host-side state only, no GPU needed."""
+    try:
+        for choice in (kvb.KERNEL_WARP_MMA, kvb.KERNEL_TCGEN05, kvb.KERNEL_GENERAL, kvb.KERNEL_AUTO):
+            kvb.set_decode_kernel(choice)
+            assert kvb.decode_kernel() == choice
+        kvb.set_decode_kernel(7)
+        assert kvb.decode_kernel() == kvb.KERNEL_AUTO
+    finally:
+        kvb.set_decode_kernel(kvb.KERNEL_AUTO)
+
+
 def test_launch_failure_hook_does_not_mask_validation(kvb_lib):
     """An armed launch-failure hook only replaces a launch: a call that fails
     validation first still reports KVB_EINVAL, and disarming is a no-op."""
