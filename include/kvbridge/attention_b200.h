@@ -27,19 +27,7 @@ struct LaunchOptions {
   // Optional __nv_bfloat16[rows * q_heads * dim], the same n / l in bf16 (for
   // an out-projection that takes bf16 activations). Either, both or neither.
   void* out_bf16 = nullptr;
-  // Optional uint32[fused_merge_counter_words(shape)], zeroed by the caller
-  // before its first use. With it, a call whose KV heads each get at least
-  // 64 partitions on the warp-level tensor-core kernel (few KV heads per
-  // GPU) merges its partials inside the partial kernel -- the last CTA of
-  // each group of 16 partitions, then the last group -- instead of launching
-  // the merge kernel; outputs, the scratch decomposition and the error
-  // behaviour are those of the call without it. The kernel leaves every
-  // counter at zero; calls that share a buffer must not overlap on the GPU.
-  uint32_t* merge_counters = nullptr;
 };
-
-// uint32 words LaunchOptions::merge_counters needs for this shape.
-size_t fused_merge_counter_words(const Shape&);
 
 // True when launch_attention(_ex) will use the TMA/tensor-core kernel for this
 // shape and these buffers (int8 KV, dim in {64,128,256}, page_tokens 16, 32

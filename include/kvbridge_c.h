@@ -93,14 +93,6 @@ int kvb_launch_attention_ex2(const kvb_shape* s, const kvb_device_input* in, uns
                              void* out_f16, void* out_bf16, float* scratch, float* m, float* l,
                              float* n, void* stream);
 
-/* kvb_launch_attention_ex2 with the optional fused-merge counters
- * (kvbridge::LaunchOptions::merge_counters: uint32[words] zeroed before the
- * first call, words from kvb_fused_merge_counter_words; NULL = off). */
-int kvb_launch_attention_ex3(const kvb_shape* s, const kvb_device_input* in, unsigned partitions,
-                             void* out_f16, void* out_bf16, uint32_t* merge_counters, float* scratch,
-                             float* m, float* l, float* n, void* stream);
-int kvb_fused_merge_counter_words(const kvb_shape* s, size_t* words);
-
 /* the two halves of kvb_launch_attention_ex (partial kernel; merge of the
  * leading `partitions` splits). *partitions_used may be NULL. */
 int kvb_launch_attention_partials(const kvb_shape* s, const kvb_device_input* in,

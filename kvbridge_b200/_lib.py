@@ -171,11 +171,6 @@ SIGNATURES = {
         c_int,
         [POINTER(KvbShape), POINTER(KvbDeviceInput), ctypes.c_uint] + [c_void_p] * 7,
     ),
-    "kvb_launch_attention_ex3": (
-        c_int,
-        [POINTER(KvbShape), POINTER(KvbDeviceInput), ctypes.c_uint] + [c_void_p] * 8,
-    ),
-    "kvb_fused_merge_counter_words": (c_int, [POINTER(KvbShape), POINTER(c_size_t)]),
     "kvb_merge_attention_ex2": (
         c_int,
         [POINTER(KvbShape), c_void_p, ctypes.c_uint] + [c_void_p] * 6,

@@ -194,13 +194,6 @@ def attention_b200_supported(s: Shape, inp: DeviceInput) -> bool:
     return bool(_lib.load().kvb_attention_b200_supported(ctypes.byref(s.c()), ctypes.byref(inp.c())))
 
 
-def fused_merge_counter_words(s: Shape) -> int:
-    """uint32 words of the fused-merge counter buffer for this shape."""
-    out = ctypes.c_size_t()
-    check(_lib.load().kvb_fused_merge_counter_words(ctypes.byref(s.c()), ctypes.byref(out)))
-    return out.value
-
-
 def attention_partitions(s: Shape, requested: int = 0) -> int:
     out = ctypes.c_uint()
     check(_lib.load().kvb_attention_partitions(ctypes.byref(s.c()), requested, ctypes.byref(out)))
@@ -209,18 +202,11 @@ def attention_partitions(s: Shape, requested: int = 0) -> int:
 
 def launch_attention_ex(
     s: Shape, inp: DeviceInput, scratch, m, l, n, partitions: int = 0, out_f16=None, stream=None,
-    out_bf16=None, merge_counters=None,
+    out_bf16=None,
 ) -> None:
     """launch_attention with explicit partitions and optional normalised
-    outputs n / l in fp16 (``out_f16``) and/or bf16 (``out_bf16``).
-    ``merge_counters`` (an int32 tensor of fused_merge_counter_words(s)
-    elements, zeroed before its first use) lets calls with many partitions
-    per KV head merge inside the partial kernel."""
-    if merge_counters is not None:
-        status = _lib.load().kvb_launch_attention_ex3(
-            ctypes.byref(s.c()), ctypes.byref(inp.c()), partitions, _ptr(out_f16), _ptr(out_bf16),
-            _ptr(merge_counters), _ptr(scratch), _ptr(m), _ptr(l), _ptr(n), _stream(stream))
-    elif out_bf16 is None:
+    outputs n / l in fp16 (``out_f16``) and/or bf16 (``out_bf16``)."""
+    if out_bf16 is None:
         status = _lib.load().kvb_launch_attention_ex(
             ctypes.byref(s.c()), ctypes.byref(inp.c()), partitions, _ptr(out_f16), _ptr(scratch),
             _ptr(m), _ptr(l), _ptr(n), _stream(stream))

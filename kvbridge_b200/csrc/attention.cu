@@ -632,36 +632,15 @@ bool set_tc_maps(kvb::DecodeParamsTc& prm, uint32_t dim) {
                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// Fused merge (LaunchOptions::merge_counters): partitions per first-level
-// group, and the fewest partitions per KV head it is used for.
-constexpr uint32_t kFusedMergeGroup = 16;
-constexpr uint32_t kFusedMergeMinParts = 64;
-
-// Outputs of a fused merge (null counters: none).
-struct FusedMerge {
-  uint32_t* counters = nullptr;
-  float *m = nullptr, *l = nullptr, *n = nullptr;
-  void *out_f16 = nullptr, *out_bf16 = nullptr;
-};
-
 // The single-sequence partial kernel (tcgen05 or warp-level MMA, as chosen
 // for the shape) over `parts` partitions; partials go to `scratch` with
-// `split_stride` slots per row-head. With fuse.counters set (warp-level
-// kernel only) the kernel also merges them into fuse's outputs.
+// `split_stride` slots per row-head.
 void launch_single_partials(const Shape& s, const DeviceInput& in, uint32_t parts, float* scratch,
-                            uint32_t split_stride, cudaStream_t stream, const FusedMerge& fuse = FusedMerge{}) {
+                            uint32_t split_stride, cudaStream_t stream) {
   kvb::DecodeParamsGather prm = single_params(s, in, parts, scratch, split_stride);
   prm.prefetch_stages = kPrefetchStages;
   const TcVariant tcv = chosen_tc_variant(s);
-  if (fuse.counters != nullptr) {
-    prm.merge_counters = fuse.counters;
-    prm.merge_group = kFusedMergeGroup;
-    prm.m_out = fuse.m;
-    prm.l_out = fuse.l;
-    prm.n_out = fuse.n;
-    prm.out_f16 = static_cast<__half*>(fuse.out_f16);
-    prm.out_bf16 = static_cast<__nv_bfloat16*>(fuse.out_bf16);
-  } else if (tcv.fn != nullptr) {
+  if (tcv.fn != nullptr) {
     kvb::DecodeParamsTc tp{};
     static_cast<kvb::DecodeParams&>(tp) = static_cast<const kvb::DecodeParams&>(prm);
     tp.col_groups = 1;
@@ -809,27 +788,12 @@ void launch_attention_ex(const Shape& s, const DeviceInput& in, const LaunchOpti
                  stream);
     return;
   }
-  if (opt.merge_counters != nullptr) {
-    const uint32_t parts = attention_partitions(s, opt.partitions);
-    if (parts >= kFusedMergeMinParts && chosen_tc_variant(s).fn == nullptr) {
-      launch_single_partials(s, in, parts, scratch, splits, stream,
-                             FusedMerge{opt.merge_counters, m, l, n, opt.out_f16, opt.out_bf16});
-      return;
-    }
-  }
   const uint32_t parts = launch_attention_partials(s, in, opt.partitions, scratch, stream);
   // The partial kernel has already marked splits [parts, splits) empty.
   launch_merge(kvb::kMergeScratch,
                scratch_merge_params(s, scratch, parts, splits, false, m, l, n, opt.out_f16,
                                     opt.out_bf16),
                stream);
-}
-
-size_t fused_merge_counter_words(const Shape& s) {
-  validate_shape(s);
-  const uint32_t groups = column_plan(s.dim, query_rows(s)).groups;
-  const size_t per_key = (split_count(s) + kFusedMergeGroup - 1) / kFusedMergeGroup + 1;
-  return size_t(s.kv_heads) * groups * per_key;
 }
 
 void launch_attention(const Shape& s, const DeviceInput& in, float* scratch, float* m, float* l,

@@ -205,26 +205,6 @@ int kvb_launch_attention_ex2(const kvb_shape* s, const kvb_device_input* in, uns
   });
 }
 
-int kvb_launch_attention_ex3(const kvb_shape* s, const kvb_device_input* in, unsigned partitions,
-                             void* out_f16, void* out_bf16, uint32_t* merge_counters, float* scratch,
-                             float* m, float* l, float* n, void* stream) {
-  return guarded([&] {
-    kvbridge::LaunchOptions opt{partitions, out_f16};
-    opt.out_bf16 = out_bf16;
-    opt.merge_counters = merge_counters;
-    kvbridge::launch_attention_ex(to_shape(s), to_input(in), opt, scratch, m, l, n,
-                                  as_stream(stream));
-  });
-}
-
-int kvb_fused_merge_counter_words(const kvb_shape* s, size_t* words) {
-  return guarded([&] {
-    const size_t v = kvbridge::fused_merge_counter_words(to_shape(s));
-    if (words == nullptr) throw std::invalid_argument("output pointer is null");
-    *words = v;
-  });
-}
-
 int kvb_launch_attention_partials(const kvb_shape* s, const kvb_device_input* in,
                                   unsigned partitions, float* scratch, unsigned* partitions_used,
                                   void* stream) {

@@ -44,8 +44,6 @@
 
 #include <type_traits>
 
-#include <cuda_bf16.h>
-
 #include "kvb_device.cuh"
 #include "kvb_schedule.h"
 
@@ -87,17 +85,6 @@ struct DecodeParams {
   // of that stage waits until wait_limit_ns, records the failure and the CTA
   // returns. No memory access depends on it.
   uint32_t fault_stage;
-  // Single sequence, fused merge (null = off; the merge kernel runs after
-  // the partial kernel): zeroed uint32 counters, kv_heads * col_groups *
-  // (ceil(parts / merge_group) + 1) of them, which the kernel returns to
-  // zero, and the call's outputs (see fused_merge_tail).
-  uint32_t* merge_counters;
-  uint32_t merge_group;
-  float* m_out;
-  float* l_out;
-  float* n_out;
-  __half* out_f16;
-  __nv_bfloat16* out_bf16;
 };
 
 // Parameters of the small-page kernels. 16-token pages at dim <= 128
@@ -1205,143 +1192,6 @@ __device__ __forceinline__ void consume_stage(const DecodeParams& p, const uint8
 // 64K tokens the call's last 32 CTAs started ~3 us late. The dim-128,
 // 8-column kernels are therefore held to 144 (3 x 18 + 10 units; no
 // spills). At dim 256 one CTA has the SM to itself: 216 (2 x 27 + 10).
-// ---------------------------------------------------------------------------
-// Fused merge of a single sequence's partials (p.merge_counters set): the
-// split-K merge of reference src/attention_shared.cu:295-335 done by the
-// partial kernel's own CTAs instead of a merge kernel, as two levels of a
-// threadfence reduction. Every CTA writes its partial, fences, and counts
-// itself in its group (merge_group consecutive partitions of its KV head and
-// column group); the group's last CTA merges the group's partials into the
-// group's first slot and marks the others empty, fences, and counts the group
-// done; the last group's CTA merges the groups' partials into m, l, n and the
-// normalised outputs. No CTA waits for another; each counter is returned to
-// zero by the CTA that saw it complete. The scratch ends as a valid
-// decomposition (group partials in the groups' first slots, empty partials
-// elsewhere), and the result does not depend on which CTA came last.
-
-// Partials [first, first + count * stride) (every stride-th slot) of the
-// CTA's row-heads: the thread's column and dims. final: write m, l, n and the
-// outputs; else overwrite slot `first` with the merged partial and mark the
-// group's other slots empty. All consumer threads call it.
-template <int D, int NT>
-__device__ void merge_slots(const DecodeParams& p, const Piece& pc, uint32_t first, uint32_t count,
-                            uint32_t stride, bool final) {
-  constexpr uint32_t kCols = cta_cols<NT>();
-  constexpr uint32_t kTpc = 32 * kConsumerWarps / kCols;  // threads per column
-  constexpr uint32_t kDpt = D / kTpc;                      // dims per thread
-  constexpr uint32_t kChunk = kDpt >= 16 ? 2 : 32 / kDpt;  // partials whose loads go out together
-  const uint32_t col = threadIdx.x / kTpc, part = threadIdx.x % kTpc;
-  const uint32_t gcol = pc.col0 + col;
-  const bool valid = gcol < p.qr;
-  const uint32_t r = valid ? gcol / p.group : 0u, gq = valid ? gcol % p.group : 0u;
-  const size_t rh = size_t(r) * p.q_heads + size_t(pc.h) * p.group + gq;
-  float* row = p.part + rh * p.split_stride * (D + 2);
-  const uint32_t d0 = part * kDpt;
-  float M = -INFINITY, L = 0.f, acc[kDpt];
-#pragma unroll
-  for (uint32_t k = 0; k < kDpt; ++k) acc[k] = 0.f;
-  for (uint32_t base = 0; valid && base < count; base += kChunk) {
-    float mv[kChunk], lv[kChunk], nv[kChunk][kDpt];
-#pragma unroll
-    for (uint32_t i = 0; i < kChunk; ++i) {
-      const bool in = base + i < count;
-      const float* src = row + size_t(first + (in ? base + i : 0u) * stride) * (D + 2);
-      mv[i] = in ? __ldcg(src) : -INFINITY;
-      lv[i] = in ? __ldcg(src + 1) : 0.f;
-#pragma unroll
-      for (uint32_t k = 0; k < kDpt; k += 2) {
-        const float2 v = in ? __ldcg(reinterpret_cast<const float2*>(src + 2 + d0 + k)) : make_float2(0.f, 0.f);
-        nv[i][k] = v.x;
-        nv[i][k + 1] = v.y;
-      }
-    }
-    float cm = -INFINITY;
-#pragma unroll
-    for (uint32_t i = 0; i < kChunk; ++i) cm = lv[i] > 0.f ? fmaxf(cm, mv[i]) : cm;
-    const float mnew = fmaxf(M, cm);
-    if (mnew == -INFINITY) continue;
-    const float alpha = M == -INFINITY ? 0.f : expf(M - mnew);
-    L *= alpha;
-#pragma unroll
-    for (uint32_t k = 0; k < kDpt; ++k) acc[k] *= alpha;
-#pragma unroll
-    for (uint32_t i = 0; i < kChunk; ++i) {
-      // A partial with l = 0 contributes nothing (an empty partial's n is
-      // undefined).
-      if (!(lv[i] > 0.f)) continue;
-      const float e = expf(mv[i] - mnew);
-      L = fmaf(e, lv[i], L);
-#pragma unroll
-      for (uint32_t k = 0; k < kDpt; ++k) acc[k] = fmaf(e, nv[i][k], acc[k]);
-    }
-    M = mnew;
-  }
-  // Every thread has read the slots before any is overwritten.
-  named_barrier(1, 32 * kConsumerWarps);
-  if (!valid) return;
-  const float m_val = L > 0.f ? M : -INFINITY;
-  if (final) {
-    if (part == 0) {
-      p.m_out[rh] = m_val;
-      p.l_out[rh] = L;
-    }
-    const float inv = L > 0.f ? 1.f / L : 0.f;
-#pragma unroll
-    for (uint32_t k = 0; k < kDpt; ++k) {
-      const float v = L > 0.f ? acc[k] : 0.f;
-      p.n_out[rh * D + d0 + k] = v;
-      if (p.out_f16 != nullptr) p.out_f16[rh * D + d0 + k] = __float2half_rn(v * inv);
-      if (p.out_bf16 != nullptr) p.out_bf16[rh * D + d0 + k] = __float2bfloat16_rn(v * inv);
-    }
-  } else {
-    float* dst = row + size_t(first) * (D + 2);
-    if (part == 0) {
-      dst[0] = m_val;
-      dst[1] = L;
-    }
-#pragma unroll
-    for (uint32_t k = 0; k < kDpt; k += 2)
-      *reinterpret_cast<float2*>(dst + 2 + d0 + k) = make_float2(acc[k], acc[k + 1]);
-    for (uint32_t i = 1 + part; i < count; i += kTpc) {
-      float* e = row + size_t(first + i * stride) * (D + 2);
-      e[0] = -INFINITY;
-      e[1] = 0.f;
-    }
-  }
-}
-
-// Counts the CTA into *counter (expected arrivals: `arrivals`) after its
-// writes; true for the last arrival, which also returns the counter to zero.
-// All consumer threads call it; `flag` is a shared word.
-__device__ __forceinline__ bool arrive_last(uint32_t* counter, uint32_t arrivals, volatile uint32_t* flag) {
-  __threadfence();
-  named_barrier(1, 32 * kConsumerWarps);
-  if (threadIdx.x == 0) {
-    const bool last = atomicAdd(counter, 1u) == arrivals - 1u;
-    if (last) *counter = 0u;
-    *flag = last ? 1u : 0u;
-  }
-  named_barrier(1, 32 * kConsumerWarps);
-  const bool last = *flag != 0u;
-  if (last) __threadfence();  // the reads of the other CTAs' slots come after the count
-  return last;
-}
-
-template <int D, int NT>
-__device__ void fused_merge_tail(const DecodeParams& p, const Piece& pc, volatile uint32_t* flag) {
-  const uint32_t parts = p.ctas / (p.kv_heads * p.col_groups);
-  const uint32_t G = p.merge_group;
-  const uint32_t groups = (parts + G - 1) / G;
-  const uint32_t key = pc.h * p.col_groups + pc.col0 / p.group_cols;
-  uint32_t* ctr = p.merge_counters + size_t(key) * (groups + 1);
-  const uint32_t grp = pc.slot / G;
-  const uint32_t gsize = min(G, parts - grp * G);
-  if (!arrive_last(ctr + grp, gsize, flag)) return;
-  merge_slots<D, NT>(p, pc, grp * G, gsize, 1, groups == 1);
-  if (groups == 1 || !arrive_last(ctr + groups, groups, flag)) return;
-  merge_slots<D, NT>(p, pc, 0, groups, G, true);
-}
-
 template <int D, int NT, bool BATCHED>
 constexpr int decode_max_regs() {
   return D == 256 ? 216 : (D == 128 && NT <= 1) ? 144 : 168;
@@ -1526,8 +1376,6 @@ __device__ __forceinline__ void decode_partial_body(const KernelParams<SMALL_PAG
       }
     }
     named_barrier(1, 32 * kConsumerWarps);
-    if (!BATCHED && p.merge_counters != nullptr)
-      fused_merge_tail<D, NT>(p, pc, reinterpret_cast<volatile uint32_t*>(stats));
     x += n;
   }
   if (threadIdx.x == 0) {
