@@ -562,10 +562,11 @@ void set_gather_maps(kvb::DecodeParamsGather& prm, uint32_t dim, uint64_t pages)
   if (make(&prm.tm_k, prm.k) && make(&prm.tm_v, prm.v)) prm.gather_kv = 1;
 }
 
-// Kernel parameters of the single-sequence tensor-core path; partials go to
+// Kernel parameters of a single-sequence partial kernel (the tensor-core
+// kernels, or with tensor_core = false the fp32-KV kernel); partials go to
 // `scratch` with `split_stride` slots per row-head.
 kvb::DecodeParamsGather single_params(const Shape& s, const DeviceInput& in, uint32_t parts,
-                                float* scratch, uint32_t split_stride) {
+                                float* scratch, uint32_t split_stride, bool tensor_core = true) {
   kvb::DecodeParamsGather prm{};
   prm.q = in.q;
   prm.q_positions = in.q_positions;
@@ -599,8 +600,10 @@ kvb::DecodeParamsGather single_params(const Shape& s, const DeviceInput& in, uin
   prm.total_stages = uint64_t(prm.seg_stages) * s.kv_heads;
   prm.score_scale = s.scale;
   prm.wait_limit_ns = wait_limit_ns();
-  prm.fault_stage = take_skip_stage();
-  set_gather_maps(prm, s.dim, s.pages);
+  // The stage-skip test hook and the gather maps belong to the tensor-core
+  // kernels; the fp32-KV kernel neither reads them nor consumes the hook.
+  prm.fault_stage = tensor_core ? take_skip_stage() : 0xffffffffu;
+  if (tensor_core) set_gather_maps(prm, s.dim, s.pages);
   return prm;
 }
 
@@ -703,7 +706,7 @@ uint32_t f32_partitions(const Shape& s, uint32_t requested) {
 
 void launch_f32_partials(const Shape& s, const DeviceInput& in, uint32_t parts, float* scratch,
                          uint32_t split_stride, cudaStream_t stream) {
-  kvb::DecodeParams prm = single_params(s, in, parts, scratch, split_stride);
+  kvb::DecodeParams prm = single_params(s, in, parts, scratch, split_stride, false);
   prm.group_cols = kvb::kF32Cols;
   prm.col_groups = f32_column_groups(s);
   prm.ctas = parts * s.kv_heads * prm.col_groups;
